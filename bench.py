@@ -1,0 +1,431 @@
+#!/usr/bin/env python3
+"""Benchmark: requests/s of the ensemble decode step on 1..8 B200 (one process per GPU).
+
+Default workload = BASELINE config 5 ("scale-out"): 65,536 symbols hashed over
+the GPUs (splitmix64 mod N), full 4-tower ensemble at the reduced dims D2
+(hidden 256, proj 512, depth 4, 8 heads; the default dims hold 153 MB of state
+per symbol and cannot hold 65,536 symbols), bf16 CastLinear weights, fp32 state,
+Zipf(1.1) symbol arrivals, micro-batches of up to 4096 requests formed by the
+reference's round rule, 79 N(0,1) float32 features per request. Weights are
+seeded (hackathon_b200.weights, seed 0); data is synthetic.
+
+A step = one micro-batch through the whole ensemble on each GPU. `value` is the
+requests all ranks stepped in the K timed steps divided by the max-over-ranks
+device time (CUDA events, inputs already in HBM). `e2e` is the same metric
+through the C-ABI with HOST buffers (b2e_engine_step: H2D of slots and features,
+the step, D2H of predictions, all inside the timed region).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload scaleout|d1-4096|d0-256]
+    python bench.py --impl reference ...   # the reference's CPU path (oracle port), same metric
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+WORKLOADS = {
+    # BASELINE config 5 at D2 (default)
+    "scaleout": dict(preset="D2", symbols=65536, max_batch=4096, lp="bf16", zipf=1.1),
+    # the north-star target row: 4096 symbols per step at D1
+    "d1-4096": dict(preset="D1", symbols=4096, max_batch=4096, lp="bf16", zipf=None),
+    # default dims, 256 symbols, one request each per step
+    "d0-256": dict(preset="D0", symbols=256, max_batch=256, lp="bf16", zipf=None),
+}
+CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="scaleout")
+    ap.add_argument("--symbols", type=int, default=None, help="override the symbol count")
+    ap.add_argument("--linear-dtype", default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graphs", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ helpers
+
+
+def step_bytes(cfg, lp: str, rows: int) -> int:
+    """Algorithmic HBM bytes of one step: every weight once, plus per row its state
+    read and written once, its features in and its 4 predictions out."""
+    from hackathon_b200 import weights as W
+    from hackathon_b200.engine import model_layout
+
+    srow = sum(int(np.prod(shape)) * dt.itemsize for shape, dt in model_layout(cfg))
+    return W.weight_bytes(cfg, lp) + rows * (2 * srow + cfg.num_features * 4 + 4 * 4 + 4)
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, device):
+        import torch
+
+        self.proc, self.path = None, None
+        try:
+            self.id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.id = str(device.index)
+
+    def start(self, path: Path):
+        self.path = path
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.id}", f"--query-gpu={CLOCK_QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def allreduce(x: float, op: str, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def make_batches(wl, n_symbols, world, rank, count, seed=0):
+    """(slots per micro-batch on this rank, capacity) for `count` micro-batches."""
+    from hackathon_b200 import batcher as B
+
+    mine, slot_of = B.shard_slots(n_symbols, world, rank)
+    if wl["zipf"] is None:
+        # every owned symbol once per step, max_batch per micro-batch
+        per = np.arange(len(mine), dtype=np.int32)
+        out = []
+        rng = np.random.default_rng(seed + rank)
+        while len(out) < count:
+            perm = rng.permutation(per)
+            for c in range(0, len(perm), wl["max_batch"]):
+                out.append(perm[c:c + wl["max_batch"]])
+        return out[:count], len(mine)
+    # A deep backlog keeps >= max_batch symbols pending, so every micro-batch is
+    # full: 10M arrivals (BASELINE config 5's stream), at least 4M per GPU.
+    need = max(10_000_000, 4_000_000 * world)
+    stream = B.zipf_stream(n_symbols, need, wl["zipf"], seed)
+    own = stream[B.owner(stream, world) == rank]
+    out = [slot_of[own[idx]].astype(np.int32)
+           for idx in B.continuous_batches(own, wl["max_batch"], limit=count)]
+    return out, len(mine)
+
+
+def read_traffic_per_row(name: str):
+    """dram bytes per row of the dominant kernel from the committed ncu summary."""
+    p = REPO / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_row:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+# ------------------------------------------------------------- reference arm
+
+
+def run_reference(a, wl):
+    """The reference's CPU path (the oracle port: numpy float32, all host threads)
+    on a bounded sample of the same workload; rank 0 only."""
+    world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+    if rank != 0:
+        return
+    from hackathon_b200 import config as C
+    from hackathon_b200 import weights as Wt
+    from oracle import model as O
+
+    cfg = C.PRESETS[wl["preset"]]
+    sd = Wt.generate_model(cfg, seed=0)
+    orc = O.Oracle(cfg, sd)
+    sample_rows = 64 if wl["preset"] != "D0" else 4
+    rng = np.random.default_rng(0)
+    state = O.init_state(cfg, sample_rows)
+    times = []
+    for i in range(a.warmup + a.steps):
+        feats = rng.standard_normal((sample_rows, cfg.num_features), dtype=np.float32)
+        t0 = time.perf_counter()
+        _, state = orc.step(feats, state)
+        if i >= a.warmup:
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = sample_rows * len(times) / total
+    cores = os.cpu_count()
+    cpu = {"value": value, "unit": "requests/s", "cores": cores, "kind": "port",
+           "sample": f"{len(times)} steps of {sample_rows} symbols at {wl['preset']} (fp32 oracle, numpy)"}
+    line = {"impl": "reference", "metric": "requests/s (full ensemble step)", "value": value,
+            "unit": "requests/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": 1e3 * total / len(times), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": a.workload, "dims": wl["preset"], "rows_per_step": sample_rows},
+            "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": "requests/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ main arm
+
+
+def main():
+    a = parse()
+    wl = dict(WORKLOADS[a.workload])
+    if a.linear_dtype:
+        wl["lp"] = a.linear_dtype
+    if a.symbols:
+        wl["symbols"] = a.symbols
+    if a.impl == "reference":
+        run_reference(a, wl)
+        return
+    import torch
+
+    from hackathon_b200 import config as C
+    from hackathon_b200 import weights as Wt
+    from hackathon_b200.engine import EnsembleEngine
+
+    world, rank, local = dist_setup(a.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = C.PRESETS[wl["preset"]]
+    n_sym = wl["symbols"]
+    K, Wm = a.steps, max(3, a.warmup)
+    batches, capacity = make_batches(wl, n_sym, world, rank, Wm + 2 * K + 2)
+    sd = Wt.generate_model(cfg, seed=0)
+    eng = EnsembleEngine(cfg, sd, device=local, linear_dtype=wl["lp"], capacity=capacity,
+                         max_batch=wl["max_batch"], graphs=not a.no_graphs)
+    del sd
+    rng = np.random.default_rng(1000 + rank)
+    F = cfg.num_features
+    feats = [rng.standard_normal((len(b), F), dtype=np.float32) for b in batches]
+    d_slots = [torch.from_numpy(b).to(dev) for b in batches]
+    d_feats = [torch.from_numpy(f).to(dev) for f in feats]
+    preds = torch.empty(wl["max_batch"], 4, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # ---- device-resident timing (value)
+    for i in range(Wm):
+        eng.step_device(d_slots[i], d_feats[i], preds, len(batches[i]))
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = Clocks(dev)
+    out_dir = REPO / "gpurun_out"
+    out_dir.mkdir(exist_ok=True)
+    clocks.start(out_dir / f"clocks_rank{rank}.csv")
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
+    torch.cuda.synchronize()
+    barrier(world)
+    ev[0].record(stream)
+    rows = 0
+    for k in range(K):
+        i = Wm + k
+        eng.step_device(d_slots[i], d_feats[i], preds, len(batches[i]))
+        ev[k + 1].record(stream)
+        rows += len(batches[i])
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    step_ms = [ev[k].elapsed_time(ev[k + 1]) for k in range(K)]
+    t_ms = ev[0].elapsed_time(ev[K])
+    assert eng.device_error() == 0
+    t_max = allreduce(t_ms, "max", world, dev)
+    rows_all = allreduce(float(rows), "sum", world, dev)
+    value = rows_all / (t_max / 1e3)
+
+    # ---- end to end through the C-ABI with host buffers (e2e)
+    barrier(world)
+    t0 = time.perf_counter()
+    h2d = d2h = 0
+    for k in range(K):
+        i = Wm + K + k
+        eng.step(batches[i], feats[i])
+        h2d += 16 + 4 * len(batches[i]) + 4 * F * len(batches[i])
+        d2h += 16 * len(batches[i])
+    e2e_s = time.perf_counter() - t0
+    e2e_rows = float(sum(len(batches[Wm + K + k]) for k in range(K)))
+    e2e_max = allreduce(e2e_s, "max", world, dev)
+    e2e_val = allreduce(e2e_rows, "sum", world, dev) / e2e_max
+
+    # ---- single-request latency through the C-ABI (host buffers, synchronous)
+    lat = []
+    one = np.zeros((1, F), np.float32)
+    for i in range(220):
+        t1 = time.perf_counter()
+        eng.step(batches[0][i % len(batches[0]):i % len(batches[0]) + 1], one)
+        lat.append((time.perf_counter() - t1) * 1e6)
+    lat = np.asarray(lat[20:])
+
+    # ---- roofline of the dominant state kernel, timed alone on its stream
+    roof = None
+    if rank == 0:
+        roof = dominant_kernel_roofline(cfg, wl, dev, K)
+    launches = eng.launches_per_step(wl["max_batch"])
+    nb = step_bytes(cfg, wl["lp"], int(np.mean([len(batches[Wm + k]) for k in range(K)])))
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(cfg, wl)
+
+    per_req = np.repeat(step_ms, [len(batches[Wm + k]) for k in range(K)])
+    if rank == 0:
+        line = {
+            "metric": "requests/s (full 4-tower ensemble decode step, micro-batches <= %d)" % wl["max_batch"],
+            "value": value, "unit": "requests/s", "n_gpus": world, "steps": K, "warmup": Wm,
+            "ms_per_step": t_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 state, %s weights" % wl["lp"], "data": "synthetic (seeded weights, N(0,1) features)",
+            "config": {"workload": a.workload, "dims": wl["preset"], "hidden": cfg.hidden_size,
+                       "proj": cfg.proj_size, "depth": cfg.tower_depth, "heads": cfg.num_heads,
+                       "symbols": n_sym, "symbols_per_gpu": capacity, "max_batch": wl["max_batch"],
+                       "arrivals": f"Zipf({wl['zipf']})" if wl["zipf"] else "uniform, every symbol once per round",
+                       "parallelism": f"symbol-sharded x{world} (splitmix64 mod N), no collective",
+                       "l2": "inputs larger than L2: %.1f GB of state streamed per step" % (nb / 1e9)},
+            "latency_us": {"batch_p50": float(np.percentile(per_req, 50) * 1e3),
+                           "batch_p99": float(np.percentile(per_req, 99) * 1e3),
+                           "single_request_p50": float(np.percentile(lat, 50)),
+                           "single_request_p99": float(np.percentile(lat, 99))},
+            "hbm_gbs_step": nb / (t_max / K / 1e3) / 1e9,
+            "e2e": {"value": e2e_val, "unit": "requests/s", "h2d_bytes_per_step": h2d // K,
+                    "d2h_bytes_per_step": d2h // K},
+            "gpu_launches": (launches + 1) * K,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def dominant_kernel_roofline(cfg, wl, dev, K):
+    """Mamba2's state step (ssm_cols) - the largest state stream of the step - timed
+    alone with CUDA events on its stream at one engine launch's shape."""
+    import torch
+
+    from hackathon_b200 import kernels as KR
+
+    peaks = {}
+    pk = REPO / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    rows = wl["max_batch"]
+    nh, hs, bc = cfg.mamba_heads, cfg.mamba_head_size, cfg.mamba_bc_size
+    g = torch.Generator(device=dev).manual_seed(0)
+    ssm = torch.randn(rows, nh, hs, bc, device=dev, generator=g)
+    x = torch.randn(rows, nh, hs, device=dev, generator=g)
+    b = torch.randn(rows, bc, device=dev, generator=g)
+    c = torch.randn(rows, bc, device=dev, generator=g)
+    dt = torch.rand(rows, nh, device=dev, generator=g)
+    dc = torch.rand(rows, nh, device=dev, generator=g)
+    s = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        KR.mamba2_step(ssm, x, b, c, dt, dc, None)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(10, K)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(n):
+        KR.mamba2_step(ssm, x, b, c, dt, dc, None)
+    e1.record(s)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / n / 1e3
+    per_row = 2 * nh * hs * bc * 4 + (nh * hs * 2 + 2 * bc + 2 * nh) * 4
+    achieved = rows * per_row / t / 1e9
+    tr = read_traffic_per_row("ssm_cols")
+    return {"kernel": "ssm_cols (Mamba2 state step)", "bound": "hbm", "achieved": achieved, "peak": peak,
+            "unit": "GB/s", "frac": achieved / peak, "traffic": None if tr is None else tr * rows,
+            "bytes_per_launch": rows * per_row, "launch_us": t * 1e6,
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs" if pk.exists() else "fallback 6650 GB/s"}
+
+
+def cpu_baseline(cfg, wl):
+    """The reference's CPU arithmetic (the numpy oracle port, fp32) on a bounded
+    sample of this workload: 64-symbol micro-batches for ~10 s."""
+    from hackathon_b200 import weights as Wt
+    from oracle import model as O
+
+    sd = Wt.generate_model(cfg, seed=0)
+    orc = O.Oracle(cfg, sd)
+    rows = 64 if cfg.hidden_size <= 512 else 2
+    state = O.init_state(cfg, rows)
+    rng = np.random.default_rng(0)
+    orc.step(rng.standard_normal((rows, cfg.num_features), dtype=np.float32), state)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 10.0:
+        _, state = orc.step(rng.standard_normal((rows, cfg.num_features), dtype=np.float32), state)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": rows * n / dt, "unit": "requests/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} micro-batches of {rows} symbols, fp32 numpy oracle, {dt:.1f} s"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,332 @@
+// Ensemble engine (see engine.cuh).
+//
+// One step = MultiTowerModel.forward over the live rows (model/inference_model.py:
+// 119-143): the four towers run concurrently on four streams forked from the step
+// stream, each a chain of its Blocks (model/inference_model.py:63-68, 85-95),
+// then output_proj per tower into its prediction column. A row's state is read
+// and written in place at its slot, so there is no blend pass: an idle symbol's
+// slot is never touched (the reference folds idle rows back bit for bit,
+// example_model.py:907-949). The step is captured once per batch bucket into a
+// CUDA graph and replayed; the live row count is read from device memory, so one
+// graph serves every batch size up to its bucket.
+#include <algorithm>
+#include <cstring>
+
+#include "engine.cuh"
+#include "gemm.cuh"
+
+namespace b2e {
+
+namespace {
+
+__global__ void k_validate(const int* slots, int n, int capacity, int* n_dev, int* err) {
+  __shared__ int bad;
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    if (slots[i] < 0 || slots[i] >= capacity) bad = 1;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *n_dev = bad ? 0 : n;
+    if (bad) *err = 1;
+  }
+}
+
+}  // namespace
+
+Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d), opt_(o) {
+  d_.validate();
+  B2E_CHECK(o.capacity > 0, kErrInvalid, "capacity must be positive");
+  B2E_CHECK(o.max_batch > 0 && o.max_batch <= 65535, kErrInvalid, "max_batch must be in 1..65535");
+  B2E_CHECK(o.lp == kF32 || o.lp == kBF16 || o.lp == kF16, kErrInvalid, "unknown linear dtype");
+  B2E_CUDA(cudaSetDevice(o.device));
+  const int H = d.H, P = d.P, F = d.F, lp = o.lp;
+
+  // ---- weights (strict key names of MultiTowerModel.state_dict())
+  towers_.resize(4);
+  for (int t = 0; t < 4; ++t) {
+    Tower& tw = towers_[t];
+    tw.kind = t;  // tower order xLSTM, Mamba2, RetNet, Hawk (model/inference_model.py:107-112)
+    const std::string tp = "towers." + std::to_string(t) + ".";
+    tw.o_upw = pack_.add(src.get(tp + "input_up.weight", long(P) * F), size_t(P) * F, lp);
+    tw.o_upb = pack_.add(src.get(tp + "input_up.bias", P), P, lp);
+    tw.o_dnw = pack_.add(src.get(tp + "input_down.weight", long(H) * P), size_t(H) * P, lp);
+    tw.o_dnb = pack_.add(src.get(tp + "input_down.bias", H), H, lp);
+    tw.blocks.resize(d.depth);
+    for (int b = 0; b < d.depth; ++b) {
+      Block& bl = tw.blocks[b];
+      const std::string bp = tp + "blocks." + std::to_string(b) + ".";
+      bl.layer = Layer::make(t, d_, lp);
+      bl.o_n1 = pack_.add(src.get(bp + "norm1.weight", H), H, kF32);
+      bl.layer->load(src, pack_, bp + "layer.");
+      bl.o_n2 = pack_.add(src.get(bp + "norm2.weight", H), H, kF32);
+      bl.o_f1w = pack_.add(src.get(bp + "mlp.fc1.weight", long(P) * H), size_t(P) * H, lp);
+      bl.o_f1b = pack_.add(src.get(bp + "mlp.fc1.bias", P), P, lp);
+      bl.o_f2w = pack_.add(src.get(bp + "mlp.fc2.weight", long(H) * P), size_t(H) * P, lp);
+      bl.o_f2b = pack_.add(src.get(bp + "mlp.fc2.bias", H), H, lp);
+    }
+  }
+  o_ow_ = pack_.add(src.get("output_proj.weight", H), H, kF32);  // fp32 kept (example_model.py:106)
+  o_ob_ = pack_.add(src.get("output_proj.bias", 1), 1, kF32);
+  src.check_all_used();
+  pack_.upload();
+
+  // ---- state table, leaves in iter_state_tensors order (example_model.py:160-176)
+  for (auto& tw : towers_)
+    for (auto& bl : tw.blocks) bl.layer->declare_state(arena_);
+  arena_.allocate(o.capacity);
+
+  for (auto& tw : towers_) {
+    tw.upw = pack_.ptr(tw.o_upw); tw.upb = pack_.ptr(tw.o_upb);
+    tw.dnw = pack_.ptr(tw.o_dnw); tw.dnb = pack_.ptr(tw.o_dnb);
+    for (auto& bl : tw.blocks) {
+      bl.n1 = pack_.ptr<float>(bl.o_n1); bl.n2 = pack_.ptr<float>(bl.o_n2);
+      bl.f1w = pack_.ptr(bl.o_f1w); bl.f1b = pack_.ptr(bl.o_f1b);
+      bl.f2w = pack_.ptr(bl.o_f2w); bl.f2b = pack_.ptr(bl.o_f2b);
+      bl.layer->resolve(pack_, arena_);
+    }
+    const size_t R = o.max_batch;
+    size_t scratch = 0;
+    for (auto& bl : tw.blocks) scratch = std::max(scratch, bl.layer->scratch_bytes(o.max_batch));
+    Carver c{nullptr};
+    c.take<float>(R * H);
+    c.take<float>(R * H);
+    c.take<float>(R * P);
+    const size_t glue = (c.off + 255) & ~size_t(255);
+    uint8_t* base = nullptr;
+    B2E_CUDA(cudaMalloc(&base, glue + scratch + 256));
+    Carver g{base};
+    tw.x = g.take<float>(R * H);
+    tw.t = g.take<float>(R * H);
+    tw.u = g.take<float>(R * P);
+    tw.scratch = base + glue;
+    B2E_CUDA(cudaStreamCreateWithFlags(&tw.s, cudaStreamNonBlocking));
+    B2E_CUDA(cudaEventCreateWithFlags(&tw.done, cudaEventDisableTiming));
+  }
+  ow_ = pack_.ptr<float>(o_ow_);
+  ob_ = pack_.ptr<float>(o_ob_);
+
+  // ---- step I/O
+  const size_t R = o.max_batch;
+  feats_off_ = (16 + 4 * R + 255) & ~size_t(255);
+  preds_off_ = (feats_off_ + 4 * R * F + 255) & ~size_t(255);
+  const size_t io = preds_off_ + 16 * R + 64;
+  B2E_CUDA(cudaMalloc(&d_io_, io));
+  B2E_CUDA(cudaMallocHost(&h_io_, io));
+  d_n_ = reinterpret_cast<int*>(d_io_);
+  d_slots_ = reinterpret_cast<int*>(d_io_ + 16);
+  d_feats_ = reinterpret_cast<float*>(d_io_ + feats_off_);
+  d_preds_ = reinterpret_cast<float*>(d_io_ + preds_off_);
+  d_err_ = reinterpret_cast<int*>(d_io_ + preds_off_ + 16 * R);
+  B2E_CUDA(cudaMemset(d_io_, 0, io));
+  B2E_CUDA(cudaStreamCreateWithFlags(&s0_, cudaStreamNonBlocking));
+  B2E_CUDA(cudaEventCreateWithFlags(&fork_, cudaEventDisableTiming));
+  seen_.assign(o.capacity, 0);
+
+  arena_.reset_all(s0_);
+  B2E_CUDA(cudaStreamSynchronize(s0_));
+}
+
+Engine::~Engine() {
+  cudaSetDevice(opt_.device);
+  if (s0_) cudaStreamSynchronize(s0_);
+  for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+  for (auto& tw : towers_) {
+    if (tw.s) cudaStreamDestroy(tw.s);
+    if (tw.done) cudaEventDestroy(tw.done);
+    if (tw.x) cudaFree(tw.x);
+  }
+  if (fork_) cudaEventDestroy(fork_);
+  if (s0_) cudaStreamDestroy(s0_);
+  if (d_io_) cudaFree(d_io_);
+  if (h_io_) cudaFreeHost(h_io_);
+}
+
+int Engine::bucket(int n) const {
+  int b = 1;
+  while (b < n) b <<= 1;
+  return std::min(b, opt_.max_batch);
+}
+
+void Engine::tower_forward(Tower& tw, int idx, const StepCtx& c) {
+  const int H = d_.H, P = d_.P, F = d_.F, lp = opt_.lp;
+  // input_up, ReLU, input_down (model/inference_model.py:88-90)
+  linear(c, d_feats_, F, tw.upw, lp, tw.upb, P, F, tw.u, P, kActRelu);
+  linear(c, tw.u, P, tw.dnw, lp, tw.dnb, H, P, tw.x, H);
+  for (auto& bl : tw.blocks) {
+    // Block.forward: x = layer(norm1(x)) + x; x = x + mlp(norm2(x)) (model/inference_model.py:63-68)
+    rmsnorm_rows(c, tw.x, bl.n1, 1.1920928955078125e-07f, H, tw.t);
+    bl.layer->forward(c, tw.t, tw.x, tw.x, tw.scratch);
+    rmsnorm_rows(c, tw.x, bl.n2, 1.1920928955078125e-07f, H, tw.t);
+    linear(c, tw.t, H, bl.f1w, lp, bl.f1b, P, H, tw.u, P, kActRelu);               // fc1 + ReLU
+    linear(c, tw.u, P, bl.f2w, lp, bl.f2b, H, P, tw.x, H, kActNone, tw.x, H);      // fc2 + residual
+  }
+  output_proj_rows(c, tw.x, ow_, ob_, H, d_preds_, 4, idx);  // shared output_proj (model/inference_model.py:142)
+}
+
+void Engine::enqueue(int rows, cudaStream_t s) {
+  B2E_CUDA(cudaEventRecord(fork_, s));
+  for (int t = 0; t < 4; ++t) {
+    Tower& tw = towers_[t];
+    B2E_CUDA(cudaStreamWaitEvent(tw.s, fork_, 0));
+    StepCtx c;
+    c.s = tw.s;
+    c.rows = rows;
+    c.n_dev = d_n_;
+    c.slots = d_slots_;
+    c.lp = opt_.lp;
+    tower_forward(tw, t, c);
+    B2E_CUDA(cudaEventRecord(tw.done, tw.s));
+  }
+  for (auto& tw : towers_) B2E_CUDA(cudaStreamWaitEvent(s, tw.done, 0));
+}
+
+void Engine::launch(int n, cudaStream_t s) {
+  const int rows = bucket(n);
+  if (!opt_.graphs) {
+    enqueue(rows, s);
+    return;
+  }
+  auto it = graphs_.find(rows);
+  if (it == graphs_.end()) {
+    // Capture on a private stream so the caller's stream is never in capture mode.
+    cudaGraph_t g = nullptr;
+    B2E_CUDA(cudaStreamBeginCapture(s0_, cudaStreamCaptureModeThreadLocal));
+    try {
+      enqueue(rows, s0_);
+    } catch (...) {
+      cudaStreamEndCapture(s0_, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    B2E_CUDA(cudaStreamEndCapture(s0_, &g));
+    cudaGraphExec_t ex = nullptr;
+    B2E_CUDA(cudaGraphInstantiate(&ex, g, 0));
+    B2E_CUDA(cudaGraphDestroy(g));
+    it = graphs_.emplace(rows, ex).first;
+  }
+  B2E_CUDA(cudaGraphLaunch(it->second, s));
+}
+
+int Engine::launches_per_step(int n) {
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  cudaGraph_t g = nullptr;
+  B2E_CUDA(cudaStreamBeginCapture(s0_, cudaStreamCaptureModeThreadLocal));
+  try {
+    enqueue(bucket(n), s0_);
+  } catch (...) {
+    cudaStreamEndCapture(s0_, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  B2E_CUDA(cudaStreamEndCapture(s0_, &g));
+  size_t count = 0;
+  B2E_CUDA(cudaGraphGetNodes(g, nullptr, &count));
+  std::vector<cudaGraphNode_t> nodes(count);
+  B2E_CUDA(cudaGraphGetNodes(g, nodes.data(), &count));
+  int kernels = 0;
+  for (auto& nd : nodes) {
+    cudaGraphNodeType ty;
+    B2E_CUDA(cudaGraphNodeGetType(nd, &ty));
+    if (ty == cudaGraphNodeTypeKernel) ++kernels;
+  }
+  B2E_CUDA(cudaGraphDestroy(g));
+  return kernels;
+}
+
+void Engine::check_host_slots(const int* slots, int n) {
+  B2E_CHECK(n >= 1 && n <= opt_.max_batch, kErrCapacity,
+            "batch of " + std::to_string(n) + " rows is outside 1.." + std::to_string(opt_.max_batch));
+  B2E_CHECK(slots != nullptr, kErrInvalid, "null slot array");
+  int i = 0;
+  for (; i < n; ++i) {
+    const int s = slots[i];
+    if (s < 0 || s >= opt_.capacity || seen_[s]) break;
+    seen_[s] = 1;
+  }
+  for (int j = 0; j < i; ++j) seen_[slots[j]] = 0;
+  if (i < n) {
+    const int s = slots[i];
+    B2E_CHECK(!(s < 0 || s >= opt_.capacity), kErrCapacity, "slot " + std::to_string(s) + " outside the state table");
+    throw Error(kErrInvalid, "slot " + std::to_string(s) + " appears twice in one step");
+  }
+}
+
+void Engine::submit(const int* slots, const float* feats, int n) {
+  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a step is already in flight on this engine");
+  check_host_slots(slots, n);
+  B2E_CHECK(feats != nullptr, kErrInvalid, "null feature array");
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  const int F = d_.F;
+  std::memcpy(h_io_, &n, 4);
+  std::memcpy(h_io_ + 16, slots, size_t(n) * 4);
+  std::memcpy(h_io_ + feats_off_, feats, size_t(n) * F * 4);
+  B2E_CUDA(cudaMemcpyAsync(d_io_, h_io_, 16 + size_t(n) * 4, cudaMemcpyHostToDevice, s0_));
+  B2E_CUDA(cudaMemcpyAsync(d_feats_, h_io_ + feats_off_, size_t(n) * F * 4, cudaMemcpyHostToDevice, s0_));
+  launch(n, s0_);
+  B2E_CUDA(cudaMemcpyAsync(h_io_ + preds_off_, d_preds_, size_t(n) * 16, cudaMemcpyDeviceToHost, s0_));
+  pending_n_ = n;
+}
+
+void Engine::wait(float* preds) {
+  B2E_CHECK(pending_n_ >= 0, kErrInvalid, "no step in flight");
+  const int n = pending_n_;
+  pending_n_ = -1;
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  B2E_CUDA(cudaStreamSynchronize(s0_));
+  if (preds) std::memcpy(preds, h_io_ + preds_off_, size_t(n) * 16);
+}
+
+void Engine::step_device(const int* d_slots, const float* d_feats, int n, float* d_preds, cudaStream_t s) {
+  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a host step is in flight on this engine");
+  B2E_CHECK(n >= 1 && n <= opt_.max_batch, kErrCapacity, "batch outside 1..max_batch");
+  B2E_CHECK(d_slots && d_feats && d_preds, kErrInvalid, "null device buffer");
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  if (d_slots != d_slots_) B2E_CUDA(cudaMemcpyAsync(d_slots_, d_slots, size_t(n) * 4, cudaMemcpyDeviceToDevice, s));
+  if (d_feats != d_feats_)
+    B2E_CUDA(cudaMemcpyAsync(d_feats_, d_feats, size_t(n) * d_.F * 4, cudaMemcpyDeviceToDevice, s));
+  k_validate<<<1, 256, 0, s>>>(d_slots_, n, opt_.capacity, d_n_, d_err_);
+  B2E_CUDA(cudaGetLastError());
+  launch(n, s);
+  if (d_preds != d_preds_) B2E_CUDA(cudaMemcpyAsync(d_preds, d_preds_, size_t(n) * 16, cudaMemcpyDeviceToDevice, s));
+}
+
+int Engine::device_error() {
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  B2E_CUDA(cudaDeviceSynchronize());
+  int e = 0;
+  B2E_CUDA(cudaMemcpy(&e, d_err_, 4, cudaMemcpyDeviceToHost));
+  B2E_CUDA(cudaMemset(d_err_, 0, 4));
+  return e;
+}
+
+void Engine::reset_slots(const int* slots, int n) {
+  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a step is in flight on this engine");
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  B2E_CUDA(cudaStreamSynchronize(s0_));
+  for (int i0 = 0; i0 < n; i0 += opt_.max_batch) {
+    const int m = std::min(opt_.max_batch, n - i0);
+    for (int i = 0; i < m; ++i)
+      B2E_CHECK(slots[i0 + i] >= 0 && slots[i0 + i] < opt_.capacity, kErrCapacity, "slot outside the state table");
+    std::memcpy(h_io_ + 16, slots + i0, size_t(m) * 4);
+    B2E_CUDA(cudaMemcpyAsync(d_slots_, h_io_ + 16, size_t(m) * 4, cudaMemcpyHostToDevice, s0_));
+    arena_.reset_slots(d_slots_, m, s0_);
+    B2E_CUDA(cudaStreamSynchronize(s0_));
+  }
+}
+
+void Engine::read_slot(int slot, void* host) {
+  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a step is in flight on this engine");
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  B2E_CUDA(cudaDeviceSynchronize());
+  arena_.read_slot(slot, host);
+}
+
+void Engine::write_slot(int slot, const void* host) {
+  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a step is in flight on this engine");
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  B2E_CUDA(cudaDeviceSynchronize());
+  arena_.write_slot(slot, host);
+}
+
+}  // namespace b2e

@@ -1,0 +1,301 @@
+// SIMT projection GEMMs for sm_100a (see gemm.cuh for the semantics).
+//
+// Two kernels:
+//  * gemm_tiled: 64x64 output tile per CTA, 16-deep K slices through shared
+//    memory with a register prefetch of the next slice, 4x4 outputs per thread.
+//    Exact f32 FMA arithmetic, which is what the fp32 path must match.
+//  * gemm_skinny: M <= 16 rows. Weight-bound: each warp streams whole W rows with
+//    128-bit loads and keeps one accumulator per live row; this is the path a
+//    single request takes, where the step is a chain of GEMVs over the weights.
+#include "gemm.cuh"
+
+#include <algorithm>
+
+namespace b2e {
+namespace {
+
+constexpr int BM = 64, BN = 64, BK = 16, TPB = 256;
+
+template <int T>
+__device__ __forceinline__ float4 load4_vec(const void* base, size_t idx) {
+  if constexpr (T == kF32) {
+    return __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx));
+  } else {
+    using L = typename LowP<T>::type;
+    uint2 raw = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const L*>(base) + idx));
+    L v[4];
+    *reinterpret_cast<uint2*>(v) = raw;
+    float4 r;
+    if constexpr (T == kBF16) {
+      r.x = __bfloat162float(v[0]); r.y = __bfloat162float(v[1]);
+      r.z = __bfloat162float(v[2]); r.w = __bfloat162float(v[3]);
+    } else {
+      r.x = __half2float(v[0]); r.y = __half2float(v[1]);
+      r.z = __half2float(v[2]); r.w = __half2float(v[3]);
+    }
+    return r;
+  }
+}
+
+template <int T>
+__device__ __forceinline__ float load1(const void* base, size_t idx) {
+  return LowP<T>::load(base, idx);
+}
+
+// Load 4 consecutive K elements of one row, zero outside [0, rows) x [0, K).
+template <int T>
+__device__ __forceinline__ float4 load_row4(const void* base, int ld, int row, int rows, int k, int K, bool vec) {
+  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (row >= rows) return r;
+  const size_t off = size_t(row) * ld + k;
+  if (vec && k + 3 < K) return load4_vec<T>(base, off);
+  if (k + 0 < K) r.x = load1<T>(base, off + 0);
+  if (k + 1 < K) r.y = load1<T>(base, off + 1);
+  if (k + 2 < K) r.z = load1<T>(base, off + 2);
+  if (k + 3 < K) r.w = load1<T>(base, off + 3);
+  return r;
+}
+
+template <int WT>
+__device__ __forceinline__ float4 round4(float4 v) {
+  v.x = LowP<WT>::round(v.x); v.y = LowP<WT>::round(v.y);
+  v.z = LowP<WT>::round(v.z); v.w = LowP<WT>::round(v.w);
+  return v;
+}
+
+template <int WT>
+__device__ __forceinline__ float epilogue(const GemmParams& p, const GemmGroup& g, float acc, int m, int n) {
+  float v = acc;
+  if (g.bias) v += load_as(p.bias_type, g.bias, n);
+  if (p.round_out) v = LowP<WT>::round(v);
+  if (p.act == kActRelu) v = fmaxf(v, 0.0f);
+  if (g.R) v += g.R[size_t(m) * p.ldr + n];
+  return v;
+}
+
+template <int AT, int WT>
+__global__ void __launch_bounds__(TPB) gemm_tiled(const __grid_constant__ GemmParams p, bool vec_a, bool vec_w) {
+  const GemmGroup& g = p.g[blockIdx.z];
+  const int M = live_rows(p.M_dev, p.M_max);
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  if (m0 >= M) return;
+
+  __shared__ float As[2][BK][BM + 4];
+  __shared__ float Ws[2][BK][BN + 4];
+
+  const int tid = threadIdx.x;
+  const int lr = tid >> 2, lk = (tid & 3) * 4;  // loader: row, k offset
+  const int tx = tid & 15, ty = tid >> 4;       // compute: cols 4tx.., rows ty+16i
+  const bool round_a = (AT == kF32 && WT != kF32);
+
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+  auto fetch = [&](int k0, float4& a, float4& w) {
+    a = load_row4<AT>(g.A, p.lda, m0 + lr, M, k0 + lk, p.K, vec_a);
+    if (round_a) a = round4<WT>(a);
+    w = load_row4<WT>(g.W, p.ldw, n0 + lr, p.N, k0 + lk, p.K, vec_w);
+  };
+  auto stash = [&](int buf, const float4& a, const float4& w) {
+    As[buf][lk + 0][lr] = a.x; As[buf][lk + 1][lr] = a.y;
+    As[buf][lk + 2][lr] = a.z; As[buf][lk + 3][lr] = a.w;
+    Ws[buf][lk + 0][lr] = w.x; Ws[buf][lk + 1][lr] = w.y;
+    Ws[buf][lk + 2][lr] = w.z; Ws[buf][lk + 3][lr] = w.w;
+  };
+
+  float4 ra, rw;
+  fetch(0, ra, rw);
+  stash(0, ra, rw);
+  __syncthreads();
+  int buf = 0;
+  for (int k0 = 0; k0 < p.K; k0 += BK) {
+    const bool more = k0 + BK < p.K;
+    if (more) fetch(k0 + BK, ra, rw);
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[buf][kk][ty + 16 * i];
+      const float4 w = *reinterpret_cast<const float4*>(&Ws[buf][kk][tx * 4]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[i][0] = fmaf(a[i], w.x, acc[i][0]);
+        acc[i][1] = fmaf(a[i], w.y, acc[i][1]);
+        acc[i][2] = fmaf(a[i], w.z, acc[i][2]);
+        acc[i][3] = fmaf(a[i], w.w, acc[i][3]);
+      }
+    }
+    if (more) {
+      stash(buf ^ 1, ra, rw);
+      __syncthreads();
+      buf ^= 1;
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty + 16 * i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n >= p.N) continue;
+      const float v = epilogue<WT>(p, g, acc[i][j], m, n);
+      if (g.C) g.C[size_t(m) * p.ldc + n] = v;
+      if (g.C_lp) store_as(WT == kF32 ? kF32 : WT, g.C_lp, size_t(m) * p.ldc_lp + n, v);
+    }
+  }
+}
+
+// One warp per output column; MM = accumulators per lane (>= live rows).
+template <int AT, int WT, int MM>
+__global__ void __launch_bounds__(256) gemm_skinny(const __grid_constant__ GemmParams p, bool vec) {
+  const GemmGroup& g = p.g[blockIdx.y];
+  const int M = min(live_rows(p.M_dev, p.M_max), MM);
+  if (M <= 0) return;
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int gw = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int stride = gridDim.x * warps;
+  const bool round_a = (AT == kF32 && WT != kF32);
+
+  for (int n = gw; n < p.N; n += stride) {
+    float acc[MM];
+#pragma unroll
+    for (int r = 0; r < MM; ++r) acc[r] = 0.f;
+    const size_t wrow = size_t(n) * p.ldw;
+    if (vec) {
+      // 4 elements per lane per step; 4 steps in flight.
+      int k = lane * 4;
+      for (; k + 3 * 128 + 3 < p.K; k += 4 * 128) {
+        float4 w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) w[u] = load4_vec<WT>(g.W, wrow + k + u * 128);
+#pragma unroll
+        for (int r = 0; r < MM; ++r) {
+          if (r < M) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              float4 a = load4_vec<AT>(g.A, size_t(r) * p.lda + k + u * 128);
+              if (round_a) a = round4<WT>(a);
+              acc[r] = fmaf(a.x, w[u].x, acc[r]);
+              acc[r] = fmaf(a.y, w[u].y, acc[r]);
+              acc[r] = fmaf(a.z, w[u].z, acc[r]);
+              acc[r] = fmaf(a.w, w[u].w, acc[r]);
+            }
+          }
+        }
+      }
+      for (; k + 3 < p.K; k += 128) {
+        const float4 w = load4_vec<WT>(g.W, wrow + k);
+#pragma unroll
+        for (int r = 0; r < MM; ++r) {
+          if (r < M) {
+            float4 a = load4_vec<AT>(g.A, size_t(r) * p.lda + k);
+            if (round_a) a = round4<WT>(a);
+            acc[r] = fmaf(a.x, w.x, acc[r]);
+            acc[r] = fmaf(a.y, w.y, acc[r]);
+            acc[r] = fmaf(a.z, w.z, acc[r]);
+            acc[r] = fmaf(a.w, w.w, acc[r]);
+          }
+        }
+      }
+    } else {
+      for (int k = lane; k < p.K; k += 32) {
+        const float w = load1<WT>(g.W, wrow + k);
+#pragma unroll
+        for (int r = 0; r < MM; ++r) {
+          if (r < M) {
+            float a = load1<AT>(g.A, size_t(r) * p.lda + k);
+            if (round_a) a = LowP<WT>::round(a);
+            acc[r] = fmaf(a, w, acc[r]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < MM; ++r) acc[r] = warp_sum(acc[r]);
+    if (lane < M) {
+      float mine = 0.f;
+#pragma unroll
+      for (int r = 0; r < MM; ++r)
+        if (r == lane) mine = acc[r];
+      const float v = epilogue<WT>(p, g, mine, lane, n);
+      if (g.C) g.C[size_t(lane) * p.ldc + n] = v;
+      if (g.C_lp) store_as(WT, g.C_lp, size_t(lane) * p.ldc_lp + n, v);
+    }
+  }
+}
+
+bool aligned(const void* ptr, int bytes) { return (reinterpret_cast<uintptr_t>(ptr) % bytes) == 0; }
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int AT, int WT>
+void launch(const GemmParams& p, cudaStream_t s) {
+  const int abytes = int(dtype_size(AT)), wbytes = int(dtype_size(WT));
+  bool vec_a = (p.K % 4 == 0) && (p.lda % 4 == 0);
+  bool vec_w = (p.K % 4 == 0) && (p.ldw % 4 == 0);
+  for (int i = 0; i < p.groups; ++i) {
+    vec_a = vec_a && aligned(p.g[i].A, 4 * abytes);
+    vec_w = vec_w && aligned(p.g[i].W, 4 * wbytes);
+  }
+  if (p.M_max <= 16) {
+    const int warps = 8;
+    int blocks = ceil_div(p.N, warps);
+    blocks = std::min(blocks, 8 * sm_count());
+    dim3 grid(blocks, p.groups);
+    const bool vec = vec_a && vec_w;
+    if (p.M_max <= 1)
+      gemm_skinny<AT, WT, 1><<<grid, 32 * warps, 0, s>>>(p, vec);
+    else if (p.M_max <= 2)
+      gemm_skinny<AT, WT, 2><<<grid, 32 * warps, 0, s>>>(p, vec);
+    else if (p.M_max <= 4)
+      gemm_skinny<AT, WT, 4><<<grid, 32 * warps, 0, s>>>(p, vec);
+    else if (p.M_max <= 8)
+      gemm_skinny<AT, WT, 8><<<grid, 32 * warps, 0, s>>>(p, vec);
+    else
+      gemm_skinny<AT, WT, 16><<<grid, 32 * warps, 0, s>>>(p, vec);
+  } else {
+    dim3 grid(ceil_div(p.N, BN), ceil_div(p.M_max, BM), p.groups);
+    gemm_tiled<AT, WT><<<grid, TPB, 0, s>>>(p, vec_a, vec_w);
+  }
+}
+
+}  // namespace
+
+void gemm(const GemmParams& p, cudaStream_t s) {
+  B2E_CHECK(p.groups >= 1 && p.groups <= kMaxGroups, kErrInternal, "gemm: bad group count");
+  B2E_CHECK(p.M_max > 0 && p.N > 0 && p.K > 0, kErrInternal, "gemm: empty problem");
+  B2E_CHECK(p.M_max <= 65535 * BM, kErrInternal, "gemm: too many rows");
+  const int a = p.a_type, w = p.w_type;
+  if (w == kF32) {
+    B2E_CHECK(a == kF32, kErrInternal, "gemm: f32 weights need f32 activations");
+    launch<kF32, kF32>(p, s);
+  } else if (w == kBF16) {
+    if (a == kF32) launch<kF32, kBF16>(p, s);
+    else if (a == kBF16) launch<kBF16, kBF16>(p, s);
+    else throw Error(kErrInternal, "gemm: activation/weight type mismatch");
+  } else if (w == kF16) {
+    if (a == kF32) launch<kF32, kF16>(p, s);
+    else if (a == kF16) launch<kF16, kF16>(p, s);
+    else throw Error(kErrInternal, "gemm: activation/weight type mismatch");
+  } else {
+    throw Error(kErrInternal, "gemm: unknown weight type");
+  }
+  B2E_CUDA(cudaGetLastError());
+}
+
+}  // namespace b2e

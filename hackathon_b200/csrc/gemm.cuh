@@ -1,0 +1,47 @@
+// Projection GEMMs: C[m, n] = epilogue( sum_k A[m, k] * W[n, k] ).
+//
+// W is an nn.Linear weight ([out, in], row-major) stored in f32 or in the
+// CastLinear low type (example_model.py:68-101). Semantics follow CastLinear
+// exactly: with a low-precision weight the input is rounded to the low type,
+// products accumulate in f32, the bias (stored in the low type) is added, and the
+// result is rounded to the low type before it is widened back to f32
+// (example_model.py:92-95). Then, in this order: activation, residual add.
+//
+// Up to kMaxGroups independent problems of the same (M, N, K) run in one launch
+// (BlockLinear's diagonal blocks, model/modules.py:52-79).
+#pragma once
+#include "common.cuh"
+
+namespace b2e {
+
+constexpr int kMaxGroups = 16;
+
+enum Act : int { kActNone = 0, kActRelu = 1 };
+
+struct GemmGroup {
+  const void* A = nullptr;     // [M, K], leading dim lda, type a_type
+  const void* W = nullptr;     // [N, K], leading dim ldw, type w_type
+  const void* bias = nullptr;  // [N], type bias_type, or null
+  float* C = nullptr;          // [M, N] f32 output, leading dim ldc, or null
+  void* C_lp = nullptr;        // [M, N] low-type copy of the output, or null
+  const float* R = nullptr;    // [M, N] residual added last, or null (may alias C)
+};
+
+struct GemmParams {
+  GemmGroup g[kMaxGroups];
+  int groups = 1;
+  int M_max = 0;               // rows the launch is sized for
+  const int* M_dev = nullptr;  // live rows (device), or null to use M_max
+  int N = 0, K = 0;
+  int lda = 0, ldw = 0, ldc = 0, ldc_lp = 0, ldr = 0;
+  int a_type = kF32, w_type = kF32, bias_type = kF32;
+  int lp = kF32;      // CastLinear low type; kF32 = plain fp32 nn.Linear
+  int round_out = 0;  // round the (acc + bias) to `lp` (CastLinear output)
+  int act = kActNone;
+};
+
+// Enqueue on `stream`. Picks the weight-streaming kernel for M_max <= 16 and the
+// tiled kernel otherwise.
+void gemm(const GemmParams& p, cudaStream_t stream);
+
+}  // namespace b2e

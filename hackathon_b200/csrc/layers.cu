@@ -1,0 +1,963 @@
+// The four recurrent layers (xLSTM, Mamba2, RetNet, Hawk) on sm_100a.
+//
+// Each layer step is a short chain: projection GEMM(s) -> one per-row fused
+// kernel (convs, gates, norms, rotary) -> the state-streaming cell kernel over
+// the big state (cells.cu) -> one per-row fused kernel -> output GEMM with the
+// Block residual in its epilogue. Every per-row kernel is one CTA per live row,
+// reads and writes the row's small state leaves in place at its slot, and keeps
+// the row's intermediate vectors in shared memory. The arithmetic of every step
+// is the reference's, in its order, in float32; the citations give the lines.
+#include <algorithm>
+#include <cmath>
+
+#include "cells.cuh"
+#include "gemm.cuh"
+#include "layers.cuh"
+
+namespace b2e {
+
+
+void Dims::validate() const {
+  B2E_CHECK(H > 0 && P > 0 && depth > 0 && F > 0, kErrInvalid, "model dims must be positive");
+  B2E_CHECK(heads >= 2 && heads % 2 == 0, kErrInvalid, "num_heads must be even (sLSTM uses num_heads // 2)");
+  B2E_CHECK(heads <= 64, kErrInvalid, "num_heads above 64 is not supported (per-row group statistics)");
+  B2E_CHECK(H % heads == 0 && H % (heads / 2) == 0 && H % 4 == 0, kErrInvalid, "hidden_size must divide by heads and 4");
+  B2E_CHECK((2 * H) % m_hs == 0, kErrInvalid, "mamba inner size must divide by its head size");
+  B2E_CHECK(retnet_hs() % 2 == 0, kErrInvalid, "RetNet head size must be even (rotary pairs)");
+  B2E_CHECK(retnet_hs() % 4 == 0 && mlstm_hs() % 4 == 0 && m_bc % 4 == 0, kErrInvalid,
+            "head sizes and the Mamba2 B/C width must be multiples of 4");
+  B2E_CHECK(retnet_hs() <= 512 && mlstm_hs() <= 512, kErrInvalid, "head sizes above 512 are not supported");
+}
+
+const char* layer_name(int kind) {
+  switch (kind) {
+    case kXLSTM: return "xlstm";
+    case kMamba2: return "mamba2";
+    case kRetNet: return "retnet";
+    case kHawk: return "hawk";
+  }
+  return "?";
+}
+
+namespace {
+
+constexpr int kRowThreads = 256;
+
+struct RowCtx {
+  const int* n_dev;
+  int rows;
+  const int* slots;
+};
+
+__device__ __forceinline__ bool row_live(const RowCtx& r, int row) { return row < live_rows(r.n_dev, r.rows); }
+__device__ __forceinline__ long long row_slot(const RowCtx& r, int row) { return r.slots ? r.slots[row] : row; }
+
+// nn.Conv1d(C, C, 4, groups=C) on the window [state (3 taps), x] (model/modules.py:37-41).
+// Weights are stored tap-major (4, C); the state row is (3, C).
+__device__ __forceinline__ float conv_step(const float* w, const float* bias, float* st, int C, int c, float x) {
+  const float s0 = st[c], s1 = st[C + c], s2 = st[2 * C + c];
+  float acc = w[c] * s0;
+  acc = fmaf(w[C + c], s1, acc);
+  acc = fmaf(w[2 * C + c], s2, acc);
+  acc = fmaf(w[3 * C + c], x, acc);
+  st[c] = s1;
+  st[C + c] = s2;
+  st[2 * C + c] = x;
+  return acc + bias[c];
+}
+
+// Mean and 1/sqrt(var + eps) of G groups of gs consecutive values; one warp per
+// group, deterministic order. Results in smem gm[g], gr[g]; ends with a barrier.
+__device__ void group_stats(const float* v, int G, int gs, float eps, float* gm, float* gr) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int g = w; g < G; g += nw) {
+    const float* x = v + size_t(g) * gs;
+    float s = 0.f;
+    for (int i = lane; i < gs; i += 32) s += x[i];
+    const float mu = warp_sum(s) / float(gs);
+    float q = 0.f;
+    for (int i = lane; i < gs; i += 32) {
+      const float d = x[i] - mu;
+      q = fmaf(d, d, q);
+    }
+    q = warp_sum(q) / float(gs);
+    if (lane == 0) {
+      gm[g] = mu;
+      gr[g] = 1.0f / sqrtf(q + eps);
+    }
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------ Block glue
+
+struct RmsP {
+  RowCtx rc;
+  const float* x; const float* w; float* out; int H; float eps;
+};
+__global__ void __launch_bounds__(kRowThreads) k_rmsnorm(const RmsP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  __shared__ float red[32];
+  const float* x = p.x + size_t(r) * p.H;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < p.H; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+  ss = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(ss / float(p.H) + p.eps);
+  float* o = p.out + size_t(r) * p.H;
+  for (int i = threadIdx.x; i < p.H; i += blockDim.x) o[i] = x[i] * inv * (p.w ? p.w[i] : 1.0f);
+}
+
+struct OutP {
+  RowCtx rc;
+  const float* x; const float* w; const float* b; int H; float* preds; int ld; int col;
+};
+__global__ void __launch_bounds__(kRowThreads) k_output_proj(const OutP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  __shared__ float red[32];
+  const float* x = p.x + size_t(r) * p.H;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < p.H; i += blockDim.x) s = fmaf(x[i], p.w[i], s);
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) p.preds[size_t(r) * p.ld + p.col] = s + p.b[0];
+}
+
+__global__ void k_set_rows(int* n, int v) { *n = v; }
+
+// ---------------------------------------------------------------- Mamba2
+// model/mamba2.py:62-168.
+
+struct Mamba2PreP {
+  RowCtx rc;
+  const float* proj; int ldp; int mi, bc, nh;  // proj row: [x (mi) | z (mi) | b (bc) | c (bc)]
+  const float* dtp;                            // dt_proj output [row][nh]
+  float* xconv; long long xcs; float* bconv; long long bcs; float* cconv; long long ccs;
+  const float *wx, *bx, *wb, *bb, *wc, *bcv, *a;
+  float *xs, *bs, *cs, *dt, *dc;
+};
+__global__ void __launch_bounds__(kRowThreads) k_mamba2_pre(const Mamba2PreP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  const long long slot = row_slot(p.rc, r);
+  const float* pr = p.proj + size_t(r) * p.ldp;
+  float* sx = p.xconv + slot * p.xcs;
+  float* sb = p.bconv + slot * p.bcs;
+  float* sc = p.cconv + slot * p.ccs;
+  // convs + SiLU (mamba2.py:84-89)
+  for (int c = threadIdx.x; c < p.mi; c += blockDim.x)
+    p.xs[size_t(r) * p.mi + c] = siluf_(conv_step(p.wx, p.bx, sx, p.mi, c, pr[c]));
+  for (int c = threadIdx.x; c < p.bc; c += blockDim.x) {
+    p.bs[size_t(r) * p.bc + c] = siluf_(conv_step(p.wb, p.bb, sb, p.bc, c, pr[2 * p.mi + c]));
+    p.cs[size_t(r) * p.bc + c] = siluf_(conv_step(p.wc, p.bcv, sc, p.bc, c, pr[2 * p.mi + p.bc + c]));
+  }
+  // dt = softplus(dt_proj(t)); decay = exp(a * dt) (mamba2.py:92-97)
+  for (int h = threadIdx.x; h < p.nh; h += blockDim.x) {
+    const float d = softplusf_(p.dtp[size_t(r) * p.nh + h]);
+    p.dt[size_t(r) * p.nh + h] = d;
+    p.dc[size_t(r) * p.nh + h] = expf(p.a[h] * d);
+  }
+}
+
+struct Mamba2PostP {
+  RowCtx rc;
+  const float* ys; const float* xs; const float* proj; int ldp; int mi, hs;
+  const float* d; const float* nw; float* A;
+};
+__global__ void __launch_bounds__(kRowThreads) k_mamba2_post(const Mamba2PostP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  extern __shared__ float g[];
+  __shared__ float red[32];
+  const float* y = p.ys + size_t(r) * p.mi;
+  const float* x = p.xs + size_t(r) * p.mi;
+  const float* z = p.proj + size_t(r) * p.ldp + p.mi;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < p.mi; c += blockDim.x) {
+    // y = state_contrib + D*x; y *= silu(z) (mamba2.py:158-163)
+    const float v = (y[c] + p.d[c / p.hs] * x[c]) * siluf_(z[c]);
+    g[c] = v;
+    ss = fmaf(v, v, ss);
+  }
+  ss = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(ss / float(p.mi) + 1e-5f);  // RMSNorm eps 1e-5 (mamba2.py:45)
+  for (int c = threadIdx.x; c < p.mi; c += blockDim.x) p.A[size_t(r) * p.mi + c] = g[c] * inv * p.nw[c];
+}
+
+class Mamba2Layer : public Layer {
+ public:
+  Mamba2Layer(const Dims& d, int lp) : d_(d), lp_(lp) {
+    mi_ = d.mamba_inner(); nh_ = d.mamba_heads(); hs_ = d.m_hs; bc_ = d.m_bc; H_ = d.H;
+    n1_ = 2 * mi_ + 2 * bc_;
+  }
+  void declare_state(StateArena& a) override {
+    l_xc_ = a.add_conv(mi_, 3);
+    l_bc_ = a.add_conv(bc_, 3);
+    l_cc_ = a.add_conv(bc_, 3);
+    l_ssm_ = a.add(nh_ * hs_ * bc_);
+  }
+  void load(WeightSource& s, WeightPack& w, const std::string& p) override {
+    const long H = H_;
+    o_w1_ = w.add_rows({{s.get(p + "input_proj.weight", mi_ * H), size_t(mi_ * H)},
+                        {s.get(p + "z_proj.weight", mi_ * H), size_t(mi_ * H)},
+                        {s.get(p + "b_proj.weight", bc_ * H), size_t(bc_ * H)},
+                        {s.get(p + "c_proj.weight", bc_ * H), size_t(bc_ * H)}}, lp_);
+    o_dtw_ = w.add(s.get(p + "dt_proj.weight", nh_ * H), nh_ * H, kF32);
+    o_dtb_ = w.add(s.get(p + "dt_proj.bias", nh_), nh_, kF32);
+    o_wx_ = w.add_conv(s.get(p + "input_conv.conv.weight", mi_ * 4), mi_, 4);
+    o_bx_ = w.add(s.get(p + "input_conv.conv.bias", mi_), mi_, kF32);
+    o_wb_ = w.add_conv(s.get(p + "b_conv.conv.weight", bc_ * 4), bc_, 4);
+    o_bb_ = w.add(s.get(p + "b_conv.conv.bias", bc_), bc_, kF32);
+    o_wc_ = w.add_conv(s.get(p + "c_conv.conv.weight", bc_ * 4), bc_, 4);
+    o_bcv_ = w.add(s.get(p + "c_conv.conv.bias", bc_), bc_, kF32);
+    o_a_ = w.add(s.get(p + "a", nh_), nh_, kF32);
+    o_d_ = w.add(s.get(p + "d", nh_), nh_, kF32);
+    o_nw_ = w.add(s.get(p + "norm.weight", mi_), mi_, kF32);
+    o_out_ = w.add(s.get(p + "out_proj.weight", H * mi_), size_t(H) * mi_, lp_);
+  }
+  void resolve(const WeightPack& w, const StateArena& a) override {
+    w1_ = w.ptr(o_w1_); dtw_ = w.ptr<float>(o_dtw_); dtb_ = w.ptr<float>(o_dtb_);
+    wx_ = w.ptr<float>(o_wx_); bx_ = w.ptr<float>(o_bx_); wb_ = w.ptr<float>(o_wb_); bb_ = w.ptr<float>(o_bb_);
+    wc_ = w.ptr<float>(o_wc_); bcv_ = w.ptr<float>(o_bcv_); a_ = w.ptr<float>(o_a_); dd_ = w.ptr<float>(o_d_);
+    nw_ = w.ptr<float>(o_nw_); out_ = w.ptr(o_out_);
+    xc_ = a.f32(l_xc_); bcs_ = a.f32(l_bc_); ccs_ = a.f32(l_cc_); ssm_ = a.f32(l_ssm_);
+    sxc_ = a.stride(l_xc_); sbc_ = a.stride(l_bc_); scc_ = a.stride(l_cc_); sssm_ = a.stride(l_ssm_);
+  }
+  struct Buf { float *proj, *dtp, *xs, *bs, *cs, *dt, *dc, *ys, *A; };
+  Buf carve(uint8_t* base, int rows) const {
+    Carver c{base};
+    Buf b;
+    b.proj = c.take<float>(size_t(rows) * n1_);
+    b.dtp = c.take<float>(size_t(rows) * nh_);
+    b.xs = c.take<float>(size_t(rows) * mi_);
+    b.bs = c.take<float>(size_t(rows) * bc_);
+    b.cs = c.take<float>(size_t(rows) * bc_);
+    b.dt = c.take<float>(size_t(rows) * nh_);
+    b.dc = c.take<float>(size_t(rows) * nh_);
+    b.ys = c.take<float>(size_t(rows) * mi_);
+    b.A = c.take<float>(size_t(rows) * mi_);
+    scratch_ = c.off;
+    return b;
+  }
+  size_t scratch_bytes(int rows) const override {
+    carve(nullptr, rows);
+    return scratch_;
+  }
+  void forward(const StepCtx& c, const float* in, float* out, const float* residual, uint8_t* scratch) override {
+    const Buf b = carve(scratch, c.rows);
+    const RowCtx rc{c.n_dev, c.rows, c.slots};
+    linear(c, in, H_, w1_, lp_, nullptr, n1_, H_, b.proj, n1_);  // x, z, b, c (mamba2.py:77-80)
+    linear(c, in, H_, dtw_, kF32, dtb_, nh_, H_, b.dtp, nh_);   // dt_proj, fp32 kept (mamba2.py:81)
+    Mamba2PreP pp{rc, b.proj, n1_, mi_, bc_, nh_, b.dtp, xc_, sxc_, bcs_, sbc_, ccs_, scc_,
+                  wx_, bx_, wb_, bb_, wc_, bcv_, a_, b.xs, b.bs, b.cs, b.dt, b.dc};
+    k_mamba2_pre<<<c.rows, kRowThreads, 0, c.s>>>(pp);
+    SsmColsParams sp;
+    sp.at = {ssm_, sssm_, c.slots, nullptr, c.rows, c.n_dev};
+    sp.nh = nh_; sp.sh = hs_; sp.sc = bc_;
+    sp.x = b.xs; sp.x_rs = mi_; sp.b = b.bs; sp.b_rs = bc_; sp.c = b.cs; sp.c_rs = bc_;
+    sp.dt = b.dt; sp.dt_rs = nh_; sp.decay = b.dc; sp.dc_rs = nh_; sp.out = b.ys; sp.o_rs = mi_;
+    ssm_cols(sp, c.rows, c.s);
+    Mamba2PostP po{rc, b.ys, b.xs, b.proj, n1_, mi_, hs_, dd_, nw_, b.A};
+    k_mamba2_post<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(po);
+    linear(c, b.A, mi_, out_, lp_, nullptr, H_, mi_, out, H_, kActNone, residual, H_);  // out_proj (mamba2.py:165)
+    B2E_CUDA(cudaGetLastError());
+  }
+
+ private:
+  Dims d_;
+  int lp_, mi_, nh_, hs_, bc_, H_, n1_;
+  mutable size_t scratch_ = 0;
+  int l_xc_ = 0, l_bc_ = 0, l_cc_ = 0, l_ssm_ = 0;
+  size_t o_w1_, o_dtw_, o_dtb_, o_wx_, o_bx_, o_wb_, o_bb_, o_wc_, o_bcv_, o_a_, o_d_, o_nw_, o_out_;
+  const void *w1_ = nullptr, *out_ = nullptr;
+  const float *dtw_, *dtb_, *wx_, *bx_, *wb_, *bb_, *wc_, *bcv_, *a_, *dd_, *nw_;
+  float *xc_, *bcs_, *ccs_, *ssm_;
+  long long sxc_, sbc_, scc_, sssm_;
+};
+
+// ---------------------------------------------------------------- RetNet
+// model/retnet.py:38-172.
+
+struct RetPreP {
+  RowCtx rc;
+  const float* proj; int H, nh, hs;  // proj row: [q | k | v | g] (4H)
+  int* pos; long long pos_s; float* scales; long long sc_s;
+  const float* angle; const float* decay; float scaling;
+  float* kr; float* qs;
+};
+__global__ void __launch_bounds__(kRowThreads) k_retnet_pre(const RetPreP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  const long long slot = row_slot(p.rc, r);
+  const float* q = p.proj + size_t(r) * 4 * p.H;
+  const float* k = q + p.H;
+  int* pos = p.pos + slot * p.pos_s;
+  float* sc = p.scales + slot * p.sc_s;
+  const float fpos = float(*pos);  // int32 counter promoted to float32 (retnet.py:78)
+  for (int e = threadIdx.x; e < p.H; e += blockDim.x) {
+    const int n = e / p.hs, j = e - n * p.hs;
+    const int mate = (j & 1) ? e - 1 : e + 1;
+    const float arg = fpos * p.angle[j];
+    const float s = sinf(arg), co = cosf(arg);
+    // rotate_every_two: even j takes -x[j+1], odd j takes x[j-1] (retnet.py:9-13)
+    const float qr = (j & 1) ? q[mate] : -q[mate];
+    const float kk = k[e] * p.scaling, km = k[mate] * p.scaling;  // k *= hs^-1/2 (retnet.py:71)
+    const float kr = (j & 1) ? km : -km;
+    const float ns = sc[n] * p.decay[n] + 1.0f;  // scales*decay + 1 (retnet.py:93)
+    const float f = 1.0f / sqrtf(ns);
+    p.qs[size_t(r) * p.H + e] = (q[e] * co + qr * s) * f;  // q_rope * scale (retnet.py:81,94-101)
+    p.kr[size_t(r) * p.H + e] = kk * co + kr * s;          // k_rope (retnet.py:82)
+  }
+  __syncthreads();  // every thread has read pos and scales
+  for (int n = threadIdx.x; n < p.nh; n += blockDim.x) sc[n] = sc[n] * p.decay[n] + 1.0f;
+  if (threadIdx.x == 0) *pos = *pos + 1;  // seq_offsets + 1 (retnet.py:172)
+}
+
+struct RetPostP {
+  RowCtx rc;
+  const float* o; const float* proj; int H, nh, hs; float* A;
+};
+__global__ void __launch_bounds__(kRowThreads) k_retnet_post(const RetPostP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  extern __shared__ float inv[];  // per head
+  const float* o = p.o + size_t(r) * p.H;
+  const float* g = p.proj + size_t(r) * 4 * p.H + 3 * p.H;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int n = w; n < p.nh; n += nw) {  // per-head RMSNorm, eps 1e-6, no affine (retnet.py:33,168)
+    float ss = 0.f;
+    for (int j = lane; j < p.hs; j += 32) ss = fmaf(o[n * p.hs + j], o[n * p.hs + j], ss);
+    ss = warp_sum(ss);
+    if (lane == 0) inv[n] = 1.0f / sqrtf(ss / float(p.hs) + 1e-6f);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < p.H; e += blockDim.x)
+    p.A[size_t(r) * p.H + e] = siluf_(g[e]) * (o[e] * inv[e / p.hs]);  // silu(g) * out (retnet.py:169)
+}
+
+class RetNetLayer : public Layer {
+ public:
+  RetNetLayer(const Dims& d, int lp) : d_(d), lp_(lp), H_(d.H), nh_(d.heads), hs_(d.retnet_hs()) {}
+  void declare_state(StateArena& a) override {
+    l_pos_ = a.add(1, kLeafI32);
+    l_sc_ = a.add(nh_);
+    l_S_ = a.add(nh_ * hs_ * hs_);
+  }
+  void load(WeightSource& s, WeightPack& w, const std::string& p) override {
+    const size_t HH = size_t(H_) * H_;
+    o_w1_ = w.add_rows({{s.get(p + "q_proj.weight", HH), HH}, {s.get(p + "k_proj.weight", HH), HH},
+                        {s.get(p + "v_proj.weight", HH), HH}, {s.get(p + "g_proj.weight", HH), HH}}, lp_);
+    o_out_ = w.add(s.get(p + "out_proj.weight", HH), HH, lp_);
+    o_decay_ = w.add(s.get(p + "decay", nh_), nh_, kF32);
+    o_angle_ = w.add(s.get(p + "angle", hs_), hs_, kF32);
+  }
+  void resolve(const WeightPack& w, const StateArena& a) override {
+    w1_ = w.ptr(o_w1_); out_ = w.ptr(o_out_); decay_ = w.ptr<float>(o_decay_); angle_ = w.ptr<float>(o_angle_);
+    pos_ = a.i32(l_pos_); sc_ = a.f32(l_sc_); S_ = a.f32(l_S_);
+    spos_ = a.stride(l_pos_); ssc_ = a.stride(l_sc_); sS_ = a.stride(l_S_);
+  }
+  struct Buf { float *proj, *kr, *qs, *o, *A; };
+  Buf carve(uint8_t* base, int rows) const {
+    Carver c{base};
+    Buf b;
+    b.proj = c.take<float>(size_t(rows) * 4 * H_);
+    b.kr = c.take<float>(size_t(rows) * H_);
+    b.qs = c.take<float>(size_t(rows) * H_);
+    b.o = c.take<float>(size_t(rows) * H_);
+    b.A = c.take<float>(size_t(rows) * H_);
+    scratch_ = c.off;
+    return b;
+  }
+  size_t scratch_bytes(int rows) const override {
+    carve(nullptr, rows);
+    return scratch_;
+  }
+  void forward(const StepCtx& c, const float* in, float* out, const float* residual, uint8_t* scratch) override {
+    const Buf b = carve(scratch, c.rows);
+    const RowCtx rc{c.n_dev, c.rows, c.slots};
+    linear(c, in, H_, w1_, lp_, nullptr, 4 * H_, H_, b.proj, 4 * H_);  // q, k, v, g (retnet.py:66-69)
+    RetPreP pp{rc, b.proj, H_, nh_, hs_, pos_, spos_, sc_, ssc_, angle_, decay_,
+               float(std::pow(double(hs_), -0.5)), b.kr, b.qs};
+    k_retnet_pre<<<c.rows, kRowThreads, 0, c.s>>>(pp);
+    OuterRowsParams op;
+    op.at = {S_, sS_, c.slots, nullptr, c.rows, c.n_dev};
+    op.nh = nh_; op.sh = hs_; op.sk = hs_;
+    op.f = decay_; op.f_rs = 0; op.f_hs = 1;
+    op.kv = b.kr; op.k_rs = H_; op.v = b.proj + 2 * H_; op.v_rs = 4 * H_;
+    op.q = b.qs; op.q_rs = H_; op.out = b.o; op.o_rs = H_;
+    outer_rows(op, c.rows, c.s);
+    RetPostP po{rc, b.o, b.proj, H_, nh_, hs_, b.A};
+    k_retnet_post<<<c.rows, kRowThreads, nh_ * sizeof(float), c.s>>>(po);
+    linear(c, b.A, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_);  // out_proj (retnet.py:170)
+    B2E_CUDA(cudaGetLastError());
+  }
+
+ private:
+  Dims d_;
+  int lp_, H_, nh_, hs_;
+  mutable size_t scratch_ = 0;
+  int l_pos_ = 0, l_sc_ = 0, l_S_ = 0;
+  size_t o_w1_, o_out_, o_decay_, o_angle_;
+  const void *w1_ = nullptr, *out_ = nullptr;
+  const float *decay_, *angle_;
+  int* pos_;
+  float *sc_, *S_;
+  long long spos_, ssc_, sS_;
+};
+
+// ------------------------------------------------------------------ Hawk
+// model/hawk.py:8-95.
+
+struct HawkConvP {
+  RowCtx rc;
+  const float* proj; int H;  // proj row: [gate (H) | recurrent (H)]
+  float* conv; long long cs; const float* w; const float* b; float* xc;
+};
+__global__ void __launch_bounds__(kRowThreads) k_hawk_conv(const HawkConvP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  float* st = p.conv + row_slot(p.rc, r) * p.cs;
+  const float* x = p.proj + size_t(r) * 2 * p.H + p.H;
+  for (int c = threadIdx.x; c < p.H; c += blockDim.x)
+    p.xc[size_t(r) * p.H + c] = conv_step(p.w, p.b, st, p.H, c, x[c]);  // hawk.py:80
+}
+
+struct RglruP {
+  RowCtx rc;
+  const float* gates; const float* xc; const float* proj; int H;
+  float* h; long long hs; const float* a; float* A;
+};
+__global__ void __launch_bounds__(kRowThreads) k_rglru(const RglruP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  float* h = p.h + row_slot(p.rc, r) * p.hs;
+  const float* gi = p.gates + size_t(r) * 2 * p.H;
+  const float* gr = gi + p.H;
+  const float* x = p.xc + size_t(r) * p.H;
+  const float* gate = p.proj + size_t(r) * 2 * p.H;
+  for (int c = threadIdx.x; c < p.H; c += blockDim.x) {
+    const float it = sigmoidf_(gi[c]), rt = sigmoidf_(gr[c]);  // hawk.py:31-32
+    const float at = powf(p.a[c], 8.0f * rt);                   // a ** (c * r), c = 8 (hawk.py:35)
+    const float mult = sqrtf(1.0f - at * at);                   // hawk.py:36
+    const float hn = h[c] * at + mult * (it * x[c]);            // hawk.py:37
+    h[c] = hn;
+    p.A[size_t(r) * p.H + c] = geluf_(gate[c]) * hn;            // out_proj(gate * h) (hawk.py:77,83-84)
+  }
+}
+
+class HawkLayer : public Layer {
+ public:
+  HawkLayer(const Dims& d, int lp) : d_(d), lp_(lp), H_(d.H), bs_(d.hawk_bs()) {}
+  void declare_state(StateArena& a) override {
+    l_conv_ = a.add_conv(H_, 3);
+    l_h_ = a.add(H_);
+  }
+  void load(WeightSource& s, WeightPack& w, const std::string& p) override {
+    const size_t HH = size_t(H_) * H_, BB = size_t(4) * bs_ * bs_;
+    o_w1_ = w.add_rows({{s.get(p + "gate_proj.weight", HH), HH}, {s.get(p + "recurrent_proj.weight", HH), HH}}, lp_);
+    o_cw_ = w.add_conv(s.get(p + "conv.conv.weight", H_ * 4), H_, 4);
+    o_cb_ = w.add(s.get(p + "conv.conv.bias", H_), H_, kF32);
+    o_a_ = w.add(s.get(p + "rglru.a", H_), H_, kF32);
+    o_gw_ = w.add_rows({{s.get(p + "rglru.input_gate.weight", BB), BB},
+                        {s.get(p + "rglru.recurrence_gate.weight", BB), BB}}, kF32);
+    o_out_ = w.add(s.get(p + "out_proj.weight", HH), HH, lp_);
+  }
+  void resolve(const WeightPack& w, const StateArena& a) override {
+    w1_ = w.ptr(o_w1_); out_ = w.ptr(o_out_); cw_ = w.ptr<float>(o_cw_); cb_ = w.ptr<float>(o_cb_);
+    a_ = w.ptr<float>(o_a_); gw_ = w.ptr<float>(o_gw_);
+    conv_ = a.f32(l_conv_); h_ = a.f32(l_h_); sconv_ = a.stride(l_conv_); sh_ = a.stride(l_h_);
+  }
+  struct Buf { float *proj, *xc, *gates, *A; };
+  Buf carve(uint8_t* base, int rows) const {
+    Carver c{base};
+    Buf b;
+    b.proj = c.take<float>(size_t(rows) * 2 * H_);
+    b.xc = c.take<float>(size_t(rows) * H_);
+    b.gates = c.take<float>(size_t(rows) * 2 * H_);
+    b.A = c.take<float>(size_t(rows) * H_);
+    scratch_ = c.off;
+    return b;
+  }
+  size_t scratch_bytes(int rows) const override {
+    carve(nullptr, rows);
+    return scratch_;
+  }
+  void forward(const StepCtx& c, const float* in, float* out, const float* residual, uint8_t* scratch) override {
+    const Buf b = carve(scratch, c.rows);
+    const RowCtx rc{c.n_dev, c.rows, c.slots};
+    linear(c, in, H_, w1_, lp_, nullptr, 2 * H_, H_, b.proj, 2 * H_);  // gate_proj, recurrent_proj (hawk.py:77-78)
+    HawkConvP cp{rc, b.proj, H_, conv_, sconv_, cw_, cb_, b.xc};
+    k_hawk_conv<<<c.rows, kRowThreads, 0, c.s>>>(cp);
+    // RG-LRU gates: two BlockLinears of 4 diagonal blocks, fp32 (hawk.py:31-32, modules.py:71-79)
+    GemmParams g;
+    g.groups = 8;
+    for (int s = 0; s < 2; ++s)
+      for (int j = 0; j < 4; ++j) {
+        GemmGroup& gg = g.g[s * 4 + j];
+        gg.A = b.xc + j * bs_;
+        gg.W = gw_ + (size_t(s) * 4 + j) * bs_ * bs_;
+        gg.C = b.gates + s * H_ + j * bs_;
+      }
+    g.M_max = c.rows; g.M_dev = c.n_dev; g.N = bs_; g.K = bs_;
+    g.lda = H_; g.ldw = bs_; g.ldc = 2 * H_;
+    gemm(g, c.s);
+    RglruP rp{rc, b.gates, b.xc, b.proj, H_, h_, sh_, a_, b.A};
+    k_rglru<<<c.rows, kRowThreads, 0, c.s>>>(rp);
+    linear(c, b.A, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_);  // out_proj (hawk.py:84)
+    B2E_CUDA(cudaGetLastError());
+  }
+
+ private:
+  Dims d_;
+  int lp_, H_, bs_;
+  mutable size_t scratch_ = 0;
+  int l_conv_ = 0, l_h_ = 0;
+  size_t o_w1_, o_cw_, o_cb_, o_a_, o_gw_, o_out_;
+  const void *w1_ = nullptr, *out_ = nullptr;
+  const float *cw_, *cb_, *a_, *gw_;
+  float *conv_, *h_;
+  long long sconv_, sh_;
+};
+
+// ----------------------------------------------------------------- xLSTM
+// model/xlstm.py:21-379: sLSTM block, then mLSTM block, then LayerNorm.
+
+struct SlstmPreP {
+  RowCtx rc;
+  const float* t; int H, nbl, bs;
+  const float* lnw;
+  float* conv; long long cs; const float* cw; const float* cb;
+  const float* h; long long hst;
+  float* axc; float* axn;  // [row][2H]: per block j, [input_j | h_j]
+};
+__global__ void __launch_bounds__(kRowThreads) k_slstm_pre(const SlstmPreP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  extern __shared__ float xn[];
+  __shared__ float gm[1], gr[1];
+  const long long slot = row_slot(p.rc, r);
+  const float* t = p.t + size_t(r) * p.H;
+  for (int c = threadIdx.x; c < p.H; c += blockDim.x) xn[c] = t[c];
+  __syncthreads();
+  group_stats(xn, 1, p.H, 1e-5f, gm, gr);  // LayerNorm(bias=False) (xlstm.py:287,307)
+  const float mu = gm[0], rs = gr[0];
+  float* st = p.conv + slot * p.cs;
+  const float* h = p.h + slot * p.hst;
+  float* axc = p.axc + size_t(r) * 2 * p.H;
+  float* axn = p.axn + size_t(r) * 2 * p.H;
+  for (int c = threadIdx.x; c < p.H; c += blockDim.x) {
+    const float x = (t[c] - mu) * rs * p.lnw[c];
+    const float xc = siluf_(conv_step(p.cw, p.cb, st, p.H, c, x));  // conv + SiLU (xlstm.py:309-310)
+    const int j = c / p.bs, e = c - j * p.bs;
+    axc[j * 2 * p.bs + e] = xc;
+    axn[j * 2 * p.bs + e] = x;
+    axc[j * 2 * p.bs + p.bs + e] = h[c];
+    axn[j * 2 * p.bs + p.bs + e] = h[c];
+  }
+}
+
+struct SlstmPostP {
+  RowCtx rc;
+  const float* G; const float* t; int H, nbl;  // G row: [i | f | z | o] (4H), pre-activations
+  float *hs_, *cs_, *ns_, *ms_; long long h_s, c_s, n_s, m_s;
+  const float *gnw, *gnb, *mlnw;
+  float* x1; float* xn2;
+};
+__global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  extern __shared__ float sm[];
+  float* y = sm;          // H
+  float* x1 = sm + p.H;   // H
+  __shared__ float gm[64], gr[64];
+  const long long slot = row_slot(p.rc, r);
+  const float* G = p.G + size_t(r) * 4 * p.H;
+  float* hh = p.hs_ + slot * p.h_s;
+  float* cc = p.cs_ + slot * p.c_s;
+  float* nn = p.ns_ + slot * p.n_s;
+  float* mm = p.ms_ + slot * p.m_s;
+  for (int e = threadIdx.x; e < p.H; e += blockDim.x) {
+    // SLSTMCell.forward (xlstm.py:247-262)
+    const float i = G[e], f = G[p.H + e], z = G[2 * p.H + e], o = G[3 * p.H + e];
+    const float lfm = mm[e] + logsigmoidf_(f);
+    const float mn = fmaxf(i, lfm);
+    const float og = sigmoidf_(o);
+    const float ig = expf(i - mn);
+    const float fg = expf(lfm - mn);
+    const float cn = fg * cc[e] + ig * tanhf(z);
+    const float nv = fg * nn[e] + ig;
+    const float yv = og * cn / (nv + 1e-6f);
+    cc[e] = cn; nn[e] = nv; mm[e] = mn; hh[e] = yv;
+    y[e] = yv;
+  }
+  __syncthreads();
+  group_stats(y, p.nbl, p.H / p.nbl, 1e-5f, gm, gr);  // GroupNorm(num_heads) (xlstm.py:300,316)
+  const float* t = p.t + size_t(r) * p.H;
+  const int gs = p.H / p.nbl;
+  for (int e = threadIdx.x; e < p.H; e += blockDim.x) {
+    const int g = e / gs;
+    const float v = (y[e] - gm[g]) * gr[g] * p.gnw[e] + p.gnb[e] + t[e];  // + skip (xlstm.py:318)
+    x1[e] = v;
+    p.x1[size_t(r) * p.H + e] = v;
+  }
+  __syncthreads();
+  group_stats(x1, 1, p.H, 1e-5f, gm, gr);  // mLSTM block LayerNorm (xlstm.py:182,202)
+  for (int e = threadIdx.x; e < p.H; e += blockDim.x)
+    p.xn2[size_t(r) * p.H + e] = (x1[e] - gm[0]) * gr[0] * p.mlnw[e];
+}
+
+struct MlstmPreP {
+  RowCtx rc;
+  const float* proj; int mi;  // proj row: [x_mlstm (mi) | x_gate (mi)]
+  float* conv; long long cs; const float* cw; const float* cb;
+  const float *wq, *wk, *wv;  // (mi/4, 4, 4)
+  float* xca; float* qkv;     // [row][mi], [row][3mi] = [q | k | v]
+};
+__global__ void __launch_bounds__(kRowThreads) k_mlstm_pre(const MlstmPreP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  extern __shared__ float xs[];  // conv+silu output (mi)
+  float* st = p.conv + row_slot(p.rc, r) * p.cs;
+  const float* xm = p.proj + size_t(r) * 2 * p.mi;
+  for (int c = threadIdx.x; c < p.mi; c += blockDim.x) {
+    const float v = siluf_(conv_step(p.cw, p.cb, st, p.mi, c, xm[c]));  // xlstm.py:206-207
+    xs[c] = v;
+    p.xca[size_t(r) * p.mi + c] = v;
+  }
+  __syncthreads();
+  float* q = p.qkv + size_t(r) * 3 * p.mi;
+  float* k = q + p.mi;
+  float* v = k + p.mi;
+  for (int e = threadIdx.x; e < p.mi; e += blockDim.x) {
+    // BlockLinear with 4x4 blocks: out[4b+kk] = sum_h x[4b+h] * W[b][kk][h] (xlstm.py:209-211)
+    const int blk = e >> 2, kk = e & 3;
+    const float* wq = p.wq + size_t(blk) * 16 + kk * 4;
+    const float* wk = p.wk + size_t(blk) * 16 + kk * 4;
+    const float* wv = p.wv + size_t(blk) * 16 + kk * 4;
+    const float* xc = xs + blk * 4;
+    const float* x0 = xm + blk * 4;
+    float aq = 0.f, ak = 0.f, av = 0.f;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      aq = fmaf(xc[h], wq[h], aq);
+      ak = fmaf(xc[h], wk[h], ak);
+      av = fmaf(x0[h], wv[h], av);
+    }
+    q[e] = aq; k[e] = ak; v[e] = av;
+  }
+}
+
+struct MlstmGatesP {
+  RowCtx rc;
+  const float* ifp; float* qkv; int mi, nh, hs;  // ifp row: [igate (nh) | fgate (nh)]
+  float* n; long long n_s; float* m; long long m_s;
+  float* g2; float* den;  // g2 row: [i (nh) | f (nh)]
+};
+__global__ void __launch_bounds__(kRowThreads) k_mlstm_gates(const MlstmGatesP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  const long long slot = row_slot(p.rc, r);
+  const float* ip = p.ifp + size_t(r) * 2 * p.nh;
+  float* q = p.qkv + size_t(r) * 3 * p.mi;
+  float* k = q + p.mi;
+  float* nst = p.n + slot * p.n_s;
+  float* mst = p.m + slot * p.m_s;
+  const float sq = sqrtf(float(p.hs));
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int h = w; h < p.nh; h += nw) {
+    // MLSTMCell.forward (xlstm.py:92-103, 121-126)
+    const float ig = ip[h], fg = ip[p.nh + h], m = mst[h];
+    const float lf = logsigmoidf_(fg);
+    const float mn = fmaxf(ig, m + lf);
+    const float i_g = expf(ig - mn);
+    const float f_g = expf(lf + m - mn);
+    float qn = 0.f;
+    for (int j = lane; j < p.hs; j += 32) {
+      const int e = h * p.hs + j;
+      const float ks = k[e] / sq;  // k / sqrt(head_size) (xlstm.py:99)
+      const float nv = f_g * nst[e] + i_g * ks;
+      k[e] = ks;
+      nst[e] = nv;
+      qn = fmaf(q[e], nv, qn);
+    }
+    qn = warp_sum(qn);
+    if (lane == 0) {
+      mst[h] = mn;
+      p.g2[size_t(r) * 2 * p.nh + h] = i_g;
+      p.g2[size_t(r) * 2 * p.nh + p.nh + h] = f_g;
+      p.den[size_t(r) * p.nh + h] = fmaxf(fabsf(qn), expf(-mn)) + 1e-6f;  // xlstm.py:130-132
+    }
+  }
+}
+
+struct MlstmPostP {
+  RowCtx rc;
+  const float* num; const float* den; const float* xca; const float* proj; int mi, nh;
+  const float *gnw, *gnb, *skip; float* A;
+};
+__global__ void __launch_bounds__(kRowThreads) k_mlstm_post(const MlstmPostP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  extern __shared__ float o[];
+  __shared__ float gm[64], gr[64];
+  const int hs = p.mi / p.nh;
+  const float* num = p.num + size_t(r) * p.mi;
+  for (int e = threadIdx.x; e < p.mi; e += blockDim.x) o[e] = num[e] / p.den[size_t(r) * p.nh + e / hs];  // xlstm.py:133
+  __syncthreads();
+  group_stats(o, p.nh, hs, 1e-5f, gm, gr);  // outnorm GroupNorm (xlstm.py:135)
+  const float* xca = p.xca + size_t(r) * p.mi;
+  const float* xg = p.proj + size_t(r) * 2 * p.mi + p.mi;
+  for (int e = threadIdx.x; e < p.mi; e += blockDim.x) {
+    const int g = e / hs;
+    const float on = (o[e] - gm[g]) * gr[g] * p.gnw[e] + p.gnb[e];
+    p.A[size_t(r) * p.mi + e] = (on + p.skip[e] * xca[e]) * siluf_(xg[e]);  // xlstm.py:215-216
+  }
+}
+
+struct XFinalP {
+  RowCtx rc;
+  const float* x2; int H; const float* w; const float* res; float* out;
+};
+__global__ void __launch_bounds__(kRowThreads) k_xlstm_final(const XFinalP p) {
+  const int r = blockIdx.x;
+  if (!row_live(p.rc, r)) return;
+  extern __shared__ float x[];
+  __shared__ float gm[1], gr[1];
+  for (int e = threadIdx.x; e < p.H; e += blockDim.x) x[e] = p.x2[size_t(r) * p.H + e];
+  __syncthreads();
+  group_stats(x, 1, p.H, 1e-5f, gm, gr);  // final LayerNorm (xlstm.py:365)
+  for (int e = threadIdx.x; e < p.H; e += blockDim.x) {
+    const float y = (x[e] - gm[0]) * gr[0] * p.w[e];
+    p.out[size_t(r) * p.H + e] = p.res ? p.res[size_t(r) * p.H + e] + y : y;
+  }
+}
+
+class XLSTMLayer : public Layer {
+ public:
+  XLSTMLayer(const Dims& d, int lp) : d_(d), lp_(lp) {
+    H_ = d.H; nbl_ = d.slstm_heads(); bs_ = d.slstm_bs();
+    mi_ = d.mlstm_inner(); nh_ = d.mlstm_heads(); hs_ = d.mlstm_hs();
+  }
+  void declare_state(StateArena& a) override {
+    // (xlstm.py:331-336, 276-282, 232-236, 150-156) in init_state order
+    l_sconv_ = a.add_conv(H_, 3);
+    l_sh_ = a.add(H_);
+    l_sc_ = a.add(H_);
+    l_sn_ = a.add(H_);
+    l_sm_ = a.add(H_, kLeafF32, -INFINITY);
+    l_mconv_ = a.add_conv(mi_, 3);
+    l_C_ = a.add(nh_ * hs_ * hs_);
+    l_n_ = a.add(nh_ * hs_);
+    l_m_ = a.add(nh_);
+  }
+  void load(WeightSource& s, WeightPack& w, const std::string& p) override {
+    const size_t H = H_, BB = size_t(nbl_) * bs_ * bs_;
+    o_slnw_ = w.add(s.get(p + "slstm.norm.weight", H), H, kF32);
+    o_scw_ = w.add_conv(s.get(p + "slstm.conv1d.conv.weight", H * 4), H_, 4);
+    o_scb_ = w.add(s.get(p + "slstm.conv1d.conv.bias", H), H, kF32);
+    // Wcat[g][j] = [W_input_g[j] | W_state_g[j]]  (bs x 2bs), gates in order i, f, z, o
+    const char* gates = "ifzo";
+    std::vector<const float*> win(4), wst(4), bst(4);
+    for (int g = 0; g < 4; ++g) {
+      const std::string gn(1, gates[g]);
+      win[g] = s.get(p + "slstm." + gn + "gate_input.weight", BB);
+      wst[g] = s.get(p + "slstm." + gn + "gate_state.weight", BB);
+      bst[g] = s.get(p + "slstm." + gn + "gate_state.bias", H);
+    }
+    const int nbl = nbl_, bs = bs_;
+    o_swcat_ = w.reserve(size_t(4) * nbl * bs * 2 * bs * 4, [=](uint8_t* dst) {
+      float* o = reinterpret_cast<float*>(dst);
+      for (int g = 0; g < 4; ++g)
+        for (int j = 0; j < nbl; ++j)
+          for (int e = 0; e < bs; ++e) {
+            float* row = o + ((size_t(g) * nbl + j) * bs + e) * 2 * bs;
+            const float* a = win[g] + (size_t(j) * bs + e) * bs;
+            const float* b = wst[g] + (size_t(j) * bs + e) * bs;
+            std::copy(a, a + bs, row);
+            std::copy(b, b + bs, row + bs);
+          }
+    });
+    o_sbias_ = w.add_rows({{bst[0], H}, {bst[1], H}, {bst[2], H}, {bst[3], H}}, kF32);
+    o_sgnw_ = w.add(s.get(p + "slstm.group_norm.weight", H), H, kF32);
+    o_sgnb_ = w.add(s.get(p + "slstm.group_norm.bias", H), H, kF32);
+    const size_t mi = mi_, QB = size_t(mi_ / 4) * 16;
+    o_skip_ = w.add(s.get(p + "mlstm.learnable_skip", mi), mi, kF32);
+    o_mlnw_ = w.add(s.get(p + "mlstm.norm.weight", H), H, kF32);
+    o_mw1_ = w.add_rows({{s.get(p + "mlstm.x_proj.weight", mi * H), mi * H},
+                         {s.get(p + "mlstm.gate_proj.weight", mi * H), mi * H}}, lp_);
+    o_wq_ = w.add(s.get(p + "mlstm.q_proj.weight", QB), QB, kF32);
+    o_wk_ = w.add(s.get(p + "mlstm.k_proj.weight", QB), QB, kF32);
+    o_wv_ = w.add(s.get(p + "mlstm.v_proj.weight", QB), QB, kF32);
+    o_mcw_ = w.add_conv(s.get(p + "mlstm.conv1d.conv.weight", mi * 4), mi_, 4);
+    o_mcb_ = w.add(s.get(p + "mlstm.conv1d.conv.bias", mi), mi, kF32);
+    const std::string cp = p + "mlstm.mlstm_cell.";
+    const size_t GW = size_t(nh_) * 3 * mi;
+    o_gw_ = w.add_rows({{s.get(cp + "igate_proj.weight", GW), GW}, {s.get(cp + "fgate_proj.weight", GW), GW}}, kF32);
+    o_gb_ = w.add_rows({{s.get(cp + "igate_proj.bias", nh_), size_t(nh_)},
+                        {s.get(cp + "fgate_proj.bias", nh_), size_t(nh_)}}, kF32);
+    o_ongw_ = w.add(s.get(cp + "outnorm.weight", mi), mi, kF32);
+    o_ongb_ = w.add(s.get(cp + "outnorm.bias", mi), mi, kF32);
+    o_down_ = w.add(s.get(p + "mlstm.proj_down.weight", H * mi), H * mi, lp_);
+    o_fnw_ = w.add(s.get(p + "final_norm.weight", H), H, kF32);
+  }
+  void resolve(const WeightPack& w, const StateArena& a) override {
+    slnw_ = w.ptr<float>(o_slnw_); scw_ = w.ptr<float>(o_scw_); scb_ = w.ptr<float>(o_scb_);
+    swcat_ = w.ptr<float>(o_swcat_); sbias_ = w.ptr<float>(o_sbias_);
+    sgnw_ = w.ptr<float>(o_sgnw_); sgnb_ = w.ptr<float>(o_sgnb_);
+    skip_ = w.ptr<float>(o_skip_); mlnw_ = w.ptr<float>(o_mlnw_); mw1_ = w.ptr(o_mw1_);
+    wq_ = w.ptr<float>(o_wq_); wk_ = w.ptr<float>(o_wk_); wv_ = w.ptr<float>(o_wv_);
+    mcw_ = w.ptr<float>(o_mcw_); mcb_ = w.ptr<float>(o_mcb_); gw_ = w.ptr<float>(o_gw_); gb_ = w.ptr<float>(o_gb_);
+    ongw_ = w.ptr<float>(o_ongw_); ongb_ = w.ptr<float>(o_ongb_); down_ = w.ptr(o_down_); fnw_ = w.ptr<float>(o_fnw_);
+    sconv_ = a.f32(l_sconv_); sh_ = a.f32(l_sh_); sc_ = a.f32(l_sc_); sn_ = a.f32(l_sn_); sm_ = a.f32(l_sm_);
+    mconv_ = a.f32(l_mconv_); C_ = a.f32(l_C_); n_ = a.f32(l_n_); m_ = a.f32(l_m_);
+    ssconv_ = a.stride(l_sconv_); ssh_ = a.stride(l_sh_); ssc_ = a.stride(l_sc_); ssn_ = a.stride(l_sn_);
+    ssm_ = a.stride(l_sm_); smconv_ = a.stride(l_mconv_); sC_ = a.stride(l_C_); sn2_ = a.stride(l_n_);
+    sm2_ = a.stride(l_m_);
+  }
+  struct Buf { float *axc, *axn, *G, *x1, *xn2, *proj, *xca, *qkv, *ifp, *g2, *den, *num, *A, *x2; };
+  Buf carve(uint8_t* base, int rows) const {
+    Carver c{base};
+    Buf b;
+    const size_t R = rows;
+    b.axc = c.take<float>(R * 2 * H_);
+    b.axn = c.take<float>(R * 2 * H_);
+    b.G = c.take<float>(R * 4 * H_);
+    b.x1 = c.take<float>(R * H_);
+    b.xn2 = c.take<float>(R * H_);
+    b.proj = c.take<float>(R * 2 * mi_);
+    b.xca = c.take<float>(R * mi_);
+    b.qkv = c.take<float>(R * 3 * mi_);
+    b.ifp = c.take<float>(R * 2 * nh_);
+    b.g2 = c.take<float>(R * 2 * nh_);
+    b.den = c.take<float>(R * nh_);
+    b.num = c.take<float>(R * mi_);
+    b.A = c.take<float>(R * mi_);
+    b.x2 = c.take<float>(R * H_);
+    scratch_ = c.off;
+    return b;
+  }
+  size_t scratch_bytes(int rows) const override {
+    carve(nullptr, rows);
+    return scratch_;
+  }
+  void forward(const StepCtx& c, const float* in, float* out, const float* residual, uint8_t* scratch) override {
+    const Buf b = carve(scratch, c.rows);
+    const RowCtx rc{c.n_dev, c.rows, c.slots};
+    // ---- sLSTM block (xlstm.py:304-318)
+    SlstmPreP sp{rc, in, H_, nbl_, bs_, slnw_, sconv_, ssconv_, scw_, scb_, sh_, ssh_, b.axc, b.axn};
+    k_slstm_pre<<<c.rows, kRowThreads, H_ * sizeof(float), c.s>>>(sp);
+    // i, f from the conv branch, z, o from the normed input, each + BlockLinear(h) + bias (xlstm.py:312-315)
+    for (int g0 = 0; g0 < 4 * nbl_; g0 += kMaxGroups) {
+      GemmParams gp;
+      gp.groups = std::min(kMaxGroups, 4 * nbl_ - g0);
+      for (int q = 0; q < gp.groups; ++q) {
+        const int gi = g0 + q, g = gi / nbl_, j = gi % nbl_;
+        GemmGroup& gg = gp.g[q];
+        gg.A = (g < 2 ? b.axc : b.axn) + size_t(j) * 2 * bs_;
+        gg.W = swcat_ + size_t(gi) * bs_ * 2 * bs_;
+        gg.bias = sbias_ + size_t(g) * H_ + j * bs_;
+        gg.C = b.G + size_t(g) * H_ + j * bs_;
+      }
+      gp.M_max = c.rows; gp.M_dev = c.n_dev; gp.N = bs_; gp.K = 2 * bs_;
+      gp.lda = 2 * H_; gp.ldw = 2 * bs_; gp.ldc = 4 * H_;
+      gemm(gp, c.s);
+    }
+    SlstmPostP so{rc, b.G, in, H_, nbl_, sh_, sc_, sn_, sm_, ssh_, ssc_, ssn_, ssm_, sgnw_, sgnb_, mlnw_, b.x1, b.xn2};
+    k_slstm_post<<<c.rows, kRowThreads, 2 * H_ * sizeof(float), c.s>>>(so);
+    // ---- mLSTM block (xlstm.py:198-219)
+    linear(c, b.xn2, H_, mw1_, lp_, nullptr, 2 * mi_, H_, b.proj, 2 * mi_);  // x_proj, gate_proj
+    MlstmPreP mp{rc, b.proj, mi_, mconv_, smconv_, mcw_, mcb_, wq_, wk_, wv_, b.xca, b.qkv};
+    k_mlstm_pre<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(mp);
+    linear(c, b.qkv, 3 * mi_, gw_, kF32, gb_, 2 * nh_, 3 * mi_, b.ifp, 2 * nh_);  // igate/fgate, fp32 kept
+    MlstmGatesP gp{rc, b.ifp, b.qkv, mi_, nh_, hs_, n_, sn2_, m_, sm2_, b.g2, b.den};
+    k_mlstm_gates<<<c.rows, kRowThreads, 0, c.s>>>(gp);
+    OuterRowsParams op;
+    op.at = {C_, sC_, c.slots, nullptr, c.rows, c.n_dev};
+    op.nh = nh_; op.sh = hs_; op.sk = hs_;
+    op.f = b.g2 + nh_; op.f_rs = 2 * nh_; op.f_hs = 1;
+    op.i = b.g2; op.i_rs = 2 * nh_; op.i_hs = 1;
+    op.kv = b.qkv + mi_; op.k_rs = 3 * mi_;
+    op.v = b.qkv + 2 * mi_; op.v_rs = 3 * mi_;
+    op.q = b.qkv; op.q_rs = 3 * mi_;
+    op.out = b.num; op.o_rs = mi_;
+    outer_rows(op, c.rows, c.s);
+    MlstmPostP pp{rc, b.num, b.den, b.xca, b.proj, mi_, nh_, ongw_, ongb_, skip_, b.A};
+    k_mlstm_post<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(pp);
+    linear(c, b.A, mi_, down_, lp_, nullptr, H_, mi_, b.x2, H_, kActNone, b.x1, H_);  // proj_down + skip
+    XFinalP fp{rc, b.x2, H_, fnw_, residual, out};
+    k_xlstm_final<<<c.rows, kRowThreads, H_ * sizeof(float), c.s>>>(fp);
+    B2E_CUDA(cudaGetLastError());
+  }
+
+ private:
+  Dims d_;
+  int lp_, H_, nbl_, bs_, mi_, nh_, hs_;
+  mutable size_t scratch_ = 0;
+  int l_sconv_, l_sh_, l_sc_, l_sn_, l_sm_, l_mconv_, l_C_, l_n_, l_m_;
+  size_t o_slnw_, o_scw_, o_scb_, o_swcat_, o_sbias_, o_sgnw_, o_sgnb_, o_skip_, o_mlnw_, o_mw1_, o_wq_, o_wk_,
+      o_wv_, o_mcw_, o_mcb_, o_gw_, o_gb_, o_ongw_, o_ongb_, o_down_, o_fnw_;
+  const float *slnw_, *scw_, *scb_, *swcat_, *sbias_, *sgnw_, *sgnb_, *skip_, *mlnw_, *wq_, *wk_, *wv_, *mcw_,
+      *mcb_, *gw_, *gb_, *ongw_, *ongb_, *fnw_;
+  const void *mw1_ = nullptr, *down_ = nullptr;
+  float *sconv_, *sh_, *sc_, *sn_, *sm_, *mconv_, *C_, *n_, *m_;
+  long long ssconv_, ssh_, ssc_, ssn_, ssm_, smconv_, sC_, sn2_, sm2_;
+};
+
+}  // namespace
+
+// ------------------------------------------------------------ public glue
+
+std::unique_ptr<Layer> Layer::make(int kind, const Dims& d, int lp) {
+  switch (kind) {
+    case kXLSTM: return std::make_unique<XLSTMLayer>(d, lp);
+    case kMamba2: return std::make_unique<Mamba2Layer>(d, lp);
+    case kRetNet: return std::make_unique<RetNetLayer>(d, lp);
+    case kHawk: return std::make_unique<HawkLayer>(d, lp);
+  }
+  throw Error(kErrInvalid, "unknown layer kind " + std::to_string(kind));
+}
+
+void rmsnorm_rows(const StepCtx& c, const float* x, const float* w, float eps, int H, float* out) {
+  RmsP p{{c.n_dev, c.rows, c.slots}, x, w, out, H, eps};
+  k_rmsnorm<<<c.rows, kRowThreads, 0, c.s>>>(p);
+  B2E_CUDA(cudaGetLastError());
+}
+
+void output_proj_rows(const StepCtx& c, const float* x, const float* w, const float* b, int H, float* preds, int ld,
+                      int col) {
+  OutP p{{c.n_dev, c.rows, c.slots}, x, w, b, H, preds, ld, col};
+  k_output_proj<<<c.rows, kRowThreads, 0, c.s>>>(p);
+  B2E_CUDA(cudaGetLastError());
+}
+
+void linear(const StepCtx& c, const float* A, int lda, const void* W, int wt, const void* bias, int N, int K,
+            float* C, int ldc, int act, const float* R, int ldr) {
+  GemmParams p;
+  p.groups = 1;
+  p.g[0].A = A;
+  p.g[0].W = W;
+  p.g[0].bias = bias;
+  p.g[0].C = C;
+  p.g[0].R = R;
+  p.M_max = c.rows;
+  p.M_dev = c.n_dev;
+  p.N = N;
+  p.K = K;
+  p.lda = lda;
+  p.ldw = K;
+  p.ldc = ldc;
+  p.ldr = ldr;
+  p.a_type = kF32;
+  p.w_type = wt;
+  p.bias_type = wt;  // CastLinear stores its bias in the weight's type (example_model.py:85-88)
+  p.round_out = wt != kF32;
+  p.act = act;
+  gemm(p, c.s);
+}
+
+void set_rows(int* n_dev, int n, cudaStream_t s) {
+  k_set_rows<<<1, 1, 0, s>>>(n_dev, n);
+  B2E_CUDA(cudaGetLastError());
+}
+
+}  // namespace b2e

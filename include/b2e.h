@@ -1,0 +1,151 @@
+/*
+ * b2e.h - C ABI of the B200 ensemble decode engine (libb2e.so).
+ *
+ * Plain C types only: pointers, sizes and status codes. Every function returns 0
+ * on success or a negative B2E_ERR_* code; b2e_last_error() then holds a message
+ * for the calling thread. Nothing here aborts, traps or prints.
+ *
+ * What each entry point replaces in the reference (huixu11/hackathon), whose hot
+ * path is Python over torch:
+ *   b2e_engine_create   NnInferenceClient.__init__: MultiTowerModel(config) +
+ *                       load_state_dict + convert_linears + init_state(capacity)
+ *                       (example_model.py:249-398)
+ *   b2e_engine_step     one round of process_batch: stage features and the
+ *                       active rows, run the step, read preds
+ *                       (example_model.py:848-883, _step at :400-429)
+ *   b2e_engine_reset_slots / read_slot / write_slot
+ *                       init_state rows and the batched_state leaves
+ *                       (model/inference_model.py:145-146)
+ *   b2e_mlstm_step / b2e_retnet_step / b2e_mamba2_step
+ *                       model/kernels.py mlstm_step / retnet_step / mamba2_step
+ *                       (model/kernels.py:346-401)
+ *   b2e_layer_*         one layer's forward(x, state, mask) with its own state
+ *                       table (model/xlstm.py:355, model/mamba2.py:62,
+ *                       model/retnet.py:38, model/hawk.py:60)
+ */
+#ifndef B2E_H
+#define B2E_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2E_API __attribute__((visibility("default")))
+#else
+#define B2E_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2E_OK 0
+#define B2E_ERR_INVALID (-1)  /* bad argument, size or name */
+#define B2E_ERR_CUDA (-2)     /* a CUDA runtime call failed */
+#define B2E_ERR_WEIGHTS (-3)  /* weight missing, unexpected, or wrong size */
+#define B2E_ERR_CAPACITY (-4) /* slot or batch outside the engine's capacity */
+#define B2E_ERR_INTERNAL (-5)
+
+/* Storage type of the nn.Linear weights: LINEAR_DTYPE of example_model.py:151-157.
+ * The four fp32-kept linears (example_model.py:106), BlockLinear, convs and norms
+ * stay float32 in every mode. */
+#define B2E_DTYPE_F32 0
+#define B2E_DTYPE_BF16 1
+#define B2E_DTYPE_F16 2
+
+/* Layer kinds, in MultiTowerModel's tower order (model/inference_model.py:107-112). */
+#define B2E_LAYER_XLSTM 0
+#define B2E_LAYER_MAMBA2 1
+#define B2E_LAYER_RETNET 2
+#define B2E_LAYER_HAWK 3
+
+/* ModelConfig (model/inference_model.py:21-27) plus Mamba2's constructor sizes
+ * (model/mamba2.py:10-17; the model uses head_size 64, bc_head_size 128). */
+typedef struct b2e_model_config {
+  int32_t hidden_size;
+  int32_t proj_size;
+  int32_t tower_depth;
+  int32_t num_heads;
+  int32_t num_features;
+  int32_t mamba_head_size;
+  int32_t mamba_bc_size;
+} b2e_model_config;
+
+typedef struct b2e_engine_options {
+  int32_t device;       /* CUDA device ordinal */
+  int32_t linear_dtype; /* B2E_DTYPE_* */
+  int32_t capacity;     /* symbol slots of recurrent state (num_symbols, example_model.py:335) */
+  int32_t max_batch;    /* rows per step, <= 65535 */
+  int32_t use_graphs;   /* 1: replay each step from a CUDA graph per batch bucket */
+} b2e_engine_options;
+
+/* A named float32 host tensor, keyed like MultiTowerModel.state_dict(). */
+typedef struct b2e_tensor {
+  const char* name;
+  const float* data;
+  int64_t numel;
+} b2e_tensor;
+
+typedef struct b2e_engine b2e_engine;
+typedef struct b2e_layer b2e_layer;
+
+B2E_API const char* b2e_last_error(void);
+B2E_API const char* b2e_version(void);
+
+/* ---- ensemble engine (one per device) ---- */
+B2E_API int b2e_engine_create(const b2e_model_config* cfg, const b2e_engine_options* opt, const b2e_tensor* tensors,
+                      int32_t n_tensors, b2e_engine** out);
+B2E_API void b2e_engine_destroy(b2e_engine* e);
+/* One step over n rows: slots[n] (distinct, < capacity), features[n * num_features]
+ * and preds[n * 4] are HOST buffers; columns are xLSTM, Mamba2, RetNet, Hawk. */
+B2E_API int b2e_engine_step(b2e_engine* e, const int32_t* slots, const float* features, int32_t n, float* preds);
+/* The same step split in two, so several devices can run at once. */
+B2E_API int b2e_engine_submit(b2e_engine* e, const int32_t* slots, const float* features, int32_t n);
+B2E_API int b2e_engine_wait(b2e_engine* e, float* preds);
+/* Device-buffer step enqueued on `stream` (a cudaStream_t, NULL = default stream).
+ * Slots outside the table step no row and set a flag read by b2e_engine_device_error. */
+B2E_API int b2e_engine_step_device(b2e_engine* e, const int32_t* d_slots, const float* d_features, int32_t n,
+                           float* d_preds, void* stream);
+B2E_API int b2e_engine_device_error(b2e_engine* e, int32_t* flag);
+B2E_API int b2e_engine_reset_slots(b2e_engine* e, const int32_t* slots, int32_t n);
+/* One slot's whole state, every leaf in iter_state_tensors order
+ * (example_model.py:160-176) and in the reference's per-row layout. */
+B2E_API int b2e_engine_slot_bytes(const b2e_engine* e, int64_t* bytes);
+B2E_API int b2e_engine_read_slot(b2e_engine* e, int32_t slot, void* host, int64_t bytes);
+B2E_API int b2e_engine_write_slot(b2e_engine* e, int32_t slot, const void* host, int64_t bytes);
+/* Kernels one step of n rows launches (counted from its captured graph). */
+B2E_API int b2e_engine_launches(b2e_engine* e, int32_t n, int32_t* kernels);
+B2E_API int b2e_engine_memory(const b2e_engine* e, int64_t* weight_bytes, int64_t* state_bytes);
+
+/* ---- fused state steps: the model/kernels.py operator API ----
+ * All pointers are DEVICE pointers to contiguous float32 arrays; mask is a
+ * device bool/uint8 array of `batch` entries or NULL (every row active). The
+ * state is updated in place on active rows only; out gets zeros on idle rows. */
+B2E_API int b2e_mlstm_step(float* cell, const float* q, const float* k, const float* v, const float* i_gate,
+                   const float* f_gate, const uint8_t* mask, int32_t batch, int32_t heads, int32_t size_h,
+                   int32_t size_k, float* out, void* stream);
+B2E_API int b2e_retnet_step(float* state, const float* k_rope, const float* v, const float* q_scaled, const float* decay,
+                    const uint8_t* mask, int32_t batch, int32_t heads, int32_t size_h, int32_t size_k, float* out,
+                    void* stream);
+B2E_API int b2e_mamba2_step(float* ssm, const float* x, const float* b, const float* c, const float* dt,
+                    const float* decay, const uint8_t* mask, int32_t batch, int32_t heads, int32_t size_h,
+                    int32_t size_c, float* out, void* stream);
+
+/* ---- one recurrent layer with its own state table ----
+ * Weights are keyed like that layer's own state_dict() (no prefix). */
+B2E_API int b2e_layer_create(int32_t kind, const b2e_model_config* cfg, const b2e_engine_options* opt,
+                     const b2e_tensor* tensors, int32_t n_tensors, b2e_layer** out);
+B2E_API void b2e_layer_destroy(b2e_layer* l);
+/* y[n, hidden] = layer(x[n, hidden]) for rows at d_slots[n]; device buffers. */
+B2E_API int b2e_layer_step_device(b2e_layer* l, const int32_t* d_slots, const float* d_x, int32_t n, float* d_y,
+                          void* stream);
+B2E_API int b2e_layer_reset_slots(b2e_layer* l, const int32_t* slots, int32_t n);
+B2E_API int b2e_layer_slot_bytes(const b2e_layer* l, int64_t* bytes);
+B2E_API int b2e_layer_read_slot(b2e_layer* l, int32_t slot, void* host, int64_t bytes);
+B2E_API int b2e_layer_write_slot(b2e_layer* l, int32_t slot, const void* host, int64_t bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2E_H */

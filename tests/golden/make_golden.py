@@ -1,0 +1,299 @@
+"""Generate the golden fixtures by running the REFERENCE itself.
+
+Runs only where the reference checkout is present (it is imported, never
+copied): ``python tests/golden/make_golden.py --ref <reference checkout> <case>...``.
+Every case loads the seeded weights of hackathon_b200.weights into the
+reference's own torch modules (fp32, CPU), drives them through the reference's
+own forward / masked-step / process_batch code, and stores what comes out as a
+small .npz beside this script. The tests replay the same inputs through the CPU
+oracle (oracle/) and the CUDA engine and compare.
+
+Inputs are regenerated from seeds on both sides (numpy PCG64); each fixture
+stores a checksum of its inputs so a generator drift fails loudly instead of
+comparing different streams.
+
+Cases
+  cells      model/kernels.py *_reference on check_kernels.py's shapes and masks
+  layers     the four layers of check_cell_rewrite.py's CASES, 12 masked steps
+  model      MultiTowerModel at check_cell_rewrite.py's small config, masked steps,
+             fp32 and with the reference's convert_linears (bf16 CastLinear)
+  long       small model, 4 rows all active for 10,000 steps (long-stream drift)
+  api        NnInferenceClient.process_batch at the small config: rounds, order,
+             first-sight rows, capacity overflow answered with zeros
+  d0stream   BASELINE config 1: default dims, 10,000 requests, SYM_001..SYM_016
+             round-robin, one request per step (about 30 min on 8 cores)
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+import types
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+
+from hackathon_b200 import config as C  # noqa: E402
+from hackathon_b200 import weights as Wt  # noqa: E402
+from tests.golden import streams  # noqa: E402
+
+torch = None  # imported lazily with the reference
+
+
+def _import_reference(ref: str):
+    global torch
+    import torch as _torch
+
+    torch = _torch
+    torch.set_num_threads(os.cpu_count() or 8)
+    sys.path.insert(0, ref)
+    import model.inference_model as im  # noqa: F401
+    import model.kernels as kernels  # noqa: F401
+    import model.mamba2, model.retnet, model.hawk, model.xlstm  # noqa: F401,E401
+
+    return sys.modules
+
+
+def _ref_cfg(mods, cfg: C.ModelConfig):
+    im = mods["model.inference_model"]
+    return im.ModelConfig(hidden_size=cfg.hidden_size, proj_size=cfg.proj_size,
+                          tower_depth=cfg.tower_depth, num_heads=cfg.num_heads,
+                          num_features=cfg.num_features)
+
+
+def _load(module, sd):
+    missing = module.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in sd.items()}, strict=True)
+    del missing
+    return module.eval()
+
+
+def _leaves(state):
+    if isinstance(state, (list, tuple)):
+        for s in state:
+            yield from _leaves(s)
+    else:
+        yield state
+
+
+def _blend(old, new, mask):
+    """The reference client's own fold (example_model.py:907-949)."""
+    em = sys.modules.get("example_model")
+    if em is None:
+        import example_model as em  # noqa: F811
+    holder = types.SimpleNamespace()
+    holder._blend_state = types.MethodType(em.NnInferenceClient._blend_state, holder)
+    holder._blend_state(old, new, mask)
+
+
+def _save(name, meta, **arrays):
+    path = HERE / f"{name}.npz"
+    np.savez_compressed(path, meta=np.array(json.dumps(meta)), **arrays)
+    print(f"wrote {path} ({path.stat().st_size / 1024:.0f} KiB)")
+
+
+# ------------------------------------------------------------------ cases
+
+
+def case_cells(mods):
+    k = mods["model.kernels"]
+    out = {}
+    meta = {"cases": []}
+    for tag, dims_list in streams.CELL_CASES.items():
+        ref = {"mlstm": k.mlstm_step_reference, "retnet": k.retnet_step_reference,
+               "mamba2": k.mamba2_step_reference}[tag]
+        for ci, (batch, dims) in enumerate(dims_list):
+            state0, rest, masks = streams.cell_inputs(tag, batch, dims, seed=100 + ci)
+            for mname, mask in masks.items():
+                st = torch.from_numpy(state0.copy())
+                args = [torch.from_numpy(a) for a in rest]
+                tm = None if mask is None else torch.from_numpy(mask)
+                got = ref(st, *args, tm)
+                key = f"{tag}_{ci}_{mname}"
+                if mname == "mixed":  # all-true equals none; all-false leaves state0
+                    out[f"{key}_state"] = st.numpy()
+                out[f"{key}_out"] = got.numpy()
+                meta["cases"].append({"key": key, "tag": tag, "batch": batch, "dims": list(dims),
+                                      "seed": 100 + ci, "mask": mname})
+    _save("cells", meta, **out)
+
+
+def _layer_module(mods, tag, h):
+    if tag == "xlstm":
+        return mods["model.xlstm"].XLSTM(h, mlstm_num_heads=4, slstm_num_heads=2)
+    if tag == "mamba2":
+        return mods["model.mamba2"].Mamba2(h, head_size=16, bc_head_size=24)
+    if tag == "retnet":
+        return mods["model.retnet"].RetNet(h, num_heads=4)
+    if tag == "hawk":
+        return mods["model.hawk"].Hawk(h)
+    raise ValueError(tag)
+
+
+def case_layers(mods):
+    out, meta = {}, {"cases": []}
+    for tag, (cfg, steps, batch) in streams.LAYER_CASES.items():
+        sd = Wt.generate(Wt.layer_specs(tag, "", cfg), seed=7)
+        mod = _load(_layer_module(mods, tag, cfg.hidden_size), sd)
+        xs, masks = streams.layer_stream(tag, cfg, steps, batch, seed=11)
+        state = mod.init_state(batch, torch.device("cpu"))
+        ys = []
+        with torch.inference_mode():
+            for s in range(steps):
+                mask = torch.from_numpy(masks[s])
+                y, new = mod(torch.from_numpy(xs[s]), state, mask=mask)
+                _blend(state, new, mask)
+                ys.append(y.numpy())
+        out[f"{tag}_y"] = np.stack(ys)
+        for i, leaf in enumerate(_leaves(state)):
+            out[f"{tag}_state{i}"] = leaf.numpy()
+        meta["cases"].append({"tag": tag, "steps": steps, "batch": batch, "weight_seed": 7,
+                              "input_seed": 11, "input_sum": float(np.sum(xs, dtype=np.float64))})
+    _save("layers", meta, **out)
+
+
+def _model(mods, cfg, sd, lp=None):
+    im = mods["model.inference_model"]
+    m = _load(im.MultiTowerModel(_ref_cfg(mods, cfg)), sd)
+    if lp is not None:
+        import example_model as em
+
+        em.convert_linears(m, {"bf16": torch.bfloat16, "fp16": torch.float16}[lp])
+    return m
+
+
+def case_model(mods):
+    out, meta = {}, {"runs": []}
+    cfg, steps, batch = streams.MODEL_CASE
+    sd = Wt.generate_model(cfg, seed=0)
+    feats, masks = streams.model_stream(cfg, steps, batch, seed=3)
+    for lp in (None, "bf16"):
+        m = _model(mods, cfg, sd, lp)
+        state = m.init_state(batch, torch.device("cpu"))
+        preds = []
+        with torch.inference_mode():
+            for s in range(steps):
+                mask = torch.from_numpy(masks[s])
+                p, new = m(torch.from_numpy(feats[s]), state, mask=mask)
+                _blend(state, new, mask)
+                preds.append(p.numpy())
+        tag = lp or "fp32"
+        out[f"{tag}_preds"] = np.stack(preds)
+        for i, leaf in enumerate(_leaves(state)):
+            out[f"{tag}_state{i}"] = leaf.numpy()
+        meta["runs"].append(tag)
+    meta.update({"steps": steps, "batch": batch, "weight_seed": 0, "input_seed": 3,
+                 "input_sum": float(np.sum(feats, dtype=np.float64))})
+    _save("model", meta, **out)
+
+
+def case_long(mods):
+    cfg, steps, batch = streams.LONG_CASE
+    sd = Wt.generate_model(cfg, seed=0)
+    m = _model(mods, cfg, sd)
+    state = m.init_state(batch, torch.device("cpu"))
+    gen = streams.long_features(cfg, batch, seed=5)
+    preds = np.zeros((steps, batch, 4), np.float32)
+    total = 0.0
+    t0 = time.time()
+    with torch.inference_mode():
+        for s in range(steps):
+            x = next(gen)
+            total += float(np.sum(x, dtype=np.float64))
+            p, state = m(torch.from_numpy(x), state)
+            preds[s] = p.numpy()
+    print(f"long: {steps} steps in {time.time() - t0:.0f} s")
+    arrays = {"preds": preds}
+    for i, leaf in enumerate(_leaves(state)):
+        arrays[f"state{i}"] = leaf.numpy()
+    _save("long", {"steps": steps, "batch": batch, "weight_seed": 0, "input_seed": 5,
+                   "input_sum": total}, **arrays)
+
+
+def case_api(mods, ref):
+    import client as rclient
+    import example_model as em
+
+    cfg = streams.API_CFG
+    sd = Wt.generate_model(cfg, seed=0)
+    sd_t = {k: torch.from_numpy(v) for k, v in sd.items()}
+    em.hf_hub_download = lambda **kw: "<seeded>"
+    real_load = torch.load
+    torch.load = lambda f, **kw: sd_t if f == "<seeded>" else real_load(f, **kw)
+    em.ModelConfig = lambda **kw: _ref_cfg(mods, cfg)  # the client hardcodes the default dims
+    client = em.NnInferenceClient(num_symbols=streams.API_CAPACITY, device="cpu")
+    calls = streams.api_calls(cfg)
+    uids, preds, ncalls = [], [], []
+    for call in calls:
+        batch = {sym: [rclient.PendingRequest(unique_id=u, symbol=sym, features=f, received_time=0.0)
+                       for (u, f) in reqs] for sym, reqs in call}
+        r = client.process_batch(batch)
+        uids += list(r.unique_ids)
+        preds += [list(p) for p in r.predictions]
+        ncalls.append(len(r.unique_ids))
+    _save("api", {"capacity": streams.API_CAPACITY, "ncalls": ncalls,
+                  "symbol_rows": client.symbol_to_idx},
+          unique_ids=np.asarray(uids, np.int64), predictions=np.asarray(preds, np.float32))
+
+
+def case_d0stream(mods, n_requests):
+    cfg = C.D0
+    sd = Wt.generate_model(cfg, seed=0)
+    m = _model(mods, cfg, sd)
+    del sd
+    nsym = streams.D0_SYMBOLS
+    states = [m.init_state(1, torch.device("cpu")) for _ in range(nsym)]
+    feats = streams.d0_features(n_requests)
+    preds = np.zeros((n_requests, 4), np.float32)
+    t0 = time.time()
+    with torch.inference_mode():
+        for i in range(n_requests):
+            s = i % nsym
+            p, states[s] = m(torch.from_numpy(feats[i:i + 1]), states[s])
+            preds[i] = p.numpy()[0]
+            if i % 500 == 0:
+                print(f"d0stream {i}/{n_requests} {time.time() - t0:.0f} s", flush=True)
+    summ = {}
+    for s in range(nsym):
+        for li, leaf in enumerate(_leaves(states[s])):
+            a = leaf.numpy().reshape(-1)
+            summ[f"sym{s}_leaf{li}"] = streams.leaf_summary(a)
+    _save("d0stream", {"n_requests": n_requests, "symbols": nsym, "weight_seed": 0,
+                       "input_sum": float(np.sum(feats, dtype=np.float64))},
+          preds=preds, **summ)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", required=True, help="path of the reference checkout")
+    ap.add_argument("cases", nargs="+")
+    ap.add_argument("--d0-requests", type=int, default=10_000)
+    a = ap.parse_args()
+    mods = _import_reference(a.ref)
+    for c in a.cases:
+        t = time.time()
+        if c == "cells":
+            case_cells(mods)
+        elif c == "layers":
+            case_layers(mods)
+        elif c == "model":
+            case_model(mods)
+        elif c == "long":
+            case_long(mods)
+        elif c == "api":
+            case_api(mods, a.ref)
+        elif c == "d0stream":
+            case_d0stream(mods, a.d0_requests)
+        else:
+            raise SystemExit(f"unknown case {c}")
+        print(f"{c}: {time.time() - t:.0f} s")
+
+
+if __name__ == "__main__":
+    main()

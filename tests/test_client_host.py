@@ -1,0 +1,108 @@
+"""Host logic of process_batch on CPU: rounds, answer order, first-sight slots,
+overflow answered with zeros - checked against the reference's own
+process_batch (tests/golden/api.npz). The engine underneath is replaced by the
+CPU oracle here; the GPU tests run the same calls through libb2e.so."""
+
+import numpy as np
+
+from hackathon_b200 import client as CL
+from hackathon_b200 import weights as Wt
+from oracle import model as O
+from tests.conftest import assert_close, load_golden
+from tests.golden import streams
+
+
+class OracleEngine:
+    """Engine-shaped wrapper of the CPU oracle (test double)."""
+
+    def __init__(self, cfg, sd, capacity):
+        self.orc = O.Oracle(cfg, sd)
+        self.state = O.init_state(cfg, capacity)
+        self.calls = []
+
+    def submit(self, slots, feats):
+        slots = list(np.asarray(slots).reshape(-1))
+        assert len(set(slots)) == len(slots), "a symbol appears twice in one round"
+        self.calls.append(slots)
+        p, new = self.orc.step(np.asarray(feats, np.float32), O.gather_rows(self.state, slots))
+        O.scatter_rows(self.state, slots, new)
+        self._p = p
+
+    def wait(self):
+        return self._p
+
+    def close(self):
+        pass
+
+
+def make_client(monkeypatch, cfg, sd, capacity, devices=None):
+    made = []
+
+    def fake(config, weights, device, linear_dtype, cap, max_batch, graphs):
+        e = OracleEngine(config, weights, cap)
+        made.append(e)
+        return e
+
+    monkeypatch.setattr(CL.B200InferenceClient, "_make_engine", staticmethod(fake))
+    monkeypatch.setattr(CL.B200InferenceClient, "_overflow_warned", False)
+    c = CL.B200InferenceClient(num_symbols=capacity, config=cfg, weights=sd, linear_dtype="fp32", devices=devices)
+    return c, made
+
+
+def run_api_calls(client, cfg):
+    uids, preds = [], []
+    for call in streams.api_calls(cfg):
+        batch = {sym: [CL.PendingRequest(unique_id=u, symbol=sym, features=f, received_time=0.0) for (u, f) in reqs]
+                 for sym, reqs in call}
+        r = client.process_batch(batch)
+        assert len(r.unique_ids) == len(r.predictions)
+        assert all(isinstance(p, list) and len(p) == 4 and all(isinstance(v, float) for v in p)
+                   for p in r.predictions)
+        uids += list(r.unique_ids)
+        preds += r.predictions
+    return uids, np.asarray(preds, np.float32)
+
+
+def test_process_batch_matches_reference(monkeypatch, capsys):
+    g, meta = load_golden("api")
+    cfg = streams.API_CFG
+    sd = Wt.generate_model(cfg, seed=0)
+    client, _ = make_client(monkeypatch, cfg, sd, meta["capacity"])
+    uids, preds = run_api_calls(client, cfg)
+    assert uids == list(g["unique_ids"]), "answer order must be the reference's"
+    assert_close(preds, g["predictions"], 1e-4, 1e-5, "predictions")
+    assert {k: v[1] for k, v in client.symbol_to_idx.items()} == meta["symbol_rows"], "first-sight slots"
+    out = capsys.readouterr().out
+    assert out.count("WARNING: out of state rows") == 1
+
+
+def test_rounds_keep_one_request_per_symbol(monkeypatch):
+    cfg = streams.API_CFG
+    sd = Wt.generate_model(cfg, seed=0)
+    client, made = make_client(monkeypatch, cfg, sd, 8)
+    rng = np.random.default_rng(0)
+    batch = {f"S{i}": [CL.PendingRequest(100 * i + j, f"S{i}", rng.standard_normal(79).tolist(), 0.0)
+                       for j in range(n)] for i, n in enumerate([3, 1, 0, 2])}
+    r = client.process_batch(batch)
+    assert r.unique_ids == [0, 100, 300, 1, 301, 2]
+    assert made[0].calls == [[0, 1, 2], [0, 2], [0]]
+
+
+def test_sharded_client_routes_by_symbol_hash(monkeypatch):
+    """Two devices: each symbol's rows go to crc32(name) % 2, and the answers equal
+    the single-device client's."""
+    cfg = streams.API_CFG
+    sd = Wt.generate_model(cfg, seed=0)
+    one, _ = make_client(monkeypatch, cfg, sd, 16)
+    two, made = make_client(monkeypatch, cfg, sd, 16, devices=[0, 1])
+    rng = np.random.default_rng(3)
+    for step in range(3):
+        batch = {f"SYM_{i:03d}": [CL.PendingRequest(1000 * step + 10 * i + j, f"SYM_{i:03d}",
+                                                    rng.standard_normal(79).tolist(), 0.0) for j in range(1 + i % 2)]
+                 for i in range(10)}
+        r1, r2 = one.process_batch(batch), two.process_batch(batch)
+        assert r1.unique_ids == r2.unique_ids
+        assert_close(r2.predictions, r1.predictions, 1e-4, 1e-5, "sharded vs single")
+    for sym, (e, _) in two.symbol_to_idx.items():
+        assert e == CL.owner_device(sym, 2)
+    assert made[0].calls and made[1].calls
