@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--linear-dtype", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--quick", action="store_true",
+                    help="device-timed steps only (no e2e, latency, roofline or CPU legs): for profiling")
     return ap.parse_args()
 
 
@@ -296,6 +298,13 @@ def main():
     t_max = allreduce(t_ms, "max", world, dev)
     rows_all = allreduce(float(rows), "sum", world, dev)
     value = rows_all / (t_max / 1e3)
+
+    if a.quick:
+        if rank == 0:
+            print(json.dumps({"quick": True, "value": value, "unit": "requests/s", "ms_per_step": t_max / K,
+                              "launches_per_step": eng.launches_per_step(wl["max_batch"]) + 1}), flush=True)
+        eng.close()
+        return
 
     # ---- end to end through the C-ABI with host buffers (e2e)
     barrier(world)

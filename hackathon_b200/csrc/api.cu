@@ -6,6 +6,7 @@
 #include "../../include/b2e.h"
 #include "cells.cuh"
 #include "engine.cuh"
+#include "gemm.cuh"
 
 using namespace b2e;
 
@@ -15,7 +16,7 @@ struct b2e_engine {
 
 struct b2e_layer {
   Dims d;
-  int kind = 0, device = 0, capacity = 0, max_batch = 0;
+  int kind = 0, device = 0, capacity = 0, max_batch = 0, lp = 0;
   WeightPack pack;
   StateArena arena;
   std::unique_ptr<Layer> layer;
@@ -260,6 +261,36 @@ int b2e_mamba2_step(float* ssm, const float* x, const float* b, const float* c, 
   });
 }
 
+int b2e_linear(const void* x, int32_t x_dtype, int32_t m, int32_t k, const void* w, int32_t w_dtype,
+               const void* bias, int32_t n, int32_t act, float* y, int32_t* d_err, void* stream) {
+  return guard([&] {
+    B2E_CHECK(x && w && y, kErrInvalid, "null operand");
+    B2E_CHECK(m > 0 && m <= 65535 * 64 && n > 0 && k > 0, kErrInvalid, "bad GEMM sizes");
+    B2E_CHECK(w_dtype == kF32 || w_dtype == kBF16 || w_dtype == kF16, kErrInvalid, "unknown weight dtype");
+    B2E_CHECK(x_dtype == kF32 || x_dtype == w_dtype, kErrInvalid, "x must be f32 or the weight's dtype");
+    B2E_CHECK(act == kActNone || act == kActRelu, kErrInvalid, "unknown activation");
+    if (d_err) gemm_tc_init();
+    GemmParams p;
+    p.g[0].A = x;
+    p.g[0].W = w;
+    p.g[0].bias = bias;
+    p.g[0].C = y;
+    p.M_max = m;
+    p.N = n;
+    p.K = k;
+    p.lda = k;
+    p.ldw = k;
+    p.ldc = n;
+    p.a_type = x_dtype;
+    p.w_type = w_dtype;
+    p.bias_type = w_dtype;
+    p.round_out = w_dtype != kF32;
+    p.act = act;
+    p.err = d_err;
+    gemm(p, static_cast<cudaStream_t>(stream));
+  });
+}
+
 int b2e_layer_create(int32_t kind, const b2e_model_config* cfg, const b2e_engine_options* opt,
                      const b2e_tensor* tensors, int32_t n_tensors, b2e_layer** out) {
   return guard([&] {
@@ -274,7 +305,9 @@ int b2e_layer_create(int32_t kind, const b2e_model_config* cfg, const b2e_engine
     h->device = o.device;
     h->capacity = o.capacity;
     h->max_batch = o.max_batch;
+    h->lp = o.lp;
     B2E_CUDA(cudaSetDevice(o.device));
+    gemm_tc_init();
     WeightSource src;
     fill_source(src, tensors, n_tensors);
     h->layer = Layer::make(kind, h->d, o.lp);
@@ -311,7 +344,9 @@ int b2e_layer_step_device(b2e_layer* l, const int32_t* d_slots, const float* d_x
     c.rows = n;
     c.n_dev = h.d_n;
     c.slots = d_slots;
-    h.layer->forward(c, d_x, d_y, nullptr, h.scratch);
+    c.lp = h.lp;
+    c.err = h.d_err;
+    h.layer->forward(c, d_x, nullptr, d_y, nullptr, h.scratch);
   });
 }
 

@@ -40,6 +40,7 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   B2E_CHECK(o.max_batch > 0 && o.max_batch <= 65535, kErrInvalid, "max_batch must be in 1..65535");
   B2E_CHECK(o.lp == kF32 || o.lp == kBF16 || o.lp == kF16, kErrInvalid, "unknown linear dtype");
   B2E_CUDA(cudaSetDevice(o.device));
+  gemm_tc_init();
   const int H = d.H, P = d.P, F = d.F, lp = o.lp;
 
   // ---- weights (strict key names of MultiTowerModel.state_dict())
@@ -91,6 +92,7 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
     Carver c{nullptr};
     c.take<float>(R * H);
     c.take<float>(R * H);
+    c.take<float>(R * H);
     c.take<float>(R * P);
     const size_t glue = (c.off + 255) & ~size_t(255);
     uint8_t* base = nullptr;
@@ -98,6 +100,7 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
     Carver g{base};
     tw.x = g.take<float>(R * H);
     tw.t = g.take<float>(R * H);
+    tw.tl = g.take<float>(R * H);
     tw.u = g.take<float>(R * P);
     tw.scratch = base + glue;
     B2E_CUDA(cudaStreamCreateWithFlags(&tw.s, cudaStreamNonBlocking));
@@ -150,16 +153,23 @@ int Engine::bucket(int n) const {
 
 void Engine::tower_forward(Tower& tw, int idx, const StepCtx& c) {
   const int H = d_.H, P = d_.P, F = d_.F, lp = opt_.lp;
+  const bool low = lp != kF32;
+  // GEMM inputs are written in the CastLinear type (the cast CastLinear applies,
+  // example_model.py:93-94): u and tl hold bf16/f16 values when `low`.
+  float* u32 = low ? nullptr : tw.u;
+  void* ulp = low ? static_cast<void*>(tw.u) : nullptr;
+  const float eps = 1.1920928955078125e-07f;  // nn.RMSNorm(eps=None) in float32
   // input_up, ReLU, input_down (model/inference_model.py:88-90)
-  linear(c, d_feats_, F, tw.upw, lp, tw.upb, P, F, tw.u, P, kActRelu);
-  linear(c, tw.u, P, tw.dnw, lp, tw.dnb, H, P, tw.x, H);
+  linear(c, d_feats_, kF32, F, tw.upw, lp, tw.upb, P, F, u32, P, kActRelu, nullptr, 0, ulp, P);
+  linear(c, tw.u, lp, P, tw.dnw, lp, tw.dnb, H, P, tw.x, H);
   for (auto& bl : tw.blocks) {
     // Block.forward: x = layer(norm1(x)) + x; x = x + mlp(norm2(x)) (model/inference_model.py:63-68)
-    rmsnorm_rows(c, tw.x, bl.n1, 1.1920928955078125e-07f, H, tw.t);
-    bl.layer->forward(c, tw.t, tw.x, tw.x, tw.scratch);
-    rmsnorm_rows(c, tw.x, bl.n2, 1.1920928955078125e-07f, H, tw.t);
-    linear(c, tw.t, H, bl.f1w, lp, bl.f1b, P, H, tw.u, P, kActRelu);               // fc1 + ReLU
-    linear(c, tw.u, P, bl.f2w, lp, bl.f2b, H, P, tw.x, H, kActNone, tw.x, H);      // fc2 + residual
+    rmsnorm_rows(c, tw.x, bl.n1, eps, H, tw.t, low ? tw.tl : nullptr);
+    bl.layer->forward(c, tw.t, low ? tw.tl : nullptr, tw.x, tw.x, tw.scratch);
+    rmsnorm_rows(c, tw.x, bl.n2, eps, H, low ? nullptr : tw.t, low ? tw.tl : nullptr);
+    linear(c, low ? static_cast<const void*>(tw.tl) : tw.t, lp, H, bl.f1w, lp, bl.f1b, P, H, u32, P, kActRelu,
+           nullptr, 0, ulp, P);                                                       // fc1 + ReLU
+    linear(c, tw.u, lp, P, bl.f2w, lp, bl.f2b, H, P, tw.x, H, kActNone, tw.x, H);     // fc2 + residual
   }
   output_proj_rows(c, tw.x, ow_, ob_, H, d_preds_, 4, idx);  // shared output_proj (model/inference_model.py:142)
 }
@@ -175,6 +185,7 @@ void Engine::enqueue(int rows, cudaStream_t s) {
     c.n_dev = d_n_;
     c.slots = d_slots_;
     c.lp = opt_.lp;
+    c.err = d_err_;
     tower_forward(tw, t, c);
     B2E_CUDA(cudaEventRecord(tw.done, tw.s));
   }

@@ -60,7 +60,7 @@ class Engine {
     const void *upw, *upb, *dnw, *dnb;
     std::vector<Block> blocks;
     uint8_t* scratch = nullptr;  // layer scratch
-    float *x = nullptr, *t = nullptr, *u = nullptr;
+    float *x = nullptr, *t = nullptr, *tl = nullptr, *u = nullptr;  // tl, u: CastLinear-typed GEMM inputs
     cudaStream_t s = nullptr;
     cudaEvent_t done = nullptr;
   };

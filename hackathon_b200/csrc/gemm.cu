@@ -280,6 +280,10 @@ void gemm(const GemmParams& p, cudaStream_t s) {
   B2E_CHECK(p.groups >= 1 && p.groups <= kMaxGroups, kErrInternal, "gemm: bad group count");
   B2E_CHECK(p.M_max > 0 && p.N > 0 && p.K > 0, kErrInternal, "gemm: empty problem");
   B2E_CHECK(p.M_max <= 65535 * BM, kErrInternal, "gemm: too many rows");
+  if (gemm_tc_eligible(p)) {
+    gemm_tc(p, s);
+    return;
+  }
   const int a = p.a_type, w = p.w_type;
   if (w == kF32) {
     B2E_CHECK(a == kF32, kErrInternal, "gemm: f32 weights need f32 activations");

@@ -38,10 +38,17 @@ struct GemmParams {
   int lp = kF32;      // CastLinear low type; kF32 = plain fp32 nn.Linear
   int round_out = 0;  // round the (acc + bias) to `lp` (CastLinear output)
   int act = kActNone;
+  int* err = nullptr;  // device error word for bounded-wait timeouts (tensor-core path)
 };
 
-// Enqueue on `stream`. Picks the weight-streaming kernel for M_max <= 16 and the
-// tiled kernel otherwise.
+// Enqueue on `stream`. Picks, in order: the tcgen05 tensor-core kernel
+// (gemm_tc.cu) for dense low-precision problems (A and W both bf16 or both f16,
+// more than 16 rows, K and leading dims multiples of 8), the weight-streaming
+// kernel for M_max <= 16, and the tiled SIMT kernel otherwise.
 void gemm(const GemmParams& p, cudaStream_t stream);
+
+void gemm_tc_init();  // once per device, before any capture
+bool gemm_tc_eligible(const GemmParams& p);
+void gemm_tc(const GemmParams& p, cudaStream_t stream);
 
 }  // namespace b2e

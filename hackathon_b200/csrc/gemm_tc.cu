@@ -1,0 +1,318 @@
+// tcgen05 (5th-generation tensor core) GEMM for the CastLinear projections.
+//
+// C[m, n] = epilogue( sum_k A[m, k] * W[n, k] ), A and W both bf16 (or both f16)
+// in global memory, f32 accumulation in tensor memory. One CTA computes one
+// 128 x 128 output tile:
+//   warp 0     one thread issues TMA loads of A and W tiles (128 rows x 64 K,
+//              128-byte swizzle) into a 4-stage shared-memory ring;
+//   warp 1     allocates 128 TMEM columns; one thread issues tcgen05.mma
+//              (M=128, N=128, K=16 per instruction) and commits each stage back
+//              to the producer and the finished accumulator to the epilogue;
+//   warps 2-5  read the accumulator with tcgen05.ld (each warp its 32-lane
+//              quadrant) and apply bias, CastLinear rounding, ReLU and the
+//              residual, exactly like the SIMT epilogue (gemm.cu).
+// Every mbarrier wait is bounded: past ~1 s the kernel records an error code,
+// stops issuing work, waits (bounded) for what it issued, frees its TMEM and
+// returns. TMA loads here never use cluster multicast.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "gemm.cuh"
+
+namespace b2e {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr uint32_t TILE_A = BM * BK * 2, TILE_B = BN * BK * 2;
+constexpr uint32_t TMEM_COLS = 128;
+constexpr size_t SMEM = size_t(STAGES) * (TILE_A + TILE_B) + 1024 + 256;
+constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
+
+enum TcError : int { kTcTimeoutProducer = 101, kTcTimeoutMma = 102, kTcTimeoutEpilogue = 103 };
+
+struct TcEpi {
+  const void* bias;
+  int bias_type;
+  float* C;
+  int ldc;
+  void* C_lp;
+  int ldc_lp;
+  const float* R;
+  int ldr;
+  int M_max;
+  const int* M_dev;
+  int N, K;
+  int lp;  // kBF16 or kF16: operand type and CastLinear rounding type
+  int round_out, act;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: true when the phase completed, false on timeout or abort.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+  const long long t0 = clock64();
+  while (!mbar_try(b, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes, 8-row swizzle atoms 1024 bytes apart (SBO), sm100 version bit.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr & 0x3FFFF) >> 4);      // start address
+  d |= uint64_t(1) << 16;                    // leading byte offset (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;            // stride byte offset
+  d |= uint64_t(1) << 46;                    // descriptor version (sm100)
+  d |= uint64_t(2) << 61;                    // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator, A/B type, both K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int lp) {
+  const uint32_t ab = lp == kBF16 ? 1u : 0u;
+  return (1u << 4) | (ab << 7) | (ab << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                   const __grid_constant__ TcEpi e) {
+  const int M = live_rows(e.M_dev, e.M_max);
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  if (m0 >= M) return;  // whole CTA, before any barrier or TMEM use
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * TILE_A;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * TILE_B);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const int nkb = (e.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (kb >= STAGES && !mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+          if (!*abort_flag) atomicExch(e.err, kTcTimeoutProducer);
+          *abort_flag = 1;
+          break;
+        }
+        mbar_expect_tx(&full[s], TILE_A + TILE_B);
+        tma_load_2d(sA + s * TILE_A, &ta, kb * BK, m0, &full[s]);
+        tma_load_2d(sB + s * TILE_B, &tb, kb * BK, n0, &full[s]);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // drain: every load issued lands before the CTA leaves (bounded)
+        volatile int never = 0;
+        for (int kb = max(0, issued - STAGES); kb < issued; ++kb)
+          mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1, &never);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      const uint32_t idesc = instr_desc(e.lp);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag)) {
+          if (!*abort_flag) atomicExch(e.err, kTcTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a0 = smem_u32(sA + s * TILE_A), b0 = smem_u32(sB + s * TILE_B);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)  // K=16 per instruction: +32 bytes inside the swizzled row
+          mma_f16(tmem, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), idesc, (kb | k) != 0);
+        mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+      }
+      mma_commit(done);  // accumulator complete (covers every MMA issued)
+    }
+  } else {
+    // ---- epilogue: warps 2..5, TMEM lane quadrant = warp % 4
+    volatile int never = 0;  // the MMA thread always commits `done`, even after an abort
+    const bool ok = mbar_wait(done, 0, &never);
+    if (!ok) {
+      atomicExch(e.err, kTcTimeoutEpilogue);
+      *abort_flag = 1;
+    } else if (!*abort_flag) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int q = warp & 3;
+      const int m = m0 + q * 32 + lane;
+      const bool row_ok = m < M;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (n0 + c0 >= e.N) break;  // warp-uniform
+        float v[16];
+        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
+        if (!row_ok) continue;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = n0 + c0 + j;
+          if (n >= e.N) break;
+          float x = v[j];
+          if (e.bias) x += load_as(e.bias_type, e.bias, n);
+          if (e.round_out) x = round_to(e.lp, x);
+          if (e.act == kActRelu) x = fmaxf(x, 0.0f);
+          if (e.R) x += e.R[size_t(m) * e.ldr + n];
+          if (e.C) e.C[size_t(m) * e.ldc + n] = x;
+          if (e.C_lp) store_as(e.lp, e.C_lp, size_t(m) * e.ldc_lp + n, x);
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// ------------------------------------------------------------------ host
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+void make_map(CUtensorMap* m, const void* base, int lp, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_rows) {
+  auto fn = encode_fn();
+  B2E_CHECK(fn != nullptr, kErrCuda, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {BK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, lp == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  B2E_CHECK(r == CUDA_SUCCESS, kErrCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+void gemm_tc_init() {
+  B2E_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM)));
+}
+
+bool gemm_tc_eligible(const GemmParams& p) {
+  return p.groups == 1 && (p.w_type == kBF16 || p.w_type == kF16) && p.a_type == p.w_type && p.M_max > 16 &&
+         p.K % 8 == 0 && p.lda % 8 == 0 && p.ldw % 8 == 0 && p.N % 16 == 0 && aligned16(p.g[0].A) &&
+         aligned16(p.g[0].W) && p.err != nullptr && encode_fn() != nullptr;
+}
+
+void gemm_tc(const GemmParams& p, cudaStream_t s) {
+  B2E_CHECK(gemm_tc_eligible(p), kErrInternal, "gemm_tc: problem not eligible");
+  CUtensorMap ta, tb;
+  make_map(&ta, p.g[0].A, p.w_type, uint64_t(p.K), uint64_t(p.M_max), uint64_t(p.lda), BM);
+  make_map(&tb, p.g[0].W, p.w_type, uint64_t(p.K), uint64_t(p.N), uint64_t(p.ldw), BN);
+  TcEpi e{p.g[0].bias, p.bias_type, p.g[0].C, p.ldc, p.g[0].C_lp, p.ldc_lp, p.g[0].R, p.ldr, p.M_max, p.M_dev,
+          p.N, p.K, p.w_type, p.round_out, p.act, p.err};
+  dim3 grid(ceil_div(p.N, BN), ceil_div(p.M_max, BM));
+  gemm_tc_kernel<<<grid, THREADS, SMEM, s>>>(ta, tb, e);
+  B2E_CUDA(cudaGetLastError());
+}
+
+}  // namespace b2e

@@ -93,7 +93,7 @@ __device__ void group_stats(const float* v, int G, int gs, float eps, float* gm,
 
 struct RmsP {
   RowCtx rc;
-  const float* x; const float* w; float* out; int H; float eps;
+  const float* x; const float* w; float* out; int H; float eps; void* out_lp; int lp;
 };
 __global__ void __launch_bounds__(kRowThreads) k_rmsnorm(const RmsP p) {
   const int r = blockIdx.x;
@@ -104,8 +104,11 @@ __global__ void __launch_bounds__(kRowThreads) k_rmsnorm(const RmsP p) {
   for (int i = threadIdx.x; i < p.H; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
   ss = block_sum(ss, red);
   const float inv = 1.0f / sqrtf(ss / float(p.H) + p.eps);
-  float* o = p.out + size_t(r) * p.H;
-  for (int i = threadIdx.x; i < p.H; i += blockDim.x) o[i] = x[i] * inv * (p.w ? p.w[i] : 1.0f);
+  for (int i = threadIdx.x; i < p.H; i += blockDim.x) {
+    const float v = x[i] * inv * (p.w ? p.w[i] : 1.0f);
+    if (p.out) p.out[size_t(r) * p.H + i] = v;
+    if (p.out_lp) store_as(p.lp, p.out_lp, size_t(r) * p.H + i, v);
+  }
 }
 
 struct OutP {
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre(const Mamba2PreP p) 
 struct Mamba2PostP {
   RowCtx rc;
   const float* ys; const float* xs; const float* proj; int ldp; int mi, hs;
-  const float* d; const float* nw; float* A;
+  const float* d; const float* nw; void* A; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_mamba2_post(const Mamba2PostP p) {
   const int r = blockIdx.x;
@@ -181,7 +184,7 @@ __global__ void __launch_bounds__(kRowThreads) k_mamba2_post(const Mamba2PostP p
   }
   ss = block_sum(ss, red);
   const float inv = 1.0f / sqrtf(ss / float(p.mi) + 1e-5f);  // RMSNorm eps 1e-5 (mamba2.py:45)
-  for (int c = threadIdx.x; c < p.mi; c += blockDim.x) p.A[size_t(r) * p.mi + c] = g[c] * inv * p.nw[c];
+  for (int c = threadIdx.x; c < p.mi; c += blockDim.x) store_as(p.at, p.A, size_t(r) * p.mi + c, g[c] * inv * p.nw[c]);
 }
 
 class Mamba2Layer : public Layer {
@@ -243,11 +246,14 @@ class Mamba2Layer : public Layer {
     carve(nullptr, rows);
     return scratch_;
   }
-  void forward(const StepCtx& c, const float* in, float* out, const float* residual, uint8_t* scratch) override {
+  void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
+               uint8_t* scratch) override {
     const Buf b = carve(scratch, c.rows);
     const RowCtx rc{c.n_dev, c.rows, c.slots};
-    linear(c, in, H_, w1_, lp_, nullptr, n1_, H_, b.proj, n1_);  // x, z, b, c (mamba2.py:77-80)
-    linear(c, in, H_, dtw_, kF32, dtb_, nh_, H_, b.dtp, nh_);   // dt_proj, fp32 kept (mamba2.py:81)
+    const void* a1 = in_lp ? in_lp : in;
+    const int a1t = in_lp ? lp_ : kF32;
+    linear(c, a1, a1t, H_, w1_, lp_, nullptr, n1_, H_, b.proj, n1_);  // x, z, b, c (mamba2.py:77-80)
+    linear(c, in, kF32, H_, dtw_, kF32, dtb_, nh_, H_, b.dtp, nh_);   // dt_proj, fp32 kept (mamba2.py:81)
     Mamba2PreP pp{rc, b.proj, n1_, mi_, bc_, nh_, b.dtp, xc_, sxc_, bcs_, sbc_, ccs_, scc_,
                   wx_, bx_, wb_, bb_, wc_, bcv_, a_, b.xs, b.bs, b.cs, b.dt, b.dc};
     k_mamba2_pre<<<c.rows, kRowThreads, 0, c.s>>>(pp);
@@ -257,9 +263,9 @@ class Mamba2Layer : public Layer {
     sp.x = b.xs; sp.x_rs = mi_; sp.b = b.bs; sp.b_rs = bc_; sp.c = b.cs; sp.c_rs = bc_;
     sp.dt = b.dt; sp.dt_rs = nh_; sp.decay = b.dc; sp.dc_rs = nh_; sp.out = b.ys; sp.o_rs = mi_;
     ssm_cols(sp, c.rows, c.s);
-    Mamba2PostP po{rc, b.ys, b.xs, b.proj, n1_, mi_, hs_, dd_, nw_, b.A};
+    Mamba2PostP po{rc, b.ys, b.xs, b.proj, n1_, mi_, hs_, dd_, nw_, b.A, lp_};
     k_mamba2_post<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(po);
-    linear(c, b.A, mi_, out_, lp_, nullptr, H_, mi_, out, H_, kActNone, residual, H_);  // out_proj (mamba2.py:165)
+    linear(c, b.A, lp_, mi_, out_, lp_, nullptr, H_, mi_, out, H_, kActNone, residual, H_);  // out_proj (mamba2.py:165)
     B2E_CUDA(cudaGetLastError());
   }
 
@@ -315,7 +321,7 @@ __global__ void __launch_bounds__(kRowThreads) k_retnet_pre(const RetPreP p) {
 
 struct RetPostP {
   RowCtx rc;
-  const float* o; const float* proj; int H, nh, hs; float* A;
+  const float* o; const float* proj; int H, nh, hs; void* A; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_retnet_post(const RetPostP p) {
   const int r = blockIdx.x;
@@ -332,7 +338,7 @@ __global__ void __launch_bounds__(kRowThreads) k_retnet_post(const RetPostP p) {
   }
   __syncthreads();
   for (int e = threadIdx.x; e < p.H; e += blockDim.x)
-    p.A[size_t(r) * p.H + e] = siluf_(g[e]) * (o[e] * inv[e / p.hs]);  // silu(g) * out (retnet.py:169)
+    store_as(p.at, p.A, size_t(r) * p.H + e, siluf_(g[e]) * (o[e] * inv[e / p.hs]));  // silu(g) * out (retnet.py:169)
 }
 
 class RetNetLayer : public Layer {
@@ -372,10 +378,11 @@ class RetNetLayer : public Layer {
     carve(nullptr, rows);
     return scratch_;
   }
-  void forward(const StepCtx& c, const float* in, float* out, const float* residual, uint8_t* scratch) override {
+  void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
+               uint8_t* scratch) override {
     const Buf b = carve(scratch, c.rows);
     const RowCtx rc{c.n_dev, c.rows, c.slots};
-    linear(c, in, H_, w1_, lp_, nullptr, 4 * H_, H_, b.proj, 4 * H_);  // q, k, v, g (retnet.py:66-69)
+    linear(c, in_lp ? in_lp : in, in_lp ? lp_ : kF32, H_, w1_, lp_, nullptr, 4 * H_, H_, b.proj, 4 * H_);  // q, k, v, g (retnet.py:66-69)
     RetPreP pp{rc, b.proj, H_, nh_, hs_, pos_, spos_, sc_, ssc_, angle_, decay_,
                float(std::pow(double(hs_), -0.5)), b.kr, b.qs};
     k_retnet_pre<<<c.rows, kRowThreads, 0, c.s>>>(pp);
@@ -386,9 +393,9 @@ class RetNetLayer : public Layer {
     op.kv = b.kr; op.k_rs = H_; op.v = b.proj + 2 * H_; op.v_rs = 4 * H_;
     op.q = b.qs; op.q_rs = H_; op.out = b.o; op.o_rs = H_;
     outer_rows(op, c.rows, c.s);
-    RetPostP po{rc, b.o, b.proj, H_, nh_, hs_, b.A};
+    RetPostP po{rc, b.o, b.proj, H_, nh_, hs_, b.A, lp_};
     k_retnet_post<<<c.rows, kRowThreads, nh_ * sizeof(float), c.s>>>(po);
-    linear(c, b.A, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_);  // out_proj (retnet.py:170)
+    linear(c, b.A, lp_, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_);  // out_proj (retnet.py:170)
     B2E_CUDA(cudaGetLastError());
   }
 
@@ -425,7 +432,7 @@ __global__ void __launch_bounds__(kRowThreads) k_hawk_conv(const HawkConvP p) {
 struct RglruP {
   RowCtx rc;
   const float* gates; const float* xc; const float* proj; int H;
-  float* h; long long hs; const float* a; float* A;
+  float* h; long long hs; const float* a; void* A; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_rglru(const RglruP p) {
   const int r = blockIdx.x;
@@ -441,7 +448,7 @@ __global__ void __launch_bounds__(kRowThreads) k_rglru(const RglruP p) {
     const float mult = sqrtf(1.0f - at * at);                   // hawk.py:36
     const float hn = h[c] * at + mult * (it * x[c]);            // hawk.py:37
     h[c] = hn;
-    p.A[size_t(r) * p.H + c] = geluf_(gate[c]) * hn;            // out_proj(gate * h) (hawk.py:77,83-84)
+    store_as(p.at, p.A, size_t(r) * p.H + c, geluf_(gate[c]) * hn);  // out_proj(gate * h) (hawk.py:77,83-84)
   }
 }
 
@@ -482,10 +489,11 @@ class HawkLayer : public Layer {
     carve(nullptr, rows);
     return scratch_;
   }
-  void forward(const StepCtx& c, const float* in, float* out, const float* residual, uint8_t* scratch) override {
+  void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
+               uint8_t* scratch) override {
     const Buf b = carve(scratch, c.rows);
     const RowCtx rc{c.n_dev, c.rows, c.slots};
-    linear(c, in, H_, w1_, lp_, nullptr, 2 * H_, H_, b.proj, 2 * H_);  // gate_proj, recurrent_proj (hawk.py:77-78)
+    linear(c, in_lp ? in_lp : in, in_lp ? lp_ : kF32, H_, w1_, lp_, nullptr, 2 * H_, H_, b.proj, 2 * H_);  // gate_proj, recurrent_proj (hawk.py:77-78)
     HawkConvP cp{rc, b.proj, H_, conv_, sconv_, cw_, cb_, b.xc};
     k_hawk_conv<<<c.rows, kRowThreads, 0, c.s>>>(cp);
     // RG-LRU gates: two BlockLinears of 4 diagonal blocks, fp32 (hawk.py:31-32, modules.py:71-79)
@@ -501,9 +509,9 @@ class HawkLayer : public Layer {
     g.M_max = c.rows; g.M_dev = c.n_dev; g.N = bs_; g.K = bs_;
     g.lda = H_; g.ldw = bs_; g.ldc = 2 * H_;
     gemm(g, c.s);
-    RglruP rp{rc, b.gates, b.xc, b.proj, H_, h_, sh_, a_, b.A};
+    RglruP rp{rc, b.gates, b.xc, b.proj, H_, h_, sh_, a_, b.A, lp_};
     k_rglru<<<c.rows, kRowThreads, 0, c.s>>>(rp);
-    linear(c, b.A, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_);  // out_proj (hawk.py:84)
+    linear(c, b.A, lp_, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_);  // out_proj (hawk.py:84)
     B2E_CUDA(cudaGetLastError());
   }
 
@@ -561,7 +569,7 @@ struct SlstmPostP {
   const float* G; const float* t; int H, nbl;  // G row: [i | f | z | o] (4H), pre-activations
   float *hs_, *cs_, *ns_, *ms_; long long h_s, c_s, n_s, m_s;
   const float *gnw, *gnb, *mlnw;
-  float* x1; float* xn2;
+  float* x1; void* xn2; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) {
   const int r = blockIdx.x;
@@ -603,7 +611,7 @@ __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) 
   __syncthreads();
   group_stats(x1, 1, p.H, 1e-5f, gm, gr);  // mLSTM block LayerNorm (xlstm.py:182,202)
   for (int e = threadIdx.x; e < p.H; e += blockDim.x)
-    p.xn2[size_t(r) * p.H + e] = (x1[e] - gm[0]) * gr[0] * p.mlnw[e];
+    store_as(p.at, p.xn2, size_t(r) * p.H + e, (x1[e] - gm[0]) * gr[0] * p.mlnw[e]);
 }
 
 struct MlstmPreP {
@@ -693,7 +701,7 @@ __global__ void __launch_bounds__(kRowThreads) k_mlstm_gates(const MlstmGatesP p
 struct MlstmPostP {
   RowCtx rc;
   const float* num; const float* den; const float* xca; const float* proj; int mi, nh;
-  const float *gnw, *gnb, *skip; float* A;
+  const float *gnw, *gnb, *skip; void* A; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_mlstm_post(const MlstmPostP p) {
   const int r = blockIdx.x;
@@ -710,7 +718,7 @@ __global__ void __launch_bounds__(kRowThreads) k_mlstm_post(const MlstmPostP p) 
   for (int e = threadIdx.x; e < p.mi; e += blockDim.x) {
     const int g = e / hs;
     const float on = (o[e] - gm[g]) * gr[g] * p.gnw[e] + p.gnb[e];
-    p.A[size_t(r) * p.mi + e] = (on + p.skip[e] * xca[e]) * siluf_(xg[e]);  // xlstm.py:215-216
+    store_as(p.at, p.A, size_t(r) * p.mi + e, (on + p.skip[e] * xca[e]) * siluf_(xg[e]));  // xlstm.py:215-216
   }
 }
 
@@ -840,7 +848,8 @@ class XLSTMLayer : public Layer {
     carve(nullptr, rows);
     return scratch_;
   }
-  void forward(const StepCtx& c, const float* in, float* out, const float* residual, uint8_t* scratch) override {
+  void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
+               uint8_t* scratch) override {
     const Buf b = carve(scratch, c.rows);
     const RowCtx rc{c.n_dev, c.rows, c.slots};
     // ---- sLSTM block (xlstm.py:304-318)
@@ -862,13 +871,13 @@ class XLSTMLayer : public Layer {
       gp.lda = 2 * H_; gp.ldw = 2 * bs_; gp.ldc = 4 * H_;
       gemm(gp, c.s);
     }
-    SlstmPostP so{rc, b.G, in, H_, nbl_, sh_, sc_, sn_, sm_, ssh_, ssc_, ssn_, ssm_, sgnw_, sgnb_, mlnw_, b.x1, b.xn2};
+    SlstmPostP so{rc, b.G, in, H_, nbl_, sh_, sc_, sn_, sm_, ssh_, ssc_, ssn_, ssm_, sgnw_, sgnb_, mlnw_, b.x1, b.xn2, lp_};
     k_slstm_post<<<c.rows, kRowThreads, 2 * H_ * sizeof(float), c.s>>>(so);
     // ---- mLSTM block (xlstm.py:198-219)
-    linear(c, b.xn2, H_, mw1_, lp_, nullptr, 2 * mi_, H_, b.proj, 2 * mi_);  // x_proj, gate_proj
+    linear(c, b.xn2, lp_, H_, mw1_, lp_, nullptr, 2 * mi_, H_, b.proj, 2 * mi_);  // x_proj, gate_proj
     MlstmPreP mp{rc, b.proj, mi_, mconv_, smconv_, mcw_, mcb_, wq_, wk_, wv_, b.xca, b.qkv};
     k_mlstm_pre<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(mp);
-    linear(c, b.qkv, 3 * mi_, gw_, kF32, gb_, 2 * nh_, 3 * mi_, b.ifp, 2 * nh_);  // igate/fgate, fp32 kept
+    linear(c, b.qkv, kF32, 3 * mi_, gw_, kF32, gb_, 2 * nh_, 3 * mi_, b.ifp, 2 * nh_);  // igate/fgate, fp32 kept
     MlstmGatesP gp{rc, b.ifp, b.qkv, mi_, nh_, hs_, n_, sn2_, m_, sm2_, b.g2, b.den};
     k_mlstm_gates<<<c.rows, kRowThreads, 0, c.s>>>(gp);
     OuterRowsParams op;
@@ -881,9 +890,9 @@ class XLSTMLayer : public Layer {
     op.q = b.qkv; op.q_rs = 3 * mi_;
     op.out = b.num; op.o_rs = mi_;
     outer_rows(op, c.rows, c.s);
-    MlstmPostP pp{rc, b.num, b.den, b.xca, b.proj, mi_, nh_, ongw_, ongb_, skip_, b.A};
+    MlstmPostP pp{rc, b.num, b.den, b.xca, b.proj, mi_, nh_, ongw_, ongb_, skip_, b.A, lp_};
     k_mlstm_post<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(pp);
-    linear(c, b.A, mi_, down_, lp_, nullptr, H_, mi_, b.x2, H_, kActNone, b.x1, H_);  // proj_down + skip
+    linear(c, b.A, lp_, mi_, down_, lp_, nullptr, H_, mi_, b.x2, H_, kActNone, b.x1, H_);  // proj_down + skip
     XFinalP fp{rc, b.x2, H_, fnw_, residual, out};
     k_xlstm_final<<<c.rows, kRowThreads, H_ * sizeof(float), c.s>>>(fp);
     B2E_CUDA(cudaGetLastError());
@@ -917,8 +926,8 @@ std::unique_ptr<Layer> Layer::make(int kind, const Dims& d, int lp) {
   throw Error(kErrInvalid, "unknown layer kind " + std::to_string(kind));
 }
 
-void rmsnorm_rows(const StepCtx& c, const float* x, const float* w, float eps, int H, float* out) {
-  RmsP p{{c.n_dev, c.rows, c.slots}, x, w, out, H, eps};
+void rmsnorm_rows(const StepCtx& c, const float* x, const float* w, float eps, int H, float* out, void* out_lp) {
+  RmsP p{{c.n_dev, c.rows, c.slots}, x, w, out, H, eps, out_lp, c.lp};
   k_rmsnorm<<<c.rows, kRowThreads, 0, c.s>>>(p);
   B2E_CUDA(cudaGetLastError());
 }
@@ -930,8 +939,8 @@ void output_proj_rows(const StepCtx& c, const float* x, const float* w, const fl
   B2E_CUDA(cudaGetLastError());
 }
 
-void linear(const StepCtx& c, const float* A, int lda, const void* W, int wt, const void* bias, int N, int K,
-            float* C, int ldc, int act, const float* R, int ldr) {
+void linear(const StepCtx& c, const void* A, int at, int lda, const void* W, int wt, const void* bias, int N, int K,
+            float* C, int ldc, int act, const float* R, int ldr, void* C_lp, int ldc_lp) {
   GemmParams p;
   p.groups = 1;
   p.g[0].A = A;
@@ -939,6 +948,9 @@ void linear(const StepCtx& c, const float* A, int lda, const void* W, int wt, co
   p.g[0].bias = bias;
   p.g[0].C = C;
   p.g[0].R = R;
+  p.g[0].C_lp = C_lp;
+  p.ldc_lp = ldc_lp;
+  p.err = c.err;
   p.M_max = c.rows;
   p.M_dev = c.n_dev;
   p.N = N;
@@ -947,7 +959,7 @@ void linear(const StepCtx& c, const float* A, int lda, const void* W, int wt, co
   p.ldw = K;
   p.ldc = ldc;
   p.ldr = ldr;
-  p.a_type = kF32;
+  p.a_type = at;
   p.w_type = wt;
   p.bias_type = wt;  // CastLinear stores its bias in the weight's type (example_model.py:85-88)
   p.round_out = wt != kF32;

@@ -34,6 +34,7 @@ struct StepCtx {
   const int* n_dev = nullptr;
   const int* slots = nullptr;  // row -> state slot (device)
   int lp = kF32;              // CastLinear storage type; kF32 = the fp32 path
+  int* err = nullptr;         // device error word (bounded waits in tensor-core GEMMs)
 };
 
 class Layer {
@@ -46,8 +47,10 @@ class Layer {
   virtual void resolve(const WeightPack& pack, const StateArena& a) = 0;
   virtual size_t scratch_bytes(int rows) const = 0;
   // out[r] = (residual ? residual[r] : 0) + layer(in[r]) for the live rows; in,
-  // out and residual are [rows][H] f32 and out may alias residual.
-  virtual void forward(const StepCtx& c, const float* in, float* out, const float* residual,
+  // out and residual are [rows][H] f32 and out may alias residual. in_lp, when
+  // not null, is `in` already rounded to the CastLinear type (what CastLinear
+  // feeds its matmul), so the projections can run on the tensor cores.
+  virtual void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
                        uint8_t* scratch) = 0;
 
   static std::unique_ptr<Layer> make(int kind, const Dims& d, int lp);
@@ -55,14 +58,17 @@ class Layer {
 
 // ----- Block / Tower glue (model/inference_model.py:55-95, 117, 142) -----
 
-// out = x * rsqrt(mean(x^2) + eps) * w   (nn.RMSNorm)
-void rmsnorm_rows(const StepCtx& c, const float* x, const float* w, float eps, int H, float* out);
+// out = x * rsqrt(mean(x^2) + eps) * w   (nn.RMSNorm); out (f32) and/or out_lp
+// (the same values in the CastLinear type c.lp) may be null.
+void rmsnorm_rows(const StepCtx& c, const float* x, const float* w, float eps, int H, float* out, void* out_lp);
 // preds[r*ld + col] = dot(x[r], w) + b[0]     (output_proj, fp32 kept)
 void output_proj_rows(const StepCtx& c, const float* x, const float* w, const float* b, int H, float* preds,
                       int ld, int col);
-// Enqueue one nn.Linear / CastLinear application (see gemm.cuh).
-void linear(const StepCtx& c, const float* A, int lda, const void* W, int wt, const void* bias, int N, int K,
-            float* C, int ldc, int act = 0, const float* R = nullptr, int ldr = 0);
+// Enqueue one nn.Linear / CastLinear application (see gemm.cuh). A has type
+// `at` (f32, or already the weight's low type); C_lp receives a low-type copy.
+void linear(const StepCtx& c, const void* A, int at, int lda, const void* W, int wt, const void* bias, int N, int K,
+            float* C, int ldc, int act = 0, const float* R = nullptr, int ldr = 0, void* C_lp = nullptr,
+            int ldc_lp = 0);
 // Set *n_dev = n on the stream (tiny kernel; graph-capturable).
 void set_rows(int* n_dev, int n, cudaStream_t s);
 

@@ -60,9 +60,9 @@ def split_blob(blob: bytes, layout) -> List[np.ndarray]:
 def join_leaves(leaves: Sequence[np.ndarray], layout) -> bytes:
     parts = []
     for a, (shape, dt) in zip(leaves, layout, strict=True):
-        a = np.ascontiguousarray(a, dtype=dt)
+        a = np.asarray(a, dtype=dt)
         assert a.shape == tuple(shape), (a.shape, shape)
-        parts.append(a.tobytes())
+        parts.append(np.ascontiguousarray(a).tobytes())
     return b"".join(parts)
 
 

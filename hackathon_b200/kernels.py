@@ -105,3 +105,31 @@ def mamba2_step(ssm, x, b, c, dt, decay, mask):
         _lib.check(_lib.lib().b2e_mamba2_step(_ptr(ssm), _ptr(x), _ptr(b), _ptr(c), _ptr(dt), _ptr(decay),
                                               _ptr(m), bs, n, sh, sc, _ptr(out), _stream(dev)))
     return out
+
+
+_TORCH_DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def cast_linear(x, weight, bias=None, relu: bool = False, err=None):
+    """CastLinear.forward (example_model.py:92-95) / nn.Linear on the GPU.
+
+    ``weight`` (out, in) is float32, bfloat16 or float16. With a low-precision
+    weight, x is rounded to its type, products accumulate in float32, the bias
+    (same type as the weight) is added and the result is rounded to the weight's
+    type before widening: exactly CastLinear. Returns a new float32 tensor.
+    ``err`` is an optional int32 CUDA tensor of one element that receives an error
+    code if the tensor-core kernel times out; without it the tensor-core kernel
+    is not used.
+    """
+    assert weight.is_cuda and weight.dim() == 2 and weight.is_contiguous()
+    wt = _TORCH_DTYPES[weight.dtype]
+    assert x.dtype in (torch.float32, weight.dtype), f"x must be fp32 or {weight.dtype}, got {x.dtype}"
+    assert x.device == weight.device and x.dim() == 2 and x.shape[1] == weight.shape[1]
+    x = x.contiguous()
+    if bias is not None:
+        assert bias.dtype == weight.dtype and bias.shape == (weight.shape[0],)
+        bias = bias.contiguous()
+    y = torch.empty(x.shape[0], weight.shape[0], dtype=torch.float32, device=x.device)
+    _lib.check(_lib.lib().b2e_linear(_ptr(x), _TORCH_DTYPES[x.dtype], x.shape[0], x.shape[1], _ptr(weight), wt,
+                                     _ptr(bias), weight.shape[0], int(relu), _ptr(y), _ptr(err), _stream(x.device)))
+    return y

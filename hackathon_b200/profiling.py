@@ -1,0 +1,117 @@
+"""Profiling helpers: single-kernel cases for ncu, and summaries of its output.
+
+    python -m hackathon_b200.profiling cell --kind mamba2 --rows 4096 --heads 8 --sh 64 --sk 128
+        run one state-step kernel `--reps` times on a dense state (for ncu -k)
+    python -m hackathon_b200.profiling launches <launch list csv>
+        per-kernel launches, total time and share of an ncu launch list
+    python -m hackathon_b200.profiling metrics <raw csv from ncu -i ... --page raw --csv>
+        the DRAM/tensor/occupancy counters used in the roofline, per kernel
+"""
+
+from __future__ import annotations
+
+import argparse
+import collections
+import csv
+import sys
+
+SCALE = {"nsecond": 1e-3, "ns": 1e-3, "usecond": 1.0, "us": 1.0, "msecond": 1e3, "ms": 1e3}
+METRICS = ("gpu__time_duration.sum", "dram__bytes_read.sum", "dram__bytes_write.sum",
+           "gpu__dram_throughput.avg.pct_of_peak_sustained_elapsed", "dram__throughput.avg.pct_of_peak_sustained_elapsed",
+           "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active", "sm__warps_active.avg.pct_of_peak_sustained_active",
+           "launch__registers_per_thread", "launch__grid_size", "launch__block_size",
+           "sm__throughput.avg.pct_of_peak_sustained_elapsed")
+
+
+def _short(name: str) -> str:
+    return name.split("(")[0].replace("(anonymous namespace)::", "").replace("void ", "")
+
+
+def launches(path: str) -> None:
+    rows = list(csv.reader(open(path)))
+    hdr, agg = None, collections.defaultdict(lambda: [0, 0.0])
+    for r in rows:
+        if r and r[0] == "ID":
+            hdr = r
+            continue
+        if not hdr or len(r) != len(hdr):
+            continue
+        d = dict(zip(hdr, r))
+        if d["Metric Name"] != "gpu__time_duration.sum":
+            continue
+        us = float(d["Metric Value"].replace(",", "")) * SCALE.get(d["Metric Unit"], 1e-3)
+        agg[_short(d["Kernel Name"])][0] += 1
+        agg[_short(d["Kernel Name"])][1] += us
+    total = sum(v[1] for v in agg.values())
+    print(f"{'kernel':52s} {'launches':>8s} {'total us':>10s} {'share':>6s}")
+    for k, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
+        print(f"{k:52s} {n:8d} {t:10.1f} {100 * t / total:5.1f}%")
+    print(f"{'total':52s} {sum(v[0] for v in agg.values()):8d} {total:10.1f}")
+
+
+def metrics(path: str) -> None:
+    rows = list(csv.reader(open(path)))
+    hdr = rows[0]
+    units = rows[1] if len(rows) > 1 else []
+    for r in rows[2:]:
+        d = dict(zip(hdr, r))
+        print(_short(d.get("Kernel Name", "?")))
+        for m in METRICS:
+            if m in d:
+                u = units[hdr.index(m)] if units else ""
+                print(f"  {m} = {d[m]} {u}")
+
+
+def cell(kind: str, rows: int, heads: int, sh: int, sk: int, reps: int) -> None:
+    import torch
+
+    from . import kernels as K
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    state = torch.randn(rows, heads, sh, sk, device=dev, generator=g)
+    if kind == "mamba2":
+        args = (torch.randn(rows, heads, sh, device=dev, generator=g), torch.randn(rows, sk, device=dev, generator=g),
+                torch.randn(rows, sk, device=dev, generator=g), torch.rand(rows, heads, device=dev, generator=g),
+                torch.rand(rows, heads, device=dev, generator=g))
+        fn = K.mamba2_step
+    elif kind == "mlstm":
+        args = (torch.randn(rows, heads, sh, device=dev, generator=g), torch.randn(rows, heads, sh, device=dev, generator=g),
+                torch.randn(rows, heads, sk, device=dev, generator=g), torch.rand(rows, heads, device=dev, generator=g),
+                torch.rand(rows, heads, device=dev, generator=g))
+        fn = K.mlstm_step
+    elif kind == "retnet":
+        args = (torch.randn(rows, heads, sh, device=dev, generator=g), torch.randn(rows, heads, sk, device=dev, generator=g),
+                torch.randn(rows, heads, sh, device=dev, generator=g), torch.rand(heads, device=dev, generator=g))
+        fn = K.retnet_step
+    else:
+        raise SystemExit(f"unknown kind {kind}")
+    for _ in range(reps):
+        fn(state, *args, None)
+    torch.cuda.synchronize()
+    print(f"{kind} rows={rows} heads={heads} sh={sh} sk={sk}: {reps} launches, state {state.numel() * 4 / 1e9:.2f} GB")
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    c = sub.add_parser("cell")
+    c.add_argument("--kind", required=True)
+    c.add_argument("--rows", type=int, default=4096)
+    c.add_argument("--heads", type=int, default=8)
+    c.add_argument("--sh", type=int, default=64)
+    c.add_argument("--sk", type=int, default=128)
+    c.add_argument("--reps", type=int, default=4)
+    sub.add_parser("launches").add_argument("csv")
+    sub.add_parser("metrics").add_argument("csv")
+    a = ap.parse_args(argv)
+    if a.cmd == "cell":
+        cell(a.kind, a.rows, a.heads, a.sh, a.sk, a.reps)
+    elif a.cmd == "launches":
+        launches(a.csv)
+    else:
+        metrics(a.csv)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])

@@ -19,6 +19,7 @@
  *   b2e_mlstm_step / b2e_retnet_step / b2e_mamba2_step
  *                       model/kernels.py mlstm_step / retnet_step / mamba2_step
  *                       (model/kernels.py:346-401)
+ *   b2e_linear          CastLinear.forward / nn.Linear (example_model.py:92-95)
  *   b2e_layer_*         one layer's forward(x, state, mask) with its own state
  *                       table (model/xlstm.py:355, model/mamba2.py:62,
  *                       model/retnet.py:38, model/hawk.py:60)
@@ -130,6 +131,17 @@ B2E_API int b2e_retnet_step(float* state, const float* k_rope, const float* v, c
 B2E_API int b2e_mamba2_step(float* ssm, const float* x, const float* b, const float* c, const float* dt,
                     const float* decay, const uint8_t* mask, int32_t batch, int32_t heads, int32_t size_h,
                     int32_t size_c, float* out, void* stream);
+
+/* ---- one projection: CastLinear.forward / nn.Linear ----
+ * y[m, n] = act(round(sum_k x[m, k] * w[n, k] + bias[n])) in float32, where with
+ * a low-precision weight (B2E_DTYPE_BF16/F16) x is rounded to that type first
+ * and `round` rounds the result to it, as CastLinear does; with an f32 weight
+ * there is no rounding. x has type x_dtype (f32 or the weight's type), bias the
+ * weight's type; act 0 = none, 1 = ReLU. Device pointers; d_err is a device int
+ * that receives an error code if the tensor-core kernel times out (NULL keeps
+ * the problem off the tensor-core kernel). */
+B2E_API int b2e_linear(const void* x, int32_t x_dtype, int32_t m, int32_t k, const void* w, int32_t w_dtype,
+                       const void* bias, int32_t n, int32_t act, float* y, int32_t* d_err, void* stream);
 
 /* ---- one recurrent layer with its own state table ----
  * Weights are keyed like that layer's own state_dict() (no prefix). */
