@@ -48,6 +48,7 @@ struct TcEpi {
   int lp;  // kBF16 or kF16: operand type and CastLinear rounding type
   int round_out, act;
   int* err;
+  int vec;  // every row start of bias/R/C/C_lp is 16-byte (f32) / 8-byte (low type) aligned
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -123,6 +124,22 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// 32 consecutive accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(
@@ -134,6 +151,37 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// 4 consecutive values of a bias vector of type t (f32, bf16 or f16), 16/8-byte aligned.
+__device__ __forceinline__ float4 load4(int t, const void* p, int i) {
+  if (t == kF32) return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+  const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p) + i);
+  float4 r;
+  if (t == kBF16) {
+    r.x = __uint_as_float(raw.x << 16); r.y = __uint_as_float(raw.x & 0xffff0000u);
+    r.z = __uint_as_float(raw.y << 16); r.w = __uint_as_float(raw.y & 0xffff0000u);
+  } else {
+    const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
+    const float2 fa = __half22float2(a), fb = __half22float2(b);
+    r = make_float4(fa.x, fa.y, fb.x, fb.y);
+  }
+  return r;
+}
+
+// Store 4 floats as the low type (8 bytes, aligned).
+__device__ __forceinline__ void store4_lp(int t, void* p, size_t i, float4 x) {
+  uint2 raw;
+  if (t == kBF16) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(x.x, x.y), b = __floats2bfloat162_rn(x.z, x.w);
+    raw.x = *reinterpret_cast<const uint32_t*>(&a);
+    raw.y = *reinterpret_cast<const uint32_t*>(&b);
+  } else {
+    const __half2 a = __floats2half2_rn(x.x, x.y), b = __floats2half2_rn(x.z, x.w);
+    raw.x = *reinterpret_cast<const uint32_t*>(&a);
+    raw.y = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + i) = raw;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -232,22 +280,48 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int q = warp & 3;
       const int m = m0 + q * 32 + lane;
       const bool row_ok = m < M;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = 0; c0 < BN; c0 += 32) {
         if (n0 + c0 >= e.N) break;  // warp-uniform
-        float v[16];
-        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
+        float v[32];
+        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
         if (!row_ok) continue;
+        const int nb = n0 + c0;
+        if (e.vec && nb + 32 <= e.N) {
+          // 32 consecutive columns of one row: 16-byte loads and stores
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = n0 + c0 + j;
-          if (n >= e.N) break;
-          float x = v[j];
-          if (e.bias) x += load_as(e.bias_type, e.bias, n);
-          if (e.round_out) x = round_to(e.lp, x);
-          if (e.act == kActRelu) x = fmaxf(x, 0.0f);
-          if (e.R) x += e.R[size_t(m) * e.ldr + n];
-          if (e.C) e.C[size_t(m) * e.ldc + n] = x;
-          if (e.C_lp) store_as(e.lp, e.C_lp, size_t(m) * e.ldc_lp + n, x);
+          for (int j = 0; j < 32; j += 4) {
+            float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            if (e.bias) {
+              const float4 b = load4(e.bias_type, e.bias, nb + j);
+              x.x += b.x; x.y += b.y; x.z += b.z; x.w += b.w;
+            }
+            if (e.round_out) {
+              x.x = round_to(e.lp, x.x); x.y = round_to(e.lp, x.y);
+              x.z = round_to(e.lp, x.z); x.w = round_to(e.lp, x.w);
+            }
+            if (e.act == kActRelu) {
+              x.x = fmaxf(x.x, 0.f); x.y = fmaxf(x.y, 0.f); x.z = fmaxf(x.z, 0.f); x.w = fmaxf(x.w, 0.f);
+            }
+            if (e.R) {
+              const float4 r = *reinterpret_cast<const float4*>(e.R + size_t(m) * e.ldr + nb + j);
+              x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
+            }
+            if (e.C) *reinterpret_cast<float4*>(e.C + size_t(m) * e.ldc + nb + j) = x;
+            if (e.C_lp) store4_lp(e.lp, e.C_lp, size_t(m) * e.ldc_lp + nb + j, x);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = nb + j;
+            if (n >= e.N) continue;
+            float x = v[j];
+            if (e.bias) x += load_as(e.bias_type, e.bias, n);
+            if (e.round_out) x = round_to(e.lp, x);
+            if (e.act == kActRelu) x = fmaxf(x, 0.0f);
+            if (e.R) x += e.R[size_t(m) * e.ldr + n];
+            if (e.C) e.C[size_t(m) * e.ldc + n] = x;
+            if (e.C_lp) store_as(e.lp, e.C_lp, size_t(m) * e.ldc_lp + n, x);
+          }
         }
       }
     }
@@ -308,8 +382,12 @@ void gemm_tc(const GemmParams& p, cudaStream_t s) {
   CUtensorMap ta, tb;
   make_map(&ta, p.g[0].A, p.w_type, uint64_t(p.K), uint64_t(p.M_max), uint64_t(p.lda), BM);
   make_map(&tb, p.g[0].W, p.w_type, uint64_t(p.K), uint64_t(p.N), uint64_t(p.ldw), BN);
-  TcEpi e{p.g[0].bias, p.bias_type, p.g[0].C, p.ldc, p.g[0].C_lp, p.ldc_lp, p.g[0].R, p.ldr, p.M_max, p.M_dev,
-          p.N, p.K, p.w_type, p.round_out, p.act, p.err};
+  const GemmGroup& g = p.g[0];
+  const bool vec = p.N % 4 == 0 && (!g.bias || (reinterpret_cast<uintptr_t>(g.bias) % 16 == 0)) &&
+                   (!g.C || (aligned16(g.C) && p.ldc % 4 == 0)) && (!g.R || (aligned16(g.R) && p.ldr % 4 == 0)) &&
+                   (!g.C_lp || (reinterpret_cast<uintptr_t>(g.C_lp) % 8 == 0 && p.ldc_lp % 4 == 0));
+  TcEpi e{g.bias, p.bias_type, g.C, p.ldc, g.C_lp, p.ldc_lp, g.R, p.ldr, p.M_max, p.M_dev,
+          p.N, p.K, p.w_type, p.round_out, p.act, p.err, vec ? 1 : 0};
   dim3 grid(ceil_div(p.N, BN), ceil_div(p.M_max, BM));
   gemm_tc_kernel<<<grid, THREADS, SMEM, s>>>(ta, tb, e);
   B2E_CUDA(cudaGetLastError());

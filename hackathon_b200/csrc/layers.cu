@@ -95,19 +95,35 @@ struct RmsP {
   RowCtx rc;
   const float* x; const float* w; float* out; int H; float eps; void* out_lp; int lp;
 };
-__global__ void __launch_bounds__(kRowThreads) k_rmsnorm(const RmsP p) {
-  const int r = blockIdx.x;
+// One warp per row: H is a multiple of 4 (Dims::validate), so each lane moves
+// 16-byte vectors; 8 rows per 256-thread CTA.
+constexpr int kRowsPerCta = 8;
+
+__global__ void __launch_bounds__(256) k_rmsnorm(const RmsP p) {
+  const int r = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (!row_live(p.rc, r)) return;
-  __shared__ float red[32];
-  const float* x = p.x + size_t(r) * p.H;
+  const float4* x = reinterpret_cast<const float4*>(p.x + size_t(r) * p.H);
+  const int n4 = p.H >> 2;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < p.H; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
-  ss = block_sum(ss, red);
+  for (int i = lane; i < n4; i += 32) {
+    const float4 v = x[i];
+    ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+  }
+  ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(ss / float(p.H) + p.eps);
-  for (int i = threadIdx.x; i < p.H; i += blockDim.x) {
-    const float v = x[i] * inv * (p.w ? p.w[i] : 1.0f);
-    if (p.out) p.out[size_t(r) * p.H + i] = v;
-    if (p.out_lp) store_as(p.lp, p.out_lp, size_t(r) * p.H + i, v);
+  for (int i = lane; i < n4; i += 32) {
+    const float4 v = x[i];
+    const float4 w = p.w ? reinterpret_cast<const float4*>(p.w)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+    const float4 o = make_float4(v.x * inv * w.x, v.y * inv * w.y, v.z * inv * w.z, v.w * inv * w.w);
+    if (p.out) reinterpret_cast<float4*>(p.out + size_t(r) * p.H)[i] = o;
+    if (p.out_lp) {
+      const size_t base = size_t(r) * p.H + size_t(i) * 4;
+      store_as(p.lp, p.out_lp, base + 0, o.x);
+      store_as(p.lp, p.out_lp, base + 1, o.y);
+      store_as(p.lp, p.out_lp, base + 2, o.z);
+      store_as(p.lp, p.out_lp, base + 3, o.w);
+    }
   }
 }
 
@@ -115,15 +131,19 @@ struct OutP {
   RowCtx rc;
   const float* x; const float* w; const float* b; int H; float* preds; int ld; int col;
 };
-__global__ void __launch_bounds__(kRowThreads) k_output_proj(const OutP p) {
-  const int r = blockIdx.x;
+__global__ void __launch_bounds__(256) k_output_proj(const OutP p) {
+  const int r = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (!row_live(p.rc, r)) return;
-  __shared__ float red[32];
-  const float* x = p.x + size_t(r) * p.H;
+  const float4* x = reinterpret_cast<const float4*>(p.x + size_t(r) * p.H);
+  const float4* w = reinterpret_cast<const float4*>(p.w);
   float s = 0.f;
-  for (int i = threadIdx.x; i < p.H; i += blockDim.x) s = fmaf(x[i], p.w[i], s);
-  s = block_sum(s, red);
-  if (threadIdx.x == 0) p.preds[size_t(r) * p.ld + p.col] = s + p.b[0];
+  for (int i = lane; i < (p.H >> 2); i += 32) {
+    const float4 a = x[i], b = w[i];
+    s = fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, s))));
+  }
+  s = warp_sum(s);
+  if (lane == 0) p.preds[size_t(r) * p.ld + p.col] = s + p.b[0];
 }
 
 __global__ void k_set_rows(int* n, int v) { *n = v; }
@@ -928,14 +948,14 @@ std::unique_ptr<Layer> Layer::make(int kind, const Dims& d, int lp) {
 
 void rmsnorm_rows(const StepCtx& c, const float* x, const float* w, float eps, int H, float* out, void* out_lp) {
   RmsP p{{c.n_dev, c.rows, c.slots}, x, w, out, H, eps, out_lp, c.lp};
-  k_rmsnorm<<<c.rows, kRowThreads, 0, c.s>>>(p);
+  k_rmsnorm<<<ceil_div(c.rows, kRowsPerCta), 256, 0, c.s>>>(p);
   B2E_CUDA(cudaGetLastError());
 }
 
 void output_proj_rows(const StepCtx& c, const float* x, const float* w, const float* b, int H, float* preds, int ld,
                       int col) {
   OutP p{{c.n_dev, c.rows, c.slots}, x, w, b, H, preds, ld, col};
-  k_output_proj<<<c.rows, kRowThreads, 0, c.s>>>(p);
+  k_output_proj<<<ceil_div(c.rows, kRowsPerCta), 256, 0, c.s>>>(p);
   B2E_CUDA(cudaGetLastError());
 }
 

@@ -49,6 +49,9 @@ def test_cells_match_reference_fixtures():
     ("mlstm", (8, 512, 512), 3), ("mlstm", (8, 64, 64), 64), ("retnet", (8, 256, 256), 3),
     ("retnet", (8, 32, 32), 64), ("mamba2", (64, 64, 128), 3), ("mamba2", (8, 64, 128), 64),
     ("mamba2", (8, 64, 64), 33),
+    # ragged head sizes through the vectorised kernels
+    ("mamba2", (3, 17, 64), 5), ("mamba2", (2, 300, 32), 3), ("mamba2", (4, 7, 128), 4),
+    ("mlstm", (3, 40, 64), 5), ("mlstm", (2, 33, 128), 3), ("retnet", (4, 16, 32), 7),
 ])
 def test_cells_model_shapes_match_oracle(tag, dims, batch):
     """The shapes the model runs at (default and reduced dims), against the oracle."""
