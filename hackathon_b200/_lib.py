@@ -38,7 +38,8 @@ class ModelConfigC(C.Structure):
 
 class EngineOptionsC(C.Structure):
     _fields_ = [("device", C.c_int32), ("linear_dtype", C.c_int32), ("capacity", C.c_int32),
-                ("max_batch", C.c_int32), ("use_graphs", C.c_int32)]
+                ("max_batch", C.c_int32), ("use_graphs", C.c_int32), ("lanes", C.c_int32),
+                ("lane_min_rows", C.c_int32)]
 
 
 class TensorC(C.Structure):

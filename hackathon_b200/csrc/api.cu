@@ -73,6 +73,8 @@ EngineOptions to_opts(const b2e_engine_options* o) {
   e.capacity = o->capacity;
   e.max_batch = o->max_batch;
   e.graphs = o->use_graphs != 0;
+  if (o->lanes > 0) e.lanes = o->lanes;
+  if (o->lane_min_rows > 0) e.lane_min_rows = o->lane_min_rows;
   return e;
 }
 

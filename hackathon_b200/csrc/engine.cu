@@ -19,6 +19,12 @@ namespace b2e {
 
 namespace {
 
+// Live rows of each lane: lane l owns rows [l*per, (l+1)*per) of the step.
+__global__ void k_split_rows(const int* n_dev, int* n_lane, int lanes, int per) {
+  const int l = threadIdx.x;
+  if (l < lanes) n_lane[l] = max(0, min(per, *n_dev - l * per));
+}
+
 __global__ void k_validate(const int* slots, int n, int capacity, int* n_dev, int* err) {
   __shared__ int bad;
   if (threadIdx.x == 0) bad = 0;
@@ -86,6 +92,13 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
       bl.f2w = pack_.ptr(bl.o_f2w); bl.f2b = pack_.ptr(bl.o_f2b);
       bl.layer->resolve(pack_, arena_);
     }
+  }
+  B2E_CHECK(o.lanes >= 1 && o.lanes <= 8, kErrInvalid, "lanes must be in 1..8");
+  chains_.resize(size_t(o.lanes) * 4);
+  for (size_t ci = 0; ci < chains_.size(); ++ci) {
+    Chain& ch = chains_[ci];
+    const Tower& tw = towers_[ci % 4];
+    // every chain can carry a whole step (a small bucket runs as one lane)
     const size_t R = o.max_batch;
     size_t scratch = 0;
     for (auto& bl : tw.blocks) scratch = std::max(scratch, bl.layer->scratch_bytes(o.max_batch));
@@ -98,13 +111,13 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
     uint8_t* base = nullptr;
     B2E_CUDA(cudaMalloc(&base, glue + scratch + 256));
     Carver g{base};
-    tw.x = g.take<float>(R * H);
-    tw.t = g.take<float>(R * H);
-    tw.tl = g.take<float>(R * H);
-    tw.u = g.take<float>(R * P);
-    tw.scratch = base + glue;
-    B2E_CUDA(cudaStreamCreateWithFlags(&tw.s, cudaStreamNonBlocking));
-    B2E_CUDA(cudaEventCreateWithFlags(&tw.done, cudaEventDisableTiming));
+    ch.x = g.take<float>(R * H);
+    ch.t = g.take<float>(R * H);
+    ch.tl = g.take<float>(R * H);
+    ch.u = g.take<float>(R * P);
+    ch.scratch = base + glue;
+    B2E_CUDA(cudaStreamCreateWithFlags(&ch.s, cudaStreamNonBlocking));
+    B2E_CUDA(cudaEventCreateWithFlags(&ch.done, cudaEventDisableTiming));
   }
   ow_ = pack_.ptr<float>(o_ow_);
   ob_ = pack_.ptr<float>(o_ob_);
@@ -113,7 +126,7 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   const size_t R = o.max_batch;
   feats_off_ = (16 + 4 * R + 255) & ~size_t(255);
   preds_off_ = (feats_off_ + 4 * R * F + 255) & ~size_t(255);
-  const size_t io = preds_off_ + 16 * R + 64;
+  const size_t io = preds_off_ + 16 * R + 128;
   B2E_CUDA(cudaMalloc(&d_io_, io));
   B2E_CUDA(cudaMallocHost(&h_io_, io));
   d_n_ = reinterpret_cast<int*>(d_io_);
@@ -121,6 +134,7 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   d_feats_ = reinterpret_cast<float*>(d_io_ + feats_off_);
   d_preds_ = reinterpret_cast<float*>(d_io_ + preds_off_);
   d_err_ = reinterpret_cast<int*>(d_io_ + preds_off_ + 16 * R);
+  d_nl_ = d_err_ + 4;
   B2E_CUDA(cudaMemset(d_io_, 0, io));
   B2E_CUDA(cudaStreamCreateWithFlags(&s0_, cudaStreamNonBlocking));
   B2E_CUDA(cudaEventCreateWithFlags(&fork_, cudaEventDisableTiming));
@@ -134,10 +148,10 @@ Engine::~Engine() {
   cudaSetDevice(opt_.device);
   if (s0_) cudaStreamSynchronize(s0_);
   for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
-  for (auto& tw : towers_) {
-    if (tw.s) cudaStreamDestroy(tw.s);
-    if (tw.done) cudaEventDestroy(tw.done);
-    if (tw.x) cudaFree(tw.x);
+  for (auto& ch : chains_) {
+    if (ch.s) cudaStreamDestroy(ch.s);
+    if (ch.done) cudaEventDestroy(ch.done);
+    if (ch.x) cudaFree(ch.x);
   }
   if (fork_) cudaEventDestroy(fork_);
   if (s0_) cudaStreamDestroy(s0_);
@@ -151,45 +165,55 @@ int Engine::bucket(int n) const {
   return std::min(b, opt_.max_batch);
 }
 
-void Engine::tower_forward(Tower& tw, int idx, const StepCtx& c) {
+int Engine::lanes_for(int rows) const {
+  return (opt_.lanes > 1 && rows >= opt_.lane_min_rows) ? opt_.lanes : 1;
+}
+
+void Engine::tower_forward(const Tower& tw, Chain& ch, int idx, const StepCtx& c, const float* feats, float* preds) {
   const int H = d_.H, P = d_.P, F = d_.F, lp = opt_.lp;
   const bool low = lp != kF32;
   // GEMM inputs are written in the CastLinear type (the cast CastLinear applies,
   // example_model.py:93-94): u and tl hold bf16/f16 values when `low`.
-  float* u32 = low ? nullptr : tw.u;
-  void* ulp = low ? static_cast<void*>(tw.u) : nullptr;
+  float* u32 = low ? nullptr : ch.u;
+  void* ulp = low ? static_cast<void*>(ch.u) : nullptr;
   const float eps = 1.1920928955078125e-07f;  // nn.RMSNorm(eps=None) in float32
   // input_up, ReLU, input_down (model/inference_model.py:88-90)
-  linear(c, d_feats_, kF32, F, tw.upw, lp, tw.upb, P, F, u32, P, kActRelu, nullptr, 0, ulp, P);
-  linear(c, tw.u, lp, P, tw.dnw, lp, tw.dnb, H, P, tw.x, H);
+  linear(c, feats, kF32, F, tw.upw, lp, tw.upb, P, F, u32, P, kActRelu, nullptr, 0, ulp, P);
+  linear(c, ch.u, lp, P, tw.dnw, lp, tw.dnb, H, P, ch.x, H);
   for (auto& bl : tw.blocks) {
     // Block.forward: x = layer(norm1(x)) + x; x = x + mlp(norm2(x)) (model/inference_model.py:63-68)
-    rmsnorm_rows(c, tw.x, bl.n1, eps, H, tw.t, low ? tw.tl : nullptr);
-    bl.layer->forward(c, tw.t, low ? tw.tl : nullptr, tw.x, tw.x, tw.scratch);
-    rmsnorm_rows(c, tw.x, bl.n2, eps, H, low ? nullptr : tw.t, low ? tw.tl : nullptr);
-    linear(c, low ? static_cast<const void*>(tw.tl) : tw.t, lp, H, bl.f1w, lp, bl.f1b, P, H, u32, P, kActRelu,
+    rmsnorm_rows(c, ch.x, bl.n1, eps, H, ch.t, low ? ch.tl : nullptr);
+    bl.layer->forward(c, ch.t, low ? ch.tl : nullptr, ch.x, ch.x, ch.scratch);
+    rmsnorm_rows(c, ch.x, bl.n2, eps, H, low ? nullptr : ch.t, low ? ch.tl : nullptr);
+    linear(c, low ? static_cast<const void*>(ch.tl) : ch.t, lp, H, bl.f1w, lp, bl.f1b, P, H, u32, P, kActRelu,
            nullptr, 0, ulp, P);                                                       // fc1 + ReLU
-    linear(c, tw.u, lp, P, bl.f2w, lp, bl.f2b, H, P, tw.x, H, kActNone, tw.x, H);     // fc2 + residual
+    linear(c, ch.u, lp, P, bl.f2w, lp, bl.f2b, H, P, ch.x, H, kActNone, ch.x, H);     // fc2 + residual
   }
-  output_proj_rows(c, tw.x, ow_, ob_, H, d_preds_, 4, idx);  // shared output_proj (model/inference_model.py:142)
+  output_proj_rows(c, ch.x, ow_, ob_, H, preds, 4, idx);  // shared output_proj (model/inference_model.py:142)
 }
 
 void Engine::enqueue(int rows, cudaStream_t s) {
+  const int L = lanes_for(rows);
+  const int per = (rows + L - 1) / L;
+  k_split_rows<<<1, 32, 0, s>>>(d_n_, d_nl_, L, per);
+  B2E_CUDA(cudaGetLastError());
   B2E_CUDA(cudaEventRecord(fork_, s));
-  for (int t = 0; t < 4; ++t) {
-    Tower& tw = towers_[t];
-    B2E_CUDA(cudaStreamWaitEvent(tw.s, fork_, 0));
-    StepCtx c;
-    c.s = tw.s;
-    c.rows = rows;
-    c.n_dev = d_n_;
-    c.slots = d_slots_;
-    c.lp = opt_.lp;
-    c.err = d_err_;
-    tower_forward(tw, t, c);
-    B2E_CUDA(cudaEventRecord(tw.done, tw.s));
+  for (int l = 0; l < L; ++l) {
+    for (int t = 0; t < 4; ++t) {
+      Chain& ch = chains_[size_t(l) * 4 + t];
+      B2E_CUDA(cudaStreamWaitEvent(ch.s, fork_, 0));
+      StepCtx c;
+      c.s = ch.s;
+      c.rows = per;
+      c.n_dev = d_nl_ + l;
+      c.slots = d_slots_ + size_t(l) * per;
+      c.lp = opt_.lp;
+      c.err = d_err_;
+      tower_forward(towers_[t], ch, t, c, d_feats_ + size_t(l) * per * d_.F, d_preds_ + size_t(l) * per * 4);
+      B2E_CUDA(cudaEventRecord(ch.done, ch.s));
+    }
   }
-  for (auto& tw : towers_) B2E_CUDA(cudaStreamWaitEvent(s, tw.done, 0));
+  for (int ci = 0; ci < 4 * L; ++ci) B2E_CUDA(cudaStreamWaitEvent(s, chains_[ci].done, 0));
 }
 
 void Engine::launch(int n, cudaStream_t s) {

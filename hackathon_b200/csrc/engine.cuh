@@ -14,6 +14,8 @@ struct EngineOptions {
   int capacity = 1;       // state slots (symbols) held on this device
   int max_batch = 1;      // rows per step
   bool graphs = true;     // replay the step from a CUDA graph per batch bucket
+  int lanes = 2;          // independent row halves per tower for batches of >= lane_min_rows
+  int lane_min_rows = 256;
 };
 
 class Engine {
@@ -59,6 +61,10 @@ class Engine {
     size_t o_upw, o_upb, o_dnw, o_dnb;
     const void *upw, *upb, *dnw, *dnb;
     std::vector<Block> blocks;
+  };
+  // One tower over one lane (a contiguous share of the step's rows): its own
+  // stream and activations, so the chains of all towers and lanes run concurrently.
+  struct Chain {
     uint8_t* scratch = nullptr;  // layer scratch
     float *x = nullptr, *t = nullptr, *tl = nullptr, *u = nullptr;  // tl, u: CastLinear-typed GEMM inputs
     cudaStream_t s = nullptr;
@@ -68,7 +74,8 @@ class Engine {
   int bucket(int n) const;
   void launch(int n, cudaStream_t s);   // graph replay or eager enqueue
   void enqueue(int rows, cudaStream_t s);
-  void tower_forward(Tower& t, int idx, const StepCtx& c);
+  void tower_forward(const Tower& t, Chain& ch, int idx, const StepCtx& c, const float* feats, float* preds);
+  int lanes_for(int rows) const;
   void check_host_slots(const int* slots, int n);
 
   Dims d_;
@@ -76,6 +83,8 @@ class Engine {
   WeightPack pack_;
   StateArena arena_;
   std::vector<Tower> towers_;
+  std::vector<Chain> chains_;  // [lane][tower]
+  int* d_nl_ = nullptr;        // live rows per lane (device)
   size_t o_ow_ = 0, o_ob_ = 0;
   const float *ow_ = nullptr, *ob_ = nullptr;
 

@@ -4,7 +4,8 @@
 // in global memory, f32 accumulation in tensor memory. One CTA computes one
 // 128 x 128 output tile:
 //   warp 0     one thread issues TMA loads of A and W tiles (128 rows x 64 K,
-//              128-byte swizzle) into a 4-stage shared-memory ring;
+//              128-byte swizzle) into a 3-stage shared-memory ring (two CTAs
+//              fit one SM, so one tile's epilogue overlaps another's loads);
 //   warp 1     allocates 128 TMEM columns; one thread issues tcgen05.mma
 //              (M=128, N=128, K=16 per instruction) and commits each stage back
 //              to the producer and the finished accumulator to the epilogue;
@@ -25,7 +26,7 @@
 namespace b2e {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3, THREADS = 192;
 constexpr uint32_t TILE_A = BM * BK * 2, TILE_B = BN * BK * 2;
 constexpr uint32_t TMEM_COLS = 128;
 constexpr size_t SMEM = size_t(STAGES) * (TILE_A + TILE_B) + 1024 + 256;
@@ -169,6 +170,18 @@ __device__ __forceinline__ float4 load4(int t, const void* p, int i) {
   return r;
 }
 
+// Round 4 floats to the low type and back (CastLinear's output rounding), two at a time.
+__device__ __forceinline__ float4 round4_lp(int t, float4 x) {
+  if (t == kBF16) {
+    const float2 a = __bfloat1622float2(__floats2bfloat162_rn(x.x, x.y));
+    const float2 b = __bfloat1622float2(__floats2bfloat162_rn(x.z, x.w));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  const float2 a = __half22float2(__floats2half2_rn(x.x, x.y));
+  const float2 b = __half22float2(__floats2half2_rn(x.z, x.w));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 // Store 4 floats as the low type (8 bytes, aligned).
 __device__ __forceinline__ void store4_lp(int t, void* p, size_t i, float4 x) {
   uint2 raw;
@@ -184,7 +197,7 @@ __device__ __forceinline__ void store4_lp(int t, void* p, size_t i, float4 x) {
   *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + i) = raw;
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, 2)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                    const __grid_constant__ TcEpi e) {
   const int M = live_rows(e.M_dev, e.M_max);
@@ -275,41 +288,67 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (!ok) {
       atomicExch(e.err, kTcTimeoutEpilogue);
       *abort_flag = 1;
-    } else if (!*abort_flag) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int q = warp & 3;
-      const int m = m0 + q * 32 + lane;
-      const bool row_ok = m < M;
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        if (n0 + c0 >= e.N) break;  // warp-uniform
-        float v[32];
-        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
-        if (!row_ok) continue;
-        const int nb = n0 + c0;
-        if (e.vec && nb + 32 <= e.N) {
-          // 32 consecutive columns of one row: 16-byte loads and stores
+    }
+    // Both named barriers below are reached by all four epilogue warps whatever
+    // happens, so an error path cannot leave a warp waiting; `go` is read once.
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const bool go = ok && !*abort_flag;
+    const int q = warp & 3;
+    const int m = m0 + q * 32 + lane;
+    const bool row_ok = m < M;
+    if (go) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (e.vec) {
+      {
+        // Phase 1: bias, CastLinear rounding and activation per column, then the
+        // tile goes to shared memory (the operand ring is idle once `done` fired).
+        // 16-byte unit u of tile row r is stored at unit u ^ (r & 7), so the 32
+        // rows a warp writes at once fall in distinct bank groups.
+        float4* stage = reinterpret_cast<float4*>(sA);  // BM x BN floats
+        for (int c0 = 0; go && c0 < BN; c0 += 32) {
+          if (n0 + c0 >= e.N) break;  // warp-uniform
+          float v[32];
+          tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
+          const int nb = n0 + c0;
+          const int r = q * 32 + lane;
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
             float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            if (e.bias) {
+            if (e.bias && nb + j < e.N) {
               const float4 b = load4(e.bias_type, e.bias, nb + j);
               x.x += b.x; x.y += b.y; x.z += b.z; x.w += b.w;
             }
-            if (e.round_out) {
-              x.x = round_to(e.lp, x.x); x.y = round_to(e.lp, x.y);
-              x.z = round_to(e.lp, x.z); x.w = round_to(e.lp, x.w);
-            }
+            if (e.round_out) x = round4_lp(e.lp, x);
             if (e.act == kActRelu) {
               x.x = fmaxf(x.x, 0.f); x.y = fmaxf(x.y, 0.f); x.z = fmaxf(x.z, 0.f); x.w = fmaxf(x.w, 0.f);
             }
-            if (e.R) {
-              const float4 r = *reinterpret_cast<const float4*>(e.R + size_t(m) * e.ldr + nb + j);
-              x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
-            }
-            if (e.C) *reinterpret_cast<float4*>(e.C + size_t(m) * e.ldc + nb + j) = x;
-            if (e.C_lp) store4_lp(e.lp, e.C_lp, size_t(m) * e.ldc_lp + nb + j, x);
+            const int unit = (c0 + j) >> 2;
+            stage[r * (BN / 4) + (unit ^ (r & 7))] = x;
           }
-        } else {
+        }
+        // Phase 2: the four epilogue warps meet; then each warp writes whole rows,
+        // lane l moving 16-byte unit l of a row (512 contiguous bytes per store).
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        for (int r = warp - 2; go && r < BM; r += 4) {
+          const int mm = m0 + r;
+          const int n = n0 + lane * 4;
+          if (mm >= M || n >= e.N) continue;
+          float4 x = stage[r * (BN / 4) + (lane ^ (r & 7))];
+          if (e.R) {
+            const float4 rr = *reinterpret_cast<const float4*>(e.R + size_t(mm) * e.ldr + n);
+            x.x += rr.x; x.y += rr.y; x.z += rr.z; x.w += rr.w;
+          }
+          if (e.C) *reinterpret_cast<float4*>(e.C + size_t(mm) * e.ldc + n) = x;
+          if (e.C_lp) store4_lp(e.lp, e.C_lp, size_t(mm) * e.ldc_lp + n, x);
+        }
+      }
+    } else {
+      {
+        for (int c0 = 0; go && c0 < BN; c0 += 32) {
+          if (n0 + c0 >= e.N) break;  // warp-uniform
+          float v[32];
+          tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
+          if (!row_ok) continue;
+          const int nb = n0 + c0;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int n = nb + j;

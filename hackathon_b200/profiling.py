@@ -92,6 +92,25 @@ def cell(kind: str, rows: int, heads: int, sh: int, sk: int, reps: int) -> None:
     print(f"{kind} rows={rows} heads={heads} sh={sh} sk={sk}: {reps} launches, state {state.numel() * 4 / 1e9:.2f} GB")
 
 
+def linear(m: int, k: int, n: int, reps: int, dtype: str) -> None:
+    import torch
+
+    from . import kernels as K
+
+    dev = torch.device("cuda", 0)
+    dt = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[dtype]
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(m, k, device=dev, generator=g).to(dt)
+    w = (torch.randn(n, k, device=dev, generator=g) * k ** -0.5).to(dt)
+    b = torch.zeros(n, device=dev, dtype=dt)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    for _ in range(reps):
+        K.cast_linear(x, w, b, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    print(f"linear {dtype} m={m} k={k} n={n}: {reps} launches")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -102,11 +121,19 @@ def main(argv=None):
     c.add_argument("--sh", type=int, default=64)
     c.add_argument("--sk", type=int, default=128)
     c.add_argument("--reps", type=int, default=4)
+    li = sub.add_parser("linear")
+    li.add_argument("--m", type=int, default=4096)
+    li.add_argument("--k", type=int, default=512)
+    li.add_argument("--n", type=int, default=256)
+    li.add_argument("--reps", type=int, default=4)
+    li.add_argument("--dtype", default="bf16")
     sub.add_parser("launches").add_argument("csv")
     sub.add_parser("metrics").add_argument("csv")
     a = ap.parse_args(argv)
     if a.cmd == "cell":
         cell(a.kind, a.rows, a.heads, a.sh, a.sk, a.reps)
+    elif a.cmd == "linear":
+        linear(a.m, a.k, a.n, a.reps, a.dtype)
     elif a.cmd == "launches":
         launches(a.csv)
     else:

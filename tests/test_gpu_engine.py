@@ -259,3 +259,24 @@ def test_process_batch_on_gpu_matches_reference(capsys):
     assert_close(np.asarray(preds, np.float32), g["predictions"], RTOL, ATOL, "process_batch predictions")
     assert capsys.readouterr().out.count("WARNING: out of state rows") == 1
     client.close()
+
+
+def test_large_batch_split_into_lanes_matches_oracle():
+    """300 rows: the 512-row bucket runs as two lanes of 256 (the second with 44
+    live rows), each tower on its own stream per lane; every row still equals the
+    oracle, and two steps in a row keep the state consistent."""
+    cfg = C.ModelConfig(hidden_size=64, proj_size=128, tower_depth=2, num_heads=4, num_features=79)
+    sd = Wt.generate_model(cfg, seed=3)
+    eng = EnsembleEngine(cfg, sd, capacity=400, max_batch=512)
+    orc = O.Oracle(cfg, sd)
+    rng = np.random.default_rng(8)
+    slots = rng.permutation(400)[:300].astype(np.int32)
+    state = O.init_state(cfg, 300)
+    for _ in range(2):
+        feats = rng.standard_normal((300, 79), dtype=np.float32)
+        got = eng.step(slots, feats)
+        want, state = orc.step(feats, state)
+        assert_close(got, want, RTOL, ATOL, "preds of a two-lane step")
+    for i in (0, 255, 256, 299):
+        for a, b in zip(eng.read_slot(int(slots[i])), O.flat_leaves(state)):
+            assert_close(a, b[i], RTOL, ATOL, f"state of row {i}")
