@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <string>
 #include <stdexcept>
+#include <utility>
 
 namespace b2e {
 
@@ -135,5 +136,30 @@ __device__ __forceinline__ float4 ld_stream(const float4* p) { return __ldcs(p);
 __device__ __forceinline__ void st_stream(float4* p, float4 v) { __stcs(p, v); }
 
 inline int ceil_div(long a, long b) { return int((a + b - 1) / b); }
+
+// ------------------------------------------- programmatic dependent launch
+// The kernels of a tower's chain are launched with programmatic stream
+// serialization: a kernel may start while its predecessor drains, run its
+// independent prologue (barrier set-up, weight or state prefetch), and waits in
+// pdl_wait() before it reads anything the predecessor wrote or writes anything
+// the predecessor may still read. pdl_wait is per thread. pdl_launch lets the
+// successor start as soon as every CTA of this grid is resident.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2E_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 }  // namespace b2e

@@ -179,17 +179,56 @@ void Engine::tower_forward(const Tower& tw, Chain& ch, int idx, const StepCtx& c
   const float eps = 1.1920928955078125e-07f;  // nn.RMSNorm(eps=None) in float32
   // input_up, ReLU, input_down (model/inference_model.py:88-90)
   linear(c, feats, kF32, F, tw.upw, lp, tw.upb, P, F, u32, P, kActRelu, nullptr, 0, ulp, P);
-  linear(c, ch.u, lp, P, tw.dnw, lp, tw.dnb, H, P, ch.x, H);
-  for (auto& bl : tw.blocks) {
+  const bool fuse = fused_rows(c, H);
+  const size_t nb = tw.blocks.size();
+  if (fuse) {
+    // every RMSNorm, and output_proj, run inside the epilogue of the projection
+    // that produces their input row (one 128x256 tile holds whole rows)
+    RowEpi r0;
+    r0.norm_w = tw.blocks[0].n1;
+    r0.T = ch.t;
+    r0.T_lp = ch.tl;
+    r0.ldt = H;
+    linear(c, ch.u, lp, P, tw.dnw, lp, tw.dnb, H, P, ch.x, H, kActNone, nullptr, 0, nullptr, 0, &r0);
+  } else {
+    linear(c, ch.u, lp, P, tw.dnw, lp, tw.dnb, H, P, ch.x, H);
+  }
+  for (size_t bi = 0; bi < nb; ++bi) {
+    const Block& bl = tw.blocks[bi];
     // Block.forward: x = layer(norm1(x)) + x; x = x + mlp(norm2(x)) (model/inference_model.py:63-68)
-    rmsnorm_rows(c, ch.x, bl.n1, eps, H, ch.t, low ? ch.tl : nullptr);
-    bl.layer->forward(c, ch.t, low ? ch.tl : nullptr, ch.x, ch.x, ch.scratch);
-    rmsnorm_rows(c, ch.x, bl.n2, eps, H, low ? nullptr : ch.t, low ? ch.tl : nullptr);
+    if (!fuse) rmsnorm_rows(c, ch.x, bl.n1, eps, H, ch.t, low ? ch.tl : nullptr);
+    if (fuse) {
+      RowEpi r2;
+      r2.norm_w = bl.n2;
+      r2.T_lp = ch.tl;
+      r2.ldt = H;
+      bl.layer->forward(c, ch.t, ch.tl, ch.x, ch.x, ch.scratch, &r2);
+    } else {
+      bl.layer->forward(c, ch.t, low ? ch.tl : nullptr, ch.x, ch.x, ch.scratch);
+      rmsnorm_rows(c, ch.x, bl.n2, eps, H, low ? nullptr : ch.t, low ? ch.tl : nullptr);
+    }
     linear(c, low ? static_cast<const void*>(ch.tl) : ch.t, lp, H, bl.f1w, lp, bl.f1b, P, H, u32, P, kActRelu,
            nullptr, 0, ulp, P);                                                       // fc1 + ReLU
-    linear(c, ch.u, lp, P, bl.f2w, lp, bl.f2b, H, P, ch.x, H, kActNone, ch.x, H);     // fc2 + residual
+    if (fuse) {
+      RowEpi r3;
+      if (bi + 1 < nb) {  // next Block's norm1
+        r3.norm_w = tw.blocks[bi + 1].n1;
+        r3.T = ch.t;
+        r3.T_lp = ch.tl;
+        r3.ldt = H;
+      } else {  // shared output_proj (model/inference_model.py:142)
+        r3.dot_w = ow_;
+        r3.dot_b = ob_;
+        r3.dot_out = preds;
+        r3.dot_ld = 4;
+        r3.dot_col = idx;
+      }
+      linear(c, ch.u, lp, P, bl.f2w, lp, bl.f2b, H, P, ch.x, H, kActNone, ch.x, H, nullptr, 0, &r3);
+    } else {
+      linear(c, ch.u, lp, P, bl.f2w, lp, bl.f2b, H, P, ch.x, H, kActNone, ch.x, H);  // fc2 + residual
+    }
   }
-  output_proj_rows(c, ch.x, ow_, ob_, H, preds, 4, idx);  // shared output_proj (model/inference_model.py:142)
+  if (!fuse) output_proj_rows(c, ch.x, ow_, ob_, H, preds, 4, idx);  // shared output_proj (model/inference_model.py:142)
 }
 
 void Engine::enqueue(int rows, cudaStream_t s) {

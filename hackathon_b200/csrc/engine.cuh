@@ -14,7 +14,7 @@ struct EngineOptions {
   int capacity = 1;       // state slots (symbols) held on this device
   int max_batch = 1;      // rows per step
   bool graphs = true;     // replay the step from a CUDA graph per batch bucket
-  int lanes = 2;          // independent row halves per tower for batches of >= lane_min_rows
+  int lanes = 1;          // independent row shares per tower for batches of >= lane_min_rows
   int lane_min_rows = 256;
 };
 

@@ -27,6 +27,31 @@ struct GemmGroup {
   const float* R = nullptr;    // [M, N] residual added last, or null (may alias C)
 };
 
+// Row-wise work fused into the tensor-core GEMM's epilogue when one CTA holds
+// whole output rows (N <= 256). In order, per row:
+//   v = y (+ R)                         y: acc + bias, rounded, activated
+//   v = LayerNorm(v) * ln_w             if ln_w  (biased variance, eps ln_eps)
+//   v = v + R2                          if R2
+//   C = v                               (f32), C_lp as usual
+//   T = RMSNorm(v) * norm_w             if norm_w: to T (f32) and/or T_lp (low type)
+//   dot_out[m * dot_ld + dot_col] = v . dot_w + dot_b[0]   if dot_w
+struct RowEpi {
+  const float* ln_w = nullptr;
+  float ln_eps = 1e-5f;
+  const float* R2 = nullptr;
+  int ldr2 = 0;
+  const float* norm_w = nullptr;
+  float norm_eps = 1.1920928955078125e-07f;
+  float* T = nullptr;
+  void* T_lp = nullptr;
+  int ldt = 0;
+  const float* dot_w = nullptr;
+  const float* dot_b = nullptr;
+  float* dot_out = nullptr;
+  int dot_ld = 0, dot_col = 0;
+  bool active() const { return ln_w || R2 || norm_w || dot_w; }
+};
+
 struct GemmParams {
   GemmGroup g[kMaxGroups];
   int groups = 1;
@@ -39,6 +64,7 @@ struct GemmParams {
   int round_out = 0;  // round the (acc + bias) to `lp` (CastLinear output)
   int act = kActNone;
   int* err = nullptr;  // device error word for bounded-wait timeouts (tensor-core path)
+  RowEpi row;          // needs the tensor-core path and N <= 256 (gemm_tc_row_eligible)
 };
 
 // Enqueue on `stream`. Picks, in order: the tcgen05 tensor-core kernel
@@ -49,6 +75,7 @@ void gemm(const GemmParams& p, cudaStream_t stream);
 
 void gemm_tc_init();  // once per device, before any capture
 bool gemm_tc_eligible(const GemmParams& p);
+bool gemm_tc_row_eligible(const GemmParams& p);  // eligible, and N fits one 256-wide tile
 void gemm_tc(const GemmParams& p, cudaStream_t stream);
 
 }  // namespace b2e

@@ -2,16 +2,20 @@
 //
 // C[m, n] = epilogue( sum_k A[m, k] * W[n, k] ), A and W both bf16 (or both f16)
 // in global memory, f32 accumulation in tensor memory. One CTA computes one
-// 128 x 128 output tile:
-//   warp 0     one thread issues TMA loads of A and W tiles (128 rows x 64 K,
-//              128-byte swizzle) into a 3-stage shared-memory ring (two CTAs
-//              fit one SM, so one tile's epilogue overlaps another's loads);
-//   warp 1     allocates 128 TMEM columns; one thread issues tcgen05.mma
-//              (M=128, N=128, K=16 per instruction) and commits each stage back
+// 128 x BN output tile (BN = 128, or 256 so that a tile holds whole rows):
+//   warp 0     one thread issues TMA loads of A and W tiles (rows x 64 K,
+//              128-byte swizzle) into a 3-stage shared-memory ring;
+//   warp 1     allocates BN TMEM columns; one thread issues tcgen05.mma
+//              (M=128, N=BN, K=16 per instruction) and commits each stage back
 //              to the producer and the finished accumulator to the epilogue;
-//   warps 2-5  read the accumulator with tcgen05.ld (each warp its 32-lane
-//              quadrant) and apply bias, CastLinear rounding, ReLU and the
-//              residual, exactly like the SIMT epilogue (gemm.cu).
+//   warps 2-5  epilogue, in two phases. Phase 1: each warp reads its 32-lane
+//              TMEM quadrant (one thread per row) with tcgen05.ld, applies bias,
+//              CastLinear rounding and activation, and stages the tile in the
+//              now idle operand ring. Phase 2: each warp takes whole rows (lane
+//              = 16-byte column unit) and writes them with row-contiguous
+//              stores, adding the residual; optional row work (RowEpi: LayerNorm,
+//              a second residual, the next RMSNorm, a dot product) runs here with
+//              warp-shuffle reductions.
 // Every mbarrier wait is bounded: past ~1 s the kernel records an error code,
 // stops issuing work, waits (bounded) for what it issued, frees its TMEM and
 // returns. TMA loads here never use cluster multicast.
@@ -26,11 +30,17 @@
 namespace b2e {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3, THREADS = 192;
-constexpr uint32_t TILE_A = BM * BK * 2, TILE_B = BN * BK * 2;
-constexpr uint32_t TMEM_COLS = 128;
-constexpr size_t SMEM = size_t(STAGES) * (TILE_A + TILE_B) + 1024 + 256;
+constexpr int BM = 128, BK = 64, STAGES = 3, THREADS = 192;
+constexpr uint32_t TILE_A = BM * BK * 2;
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
+
+template <int BN>
+struct Cfg {
+  static constexpr uint32_t TILE_B = BN * BK * 2;
+  static constexpr uint32_t TMEM_COLS = BN;
+  static constexpr size_t SMEM = size_t(STAGES) * (TILE_A + TILE_B) + 1024 + 256;
+  static_assert(size_t(BM) * BN * 4 <= size_t(STAGES) * (TILE_A + TILE_B), "epilogue stage must fit the ring");
+};
 
 enum TcError : int { kTcTimeoutProducer = 101, kTcTimeoutMma = 102, kTcTimeoutEpilogue = 103 };
 
@@ -49,7 +59,9 @@ struct TcEpi {
   int lp;  // kBF16 or kF16: operand type and CastLinear rounding type
   int round_out, act;
   int* err;
-  int vec;  // every row start of bias/R/C/C_lp is 16-byte (f32) / 8-byte (low type) aligned
+  int vec;  // every row start of bias/R/C/C_lp (and RowEpi buffers) is 16-byte (f32) / 8-byte (low) aligned
+  RowEpi row;
+  int row_on;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -107,9 +119,9 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
 }
 
 // Instruction descriptor, kind::f16: f32 accumulator, A/B type, both K-major.
-__host__ __device__ constexpr uint32_t instr_desc(int lp) {
+__host__ __device__ constexpr uint32_t instr_desc(int lp, int bn) {
   const uint32_t ab = lp == kBF16 ? 1u : 0u;
-  return (1u << 4) | (ab << 7) | (ab << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+  return (1u << 4) | (ab << 7) | (ab << 10) | (uint32_t(bn >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
@@ -141,20 +153,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
-      "[%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-}
-
-// 4 consecutive values of a bias vector of type t (f32, bf16 or f16), 16/8-byte aligned.
+// 4 consecutive values of a vector of type t (f32, bf16 or f16), 16/8-byte aligned.
 __device__ __forceinline__ float4 load4(int t, const void* p, int i) {
   if (t == kF32) return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
   const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p) + i);
@@ -197,9 +196,16 @@ __device__ __forceinline__ void store4_lp(int t, void* p, size_t i, float4 x) {
   *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + i) = raw;
 }
 
-__global__ void __launch_bounds__(THREADS, 2)
+__device__ __forceinline__ float4 f4add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+__device__ __forceinline__ float f4sum(float4 a) { return (a.x + a.y) + (a.z + a.w); }
+
+template <int BN>
+__global__ void __launch_bounds__(THREADS, BN == 128 ? 2 : 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                    const __grid_constant__ TcEpi e) {
+  using K = Cfg<BN>;
+  constexpr int UPR = BN / 4;    // 16-byte units per tile row
+  constexpr int UPL = UPR / 32;  // units per lane in phase 2
   const int M = live_rows(e.M_dev, e.M_max);
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   if (m0 >= M) return;  // whole CTA, before any barrier or TMEM use
@@ -208,7 +214,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * TILE_A;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * TILE_B);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * K::TILE_B);
   uint64_t* empty = full + STAGES;
   uint64_t* done = empty + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -227,7 +233,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS));
+                 "r"(K::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -248,9 +254,9 @@ __global__ void __launch_bounds__(THREADS, 2)
           *abort_flag = 1;
           break;
         }
-        mbar_expect_tx(&full[s], TILE_A + TILE_B);
+        mbar_expect_tx(&full[s], TILE_A + K::TILE_B);
         tma_load_2d(sA + s * TILE_A, &ta, kb * BK, m0, &full[s]);
-        tma_load_2d(sB + s * TILE_B, &tb, kb * BK, n0, &full[s]);
+        tma_load_2d(sB + s * K::TILE_B, &tb, kb * BK, n0, &full[s]);
         ++issued;
       }
       if (*abort_flag) {
@@ -263,7 +269,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---- MMA issuer
-      const uint32_t idesc = instr_desc(e.lp);
+      const uint32_t idesc = instr_desc(e.lp, BN);
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % STAGES;
         const uint32_t ph = (kb / STAGES) & 1;
@@ -273,7 +279,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a0 = smem_u32(sA + s * TILE_A), b0 = smem_u32(sB + s * TILE_B);
+        const uint32_t a0 = smem_u32(sA + s * TILE_A), b0 = smem_u32(sB + s * K::TILE_B);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)  // K=16 per instruction: +32 bytes inside the swizzled row
           mma_f16(tmem, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), idesc, (kb | k) != 0);
@@ -298,69 +304,129 @@ __global__ void __launch_bounds__(THREADS, 2)
     const bool row_ok = m < M;
     if (go) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (e.vec) {
-      {
-        // Phase 1: bias, CastLinear rounding and activation per column, then the
-        // tile goes to shared memory (the operand ring is idle once `done` fired).
-        // 16-byte unit u of tile row r is stored at unit u ^ (r & 7), so the 32
-        // rows a warp writes at once fall in distinct bank groups.
-        float4* stage = reinterpret_cast<float4*>(sA);  // BM x BN floats
-        for (int c0 = 0; go && c0 < BN; c0 += 32) {
-          if (n0 + c0 >= e.N) break;  // warp-uniform
-          float v[32];
-          tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
-          const int nb = n0 + c0;
-          const int r = q * 32 + lane;
+      // Phase 1: bias, rounding, activation per column; tile to shared memory
+      // (the operand ring is idle once `done` fired). 16-byte unit u of tile row
+      // r lives at unit u ^ (r & 7): the 32 rows a warp writes fall in distinct
+      // bank groups.
+      float4* stage = reinterpret_cast<float4*>(sA);  // BM x BN floats
+      for (int c0 = 0; go && c0 < BN; c0 += 32) {
+        if (n0 + c0 >= e.N) break;  // warp-uniform
+        float v[32];
+        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
+        const int nb = n0 + c0;
+        const int r = q * 32 + lane;
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            if (e.bias && nb + j < e.N) {
-              const float4 b = load4(e.bias_type, e.bias, nb + j);
-              x.x += b.x; x.y += b.y; x.z += b.z; x.w += b.w;
-            }
-            if (e.round_out) x = round4_lp(e.lp, x);
-            if (e.act == kActRelu) {
-              x.x = fmaxf(x.x, 0.f); x.y = fmaxf(x.y, 0.f); x.z = fmaxf(x.z, 0.f); x.w = fmaxf(x.w, 0.f);
-            }
-            const int unit = (c0 + j) >> 2;
-            stage[r * (BN / 4) + (unit ^ (r & 7))] = x;
+        for (int j = 0; j < 32; j += 4) {
+          float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          if (e.bias && nb + j < e.N) x = f4add(x, load4(e.bias_type, e.bias, nb + j));
+          if (e.round_out) x = round4_lp(e.lp, x);
+          if (e.act == kActRelu) {
+            x.x = fmaxf(x.x, 0.f); x.y = fmaxf(x.y, 0.f); x.z = fmaxf(x.z, 0.f); x.w = fmaxf(x.w, 0.f);
+          }
+          const int unit = (c0 + j) >> 2;
+          stage[r * UPR + (unit ^ (r & 7))] = x;
+        }
+      }
+      // Phase 2: whole rows per warp; lane l owns units l, l+32, ... of a row.
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const RowEpi& re = e.row;
+      for (int r = warp - 2; go && r < BM; r += 4) {
+        const int mm = m0 + r;
+        if (mm >= M) break;  // rows only grow
+        float4 x[UPL];
+        bool in[UPL];
+#pragma unroll
+        for (int u = 0; u < UPL; ++u) {
+          const int unit = lane + 32 * u;
+          const int n = n0 + unit * 4;
+          in[u] = n < e.N;
+          x[u] = in[u] ? stage[r * UPR + (unit ^ (r & 7))] : make_float4(0.f, 0.f, 0.f, 0.f);
+          if (in[u] && e.R) x[u] = f4add(x[u], *reinterpret_cast<const float4*>(e.R + size_t(mm) * e.ldr + n));
+        }
+        if (e.row_on) {
+          const float invN = 1.0f / float(e.N);
+          if (re.ln_w) {  // LayerNorm(bias=False): two-pass mean and biased variance
+            float s = 0.f;
+#pragma unroll
+            for (int u = 0; u < UPL; ++u) s += f4sum(x[u]);
+            const float mu = warp_sum(s) * invN;
+            float q2 = 0.f;
+#pragma unroll
+            for (int u = 0; u < UPL; ++u)
+              if (in[u]) {
+                const float4 d = make_float4(x[u].x - mu, x[u].y - mu, x[u].z - mu, x[u].w - mu);
+                q2 += f4sum(make_float4(d.x * d.x, d.y * d.y, d.z * d.z, d.w * d.w));
+              }
+            const float rs = 1.0f / sqrtf(warp_sum(q2) * invN + re.ln_eps);
+#pragma unroll
+            for (int u = 0; u < UPL; ++u)
+              if (in[u]) {
+                const int n = n0 + (lane + 32 * u) * 4;
+                const float4 w = *reinterpret_cast<const float4*>(re.ln_w + n);
+                x[u] = make_float4((x[u].x - mu) * rs * w.x, (x[u].y - mu) * rs * w.y, (x[u].z - mu) * rs * w.z,
+                                   (x[u].w - mu) * rs * w.w);
+              }
+          }
+          if (re.R2) {
+#pragma unroll
+            for (int u = 0; u < UPL; ++u)
+              if (in[u])
+                x[u] = f4add(x[u], *reinterpret_cast<const float4*>(re.R2 + size_t(mm) * re.ldr2 + n0 + (lane + 32 * u) * 4));
           }
         }
-        // Phase 2: the four epilogue warps meet; then each warp writes whole rows,
-        // lane l moving 16-byte unit l of a row (512 contiguous bytes per store).
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        for (int r = warp - 2; go && r < BM; r += 4) {
-          const int mm = m0 + r;
-          const int n = n0 + lane * 4;
-          if (mm >= M || n >= e.N) continue;
-          float4 x = stage[r * (BN / 4) + (lane ^ (r & 7))];
-          if (e.R) {
-            const float4 rr = *reinterpret_cast<const float4*>(e.R + size_t(mm) * e.ldr + n);
-            x.x += rr.x; x.y += rr.y; x.z += rr.z; x.w += rr.w;
+#pragma unroll
+        for (int u = 0; u < UPL; ++u)
+          if (in[u]) {
+            const int n = n0 + (lane + 32 * u) * 4;
+            if (e.C) *reinterpret_cast<float4*>(e.C + size_t(mm) * e.ldc + n) = x[u];
+            if (e.C_lp) store4_lp(e.lp, e.C_lp, size_t(mm) * e.ldc_lp + n, x[u]);
           }
-          if (e.C) *reinterpret_cast<float4*>(e.C + size_t(mm) * e.ldc + n) = x;
-          if (e.C_lp) store4_lp(e.lp, e.C_lp, size_t(mm) * e.ldc_lp + n, x);
+        if (e.row_on && re.norm_w) {  // nn.RMSNorm of the finished row
+          float ss = 0.f;
+#pragma unroll
+          for (int u = 0; u < UPL; ++u)
+            ss += f4sum(make_float4(x[u].x * x[u].x, x[u].y * x[u].y, x[u].z * x[u].z, x[u].w * x[u].w));
+          const float inv = 1.0f / sqrtf(warp_sum(ss) * (1.0f / float(e.N)) + re.norm_eps);
+#pragma unroll
+          for (int u = 0; u < UPL; ++u)
+            if (in[u]) {
+              const int n = n0 + (lane + 32 * u) * 4;
+              const float4 w = *reinterpret_cast<const float4*>(re.norm_w + n);
+              const float4 t = make_float4(x[u].x * inv * w.x, x[u].y * inv * w.y, x[u].z * inv * w.z, x[u].w * inv * w.w);
+              if (re.T) *reinterpret_cast<float4*>(re.T + size_t(mm) * re.ldt + n) = t;
+              if (re.T_lp) store4_lp(e.lp, re.T_lp, size_t(mm) * re.ldt + n, t);
+            }
+        }
+        if (e.row_on && re.dot_w) {  // output_proj: v . w + b
+          float d = 0.f;
+#pragma unroll
+          for (int u = 0; u < UPL; ++u)
+            if (in[u]) {
+              const float4 w = *reinterpret_cast<const float4*>(re.dot_w + n0 + (lane + 32 * u) * 4);
+              d += f4sum(make_float4(x[u].x * w.x, x[u].y * w.y, x[u].z * w.z, x[u].w * w.w));
+            }
+          d = warp_sum(d);
+          if (lane == 0) re.dot_out[size_t(mm) * re.dot_ld + re.dot_col] = d + re.dot_b[0];
         }
       }
     } else {
-      {
-        for (int c0 = 0; go && c0 < BN; c0 += 32) {
-          if (n0 + c0 >= e.N) break;  // warp-uniform
-          float v[32];
-          tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
-          if (!row_ok) continue;
-          const int nb = n0 + c0;
+      for (int c0 = 0; go && c0 < BN; c0 += 32) {
+        if (n0 + c0 >= e.N) break;  // warp-uniform
+        float v[32];
+        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
+        if (!row_ok) continue;
+        const int nb = n0 + c0;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = nb + j;
-            if (n >= e.N) continue;
-            float x = v[j];
-            if (e.bias) x += load_as(e.bias_type, e.bias, n);
-            if (e.round_out) x = round_to(e.lp, x);
-            if (e.act == kActRelu) x = fmaxf(x, 0.0f);
-            if (e.R) x += e.R[size_t(m) * e.ldr + n];
-            if (e.C) e.C[size_t(m) * e.ldc + n] = x;
-            if (e.C_lp) store_as(e.lp, e.C_lp, size_t(m) * e.ldc_lp + n, x);
-          }
+        for (int j = 0; j < 32; ++j) {
+          const int n = nb + j;
+          if (n >= e.N) continue;
+          float x = v[j];
+          if (e.bias) x += load_as(e.bias_type, e.bias, n);
+          if (e.round_out) x = round_to(e.lp, x);
+          if (e.act == kActRelu) x = fmaxf(x, 0.0f);
+          if (e.R) x += e.R[size_t(m) * e.ldr + n];
+          if (e.C) e.C[size_t(m) * e.ldc + n] = x;
+          if (e.C_lp) store_as(e.lp, e.C_lp, size_t(m) * e.ldc_lp + n, x);
         }
       }
     }
@@ -369,7 +435,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(K::TMEM_COLS));
   }
 }
 
@@ -403,11 +469,34 @@ void make_map(CUtensorMap* m, const void* base, int lp, uint64_t inner, uint64_t
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
+
+template <int BN>
+void launch_tc(const GemmParams& p, bool vec, cudaStream_t s) {
+  CUtensorMap ta, tb;
+  make_map(&ta, p.g[0].A, p.w_type, uint64_t(p.K), uint64_t(p.M_max), uint64_t(p.lda), BM);
+  make_map(&tb, p.g[0].W, p.w_type, uint64_t(p.K), uint64_t(p.N), uint64_t(p.ldw), BN);
+  const GemmGroup& g = p.g[0];
+  TcEpi e{g.bias, p.bias_type, g.C, p.ldc, g.C_lp, p.ldc_lp, g.R, p.ldr, p.M_max, p.M_dev,
+          p.N, p.K, p.w_type, p.round_out, p.act, p.err, vec ? 1 : 0, p.row, p.row.active() ? 1 : 0};
+  dim3 grid(ceil_div(p.N, BN), ceil_div(p.M_max, BM));
+  gemm_tc_kernel<BN><<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ta, tb, e);
+  B2E_CUDA(cudaGetLastError());
+}
+
+bool row_buffers_ok(const GemmParams& p) {
+  const RowEpi& r = p.row;
+  return (!r.ln_w || aligned16(r.ln_w)) && (!r.R2 || (aligned16(r.R2) && r.ldr2 % 4 == 0)) &&
+         (!r.norm_w || aligned16(r.norm_w)) && (!r.T || (aligned16(r.T) && r.ldt % 4 == 0)) &&
+         (!r.T_lp || (aligned8(r.T_lp) && r.ldt % 4 == 0)) &&
+         (!r.dot_w || (aligned16(r.dot_w) && r.dot_b && r.dot_out));
+}
 
 }  // namespace
 
 void gemm_tc_init() {
-  B2E_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(SMEM)));
+  B2E_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg<128>::SMEM)));
+  B2E_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg<256>::SMEM)));
 }
 
 bool gemm_tc_eligible(const GemmParams& p) {
@@ -416,20 +505,22 @@ bool gemm_tc_eligible(const GemmParams& p) {
          aligned16(p.g[0].W) && p.err != nullptr && encode_fn() != nullptr;
 }
 
+bool gemm_tc_row_eligible(const GemmParams& p) {
+  return gemm_tc_eligible(p) && p.N <= 256 && row_buffers_ok(p);
+}
+
 void gemm_tc(const GemmParams& p, cudaStream_t s) {
   B2E_CHECK(gemm_tc_eligible(p), kErrInternal, "gemm_tc: problem not eligible");
-  CUtensorMap ta, tb;
-  make_map(&ta, p.g[0].A, p.w_type, uint64_t(p.K), uint64_t(p.M_max), uint64_t(p.lda), BM);
-  make_map(&tb, p.g[0].W, p.w_type, uint64_t(p.K), uint64_t(p.N), uint64_t(p.ldw), BN);
   const GemmGroup& g = p.g[0];
-  const bool vec = p.N % 4 == 0 && (!g.bias || (reinterpret_cast<uintptr_t>(g.bias) % 16 == 0)) &&
-                   (!g.C || (aligned16(g.C) && p.ldc % 4 == 0)) && (!g.R || (aligned16(g.R) && p.ldr % 4 == 0)) &&
-                   (!g.C_lp || (reinterpret_cast<uintptr_t>(g.C_lp) % 8 == 0 && p.ldc_lp % 4 == 0));
-  TcEpi e{g.bias, p.bias_type, g.C, p.ldc, g.C_lp, p.ldc_lp, g.R, p.ldr, p.M_max, p.M_dev,
-          p.N, p.K, p.w_type, p.round_out, p.act, p.err, vec ? 1 : 0};
-  dim3 grid(ceil_div(p.N, BN), ceil_div(p.M_max, BM));
-  gemm_tc_kernel<<<grid, THREADS, SMEM, s>>>(ta, tb, e);
-  B2E_CUDA(cudaGetLastError());
+  const bool vec = p.N % 4 == 0 && (!g.bias || aligned16(g.bias)) && (!g.C || (aligned16(g.C) && p.ldc % 4 == 0)) &&
+                   (!g.R || (aligned16(g.R) && p.ldr % 4 == 0)) &&
+                   (!g.C_lp || (aligned8(g.C_lp) && p.ldc_lp % 4 == 0));
+  if (p.row.active()) {
+    B2E_CHECK(gemm_tc_row_eligible(p) && vec, kErrInternal, "gemm_tc: row epilogue needs N <= 256 and aligned rows");
+    launch_tc<256>(p, vec, s);
+  } else {
+    launch_tc<128>(p, vec, s);
+  }
 }
 
 }  // namespace b2e

@@ -267,7 +267,7 @@ class Mamba2Layer : public Layer {
     return scratch_;
   }
   void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
-               uint8_t* scratch) override {
+               uint8_t* scratch, const RowEpi* post) override {
     const Buf b = carve(scratch, c.rows);
     const RowCtx rc{c.n_dev, c.rows, c.slots};
     const void* a1 = in_lp ? in_lp : in;
@@ -285,7 +285,7 @@ class Mamba2Layer : public Layer {
     ssm_cols(sp, c.rows, c.s);
     Mamba2PostP po{rc, b.ys, b.xs, b.proj, n1_, mi_, hs_, dd_, nw_, b.A, lp_};
     k_mamba2_post<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(po);
-    linear(c, b.A, lp_, mi_, out_, lp_, nullptr, H_, mi_, out, H_, kActNone, residual, H_);  // out_proj (mamba2.py:165)
+    linear(c, b.A, lp_, mi_, out_, lp_, nullptr, H_, mi_, out, H_, kActNone, residual, H_, nullptr, 0, post);  // out_proj (mamba2.py:165)
     B2E_CUDA(cudaGetLastError());
   }
 
@@ -399,7 +399,7 @@ class RetNetLayer : public Layer {
     return scratch_;
   }
   void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
-               uint8_t* scratch) override {
+               uint8_t* scratch, const RowEpi* post) override {
     const Buf b = carve(scratch, c.rows);
     const RowCtx rc{c.n_dev, c.rows, c.slots};
     linear(c, in_lp ? in_lp : in, in_lp ? lp_ : kF32, H_, w1_, lp_, nullptr, 4 * H_, H_, b.proj, 4 * H_);  // q, k, v, g (retnet.py:66-69)
@@ -415,7 +415,7 @@ class RetNetLayer : public Layer {
     outer_rows(op, c.rows, c.s);
     RetPostP po{rc, b.o, b.proj, H_, nh_, hs_, b.A, lp_};
     k_retnet_post<<<c.rows, kRowThreads, nh_ * sizeof(float), c.s>>>(po);
-    linear(c, b.A, lp_, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_);  // out_proj (retnet.py:170)
+    linear(c, b.A, lp_, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_, nullptr, 0, post);  // out_proj (retnet.py:170)
     B2E_CUDA(cudaGetLastError());
   }
 
@@ -510,7 +510,7 @@ class HawkLayer : public Layer {
     return scratch_;
   }
   void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
-               uint8_t* scratch) override {
+               uint8_t* scratch, const RowEpi* post) override {
     const Buf b = carve(scratch, c.rows);
     const RowCtx rc{c.n_dev, c.rows, c.slots};
     linear(c, in_lp ? in_lp : in, in_lp ? lp_ : kF32, H_, w1_, lp_, nullptr, 2 * H_, H_, b.proj, 2 * H_);  // gate_proj, recurrent_proj (hawk.py:77-78)
@@ -531,7 +531,7 @@ class HawkLayer : public Layer {
     gemm(g, c.s);
     RglruP rp{rc, b.gates, b.xc, b.proj, H_, h_, sh_, a_, b.A, lp_};
     k_rglru<<<c.rows, kRowThreads, 0, c.s>>>(rp);
-    linear(c, b.A, lp_, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_);  // out_proj (hawk.py:84)
+    linear(c, b.A, lp_, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_, nullptr, 0, post);  // out_proj (hawk.py:84)
     B2E_CUDA(cudaGetLastError());
   }
 
@@ -869,7 +869,7 @@ class XLSTMLayer : public Layer {
     return scratch_;
   }
   void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
-               uint8_t* scratch) override {
+               uint8_t* scratch, const RowEpi* post) override {
     const Buf b = carve(scratch, c.rows);
     const RowCtx rc{c.n_dev, c.rows, c.slots};
     // ---- sLSTM block (xlstm.py:304-318)
@@ -912,9 +912,20 @@ class XLSTMLayer : public Layer {
     outer_rows(op, c.rows, c.s);
     MlstmPostP pp{rc, b.num, b.den, b.xca, b.proj, mi_, nh_, ongw_, ongb_, skip_, b.A, lp_};
     k_mlstm_post<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(pp);
-    linear(c, b.A, lp_, mi_, down_, lp_, nullptr, H_, mi_, b.x2, H_, kActNone, b.x1, H_);  // proj_down + skip
-    XFinalP fp{rc, b.x2, H_, fnw_, residual, out};
-    k_xlstm_final<<<c.rows, kRowThreads, H_ * sizeof(float), c.s>>>(fp);
+    if (post) {
+      // proj_down + skip, final LayerNorm, Block residual and the Block's norm2,
+      // all in the GEMM epilogue (xlstm.py:217-219, 365; inference_model.py:65-67)
+      RowEpi re = *post;
+      re.ln_w = fnw_;
+      re.ln_eps = 1e-5f;
+      re.R2 = residual;
+      re.ldr2 = H_;
+      linear(c, b.A, lp_, mi_, down_, lp_, nullptr, H_, mi_, out, H_, kActNone, b.x1, H_, nullptr, 0, &re);
+    } else {
+      linear(c, b.A, lp_, mi_, down_, lp_, nullptr, H_, mi_, b.x2, H_, kActNone, b.x1, H_);  // proj_down + skip
+      XFinalP fp{rc, b.x2, H_, fnw_, residual, out};
+      k_xlstm_final<<<c.rows, kRowThreads, H_ * sizeof(float), c.s>>>(fp);
+    }
     B2E_CUDA(cudaGetLastError());
   }
 
@@ -959,8 +970,10 @@ void output_proj_rows(const StepCtx& c, const float* x, const float* w, const fl
   B2E_CUDA(cudaGetLastError());
 }
 
+bool fused_rows(const StepCtx& c, int H) { return c.lp != kF32 && c.rows > 16 && H <= 256 && H % 16 == 0; }
+
 void linear(const StepCtx& c, const void* A, int at, int lda, const void* W, int wt, const void* bias, int N, int K,
-            float* C, int ldc, int act, const float* R, int ldr, void* C_lp, int ldc_lp) {
+            float* C, int ldc, int act, const float* R, int ldr, void* C_lp, int ldc_lp, const RowEpi* row) {
   GemmParams p;
   p.groups = 1;
   p.g[0].A = A;
@@ -984,6 +997,10 @@ void linear(const StepCtx& c, const void* A, int at, int lda, const void* W, int
   p.bias_type = wt;  // CastLinear stores its bias in the weight's type (example_model.py:85-88)
   p.round_out = wt != kF32;
   p.act = act;
+  if (row) {
+    p.row = *row;
+    B2E_CHECK(gemm_tc_row_eligible(p), kErrInternal, "fused row epilogue requested for an ineligible projection");
+  }
   gemm(p, c.s);
 }
 

@@ -3,6 +3,7 @@
 #include <memory>
 #include <string>
 
+#include "gemm.cuh"
 #include "runtime.cuh"
 
 namespace b2e {
@@ -50,8 +51,10 @@ class Layer {
   // out and residual are [rows][H] f32 and out may alias residual. in_lp, when
   // not null, is `in` already rounded to the CastLinear type (what CastLinear
   // feeds its matmul), so the projections can run on the tensor cores.
+  // `post`, when not null, is row work for the layer's final projection
+  // (fused_rows(c, H) must hold): the engine passes the Block's norm2 there.
   virtual void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
-                       uint8_t* scratch) = 0;
+                       uint8_t* scratch, const RowEpi* post = nullptr) = 0;
 
   static std::unique_ptr<Layer> make(int kind, const Dims& d, int lp);
 };
@@ -65,10 +68,14 @@ void rmsnorm_rows(const StepCtx& c, const float* x, const float* w, float eps, i
 void output_proj_rows(const StepCtx& c, const float* x, const float* w, const float* b, int H, float* preds,
                       int ld, int col);
 // Enqueue one nn.Linear / CastLinear application (see gemm.cuh). A has type
-// `at` (f32, or already the weight's low type); C_lp receives a low-type copy.
+// `at` (f32, or already the weight's low type); C_lp receives a low-type copy;
+// `row` is optional row work fused into the tensor-core epilogue.
 void linear(const StepCtx& c, const void* A, int at, int lda, const void* W, int wt, const void* bias, int N, int K,
             float* C, int ldc, int act = 0, const float* R = nullptr, int ldr = 0, void* C_lp = nullptr,
-            int ldc_lp = 0);
+            int ldc_lp = 0, const RowEpi* row = nullptr);
+// True when this step's projections run on the tensor cores and a 256-wide tile
+// holds a whole hidden-size row, so row norms fuse into GEMM epilogues.
+bool fused_rows(const StepCtx& c, int H);
 // Set *n_dev = n on the stream (tiny kernel; graph-capturable).
 void set_rows(int* n_dev, int n, cudaStream_t s);
 

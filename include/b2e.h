@@ -78,7 +78,7 @@ typedef struct b2e_engine_options {
   int32_t capacity;     /* symbol slots of recurrent state (num_symbols, example_model.py:335) */
   int32_t max_batch;    /* rows per step, <= 65535 */
   int32_t use_graphs;   /* 1: replay each step from a CUDA graph per batch bucket */
-  int32_t lanes;        /* independent row shares per tower for large batches; 0 = default (2) */
+  int32_t lanes;        /* independent row shares per tower for large batches; 0 = default (1) */
   int32_t lane_min_rows;/* batches from this many rows use `lanes`; 0 = default (256) */
 } b2e_engine_options;
 

@@ -267,7 +267,7 @@ def test_large_batch_split_into_lanes_matches_oracle():
     oracle, and two steps in a row keep the state consistent."""
     cfg = C.ModelConfig(hidden_size=64, proj_size=128, tower_depth=2, num_heads=4, num_features=79)
     sd = Wt.generate_model(cfg, seed=3)
-    eng = EnsembleEngine(cfg, sd, capacity=400, max_batch=512)
+    eng = EnsembleEngine(cfg, sd, capacity=400, max_batch=512, lanes=2)
     orc = O.Oracle(cfg, sd)
     rng = np.random.default_rng(8)
     slots = rng.permutation(400)[:300].astype(np.int32)

