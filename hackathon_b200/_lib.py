@@ -74,6 +74,7 @@ _SIGS = {
     "b2e_retnet_step": (C.c_int, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P]),
     "b2e_mamba2_step": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P]),
     "b2e_linear": (C.c_int, [_P, _I32, _I32, _I32, _P, _I32, _P, _I32, _I32, _P, _P, _P]),
+    "b2e_linear_static": (C.c_int, [_P, _I32, _I32, _I32, _P, _I32, _P, _I32, _I32, _P, _P, _P]),
     "b2e_layer_create": (C.c_int, [_I32, C.POINTER(ModelConfigC), C.POINTER(EngineOptionsC), C.POINTER(TensorC),
                                    _I32, C.POINTER(_P)]),
     "b2e_layer_destroy": (None, [_P]),

@@ -1,5 +1,6 @@
 // C ABI (include/b2e.h): status codes in, exceptions never cross the boundary.
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <string>
 
@@ -115,6 +116,12 @@ void check_cell(int batch, int heads, int a, int b) {
 }
 
 }  // namespace
+
+namespace b2e {
+// The status/last-error translation above, for entry points defined in other
+// translation units.
+int abi_call(const std::function<void()>& f) { return guard(f); }
+}  // namespace b2e
 
 extern "C" {
 

@@ -145,6 +145,27 @@ B2E_API int b2e_mamba2_step(float* ssm, const float* x, const float* b, const fl
 B2E_API int b2e_linear(const void* x, int32_t x_dtype, int32_t m, int32_t k, const void* w, int32_t w_dtype,
                        const void* bias, int32_t n, int32_t act, float* y, int32_t* d_err, void* stream);
 
+/* ---- b2e_linear for callers that cannot allocate device memory ----
+ * No counterpart in the reference: an addition of this library. Same operands,
+ * types and result as b2e_linear, but every byte of scratch (the tensor-core
+ * kernel's error word and, for an f32 x with a bf16/fp16 weight, x rounded to
+ * the weight's type) lives in one static device array of 16 MiB + 256 B inside
+ * the library, so the call makes no cudaMalloc, cudaFree or other allocating
+ * call. For hosts whose device memory is all owned by their own pool, and for
+ * loops that must not allocate after start-up.
+ *  - f32 x with a bf16/fp16 weight needs m * k <= 8388608; larger is refused
+ *    with B2E_ERR_INVALID (use b2e_linear).
+ *  - The first call on a device (the current device) looks up the array's
+ *    device address; make that first call before any stream capture.
+ *  - Every GPU that loads the library holds the array until the process exits.
+ *  - All calls share the array: calls that overlap on the GPU (other streams,
+ *    other threads) race. Each call clears the error word it needs.
+ *  - h_err: NULL, or a host int; when given, the call waits for the stream and
+ *    stores the tensor-core kernel's error code there (0 = finished). */
+B2E_API int b2e_linear_static(const void* x, int32_t x_dtype, int32_t m, int32_t k, const void* w,
+                              int32_t w_dtype, const void* bias, int32_t n, int32_t act, float* y,
+                              int32_t* h_err, void* stream);
+
 /* ---- one recurrent layer with its own state table ----
  * Weights are keyed like that layer's own state_dict() (no prefix). */
 B2E_API int b2e_layer_create(int32_t kind, const b2e_model_config* cfg, const b2e_engine_options* opt,
