@@ -16,6 +16,8 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libb2e.so"
 B2E_OK = 0
 DTYPES = {"fp32": 0, "bf16": 1, "fp16": 2}
 LAYER_KINDS = {"xlstm": 0, "mamba2": 1, "retnet": 2, "hawk": 3}
+FLAG_PDL = 1            # B2E_FLAG_PDL
+FLAG_NO_PRIORITIES = 2  # B2E_FLAG_NO_PRIORITIES
 
 
 class B2ELibraryError(RuntimeError):
@@ -39,7 +41,7 @@ class ModelConfigC(C.Structure):
 class EngineOptionsC(C.Structure):
     _fields_ = [("device", C.c_int32), ("linear_dtype", C.c_int32), ("capacity", C.c_int32),
                 ("max_batch", C.c_int32), ("use_graphs", C.c_int32), ("lanes", C.c_int32),
-                ("lane_min_rows", C.c_int32)]
+                ("lane_min_rows", C.c_int32), ("flags", C.c_int32)]
 
 
 class TensorC(C.Structure):

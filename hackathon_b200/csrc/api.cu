@@ -18,6 +18,7 @@ struct b2e_engine {
 struct b2e_layer {
   Dims d;
   int kind = 0, device = 0, capacity = 0, max_batch = 0, lp = 0;
+  bool pdl = true;
   WeightPack pack;
   StateArena arena;
   std::unique_ptr<Layer> layer;
@@ -76,6 +77,8 @@ EngineOptions to_opts(const b2e_engine_options* o) {
   e.graphs = o->use_graphs != 0;
   if (o->lanes > 0) e.lanes = o->lanes;
   if (o->lane_min_rows > 0) e.lane_min_rows = o->lane_min_rows;
+  e.pdl = (o->flags & B2E_FLAG_PDL) != 0;
+  e.priorities = !(o->flags & B2E_FLAG_NO_PRIORITIES);
   return e;
 }
 
@@ -315,6 +318,7 @@ int b2e_layer_create(int32_t kind, const b2e_model_config* cfg, const b2e_engine
     h->capacity = o.capacity;
     h->max_batch = o.max_batch;
     h->lp = o.lp;
+    h->pdl = o.pdl;
     B2E_CUDA(cudaSetDevice(o.device));
     gemm_tc_init();
     WeightSource src;
@@ -355,6 +359,7 @@ int b2e_layer_step_device(b2e_layer* l, const int32_t* d_slots, const float* d_x
     c.slots = d_slots;
     c.lp = h.lp;
     c.err = h.d_err;
+    c.ln.pdl = c.ln_bulk.pdl = h.pdl;
     h.layer->forward(c, d_x, nullptr, d_y, nullptr, h.scratch);
   });
 }

@@ -15,7 +15,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kMaxSh = 512;   // largest contracted/carried head axis kept in smem
 constexpr int kKT = 128;      // k-columns per CTA in outer_rows
-constexpr int kPart = 1024;   // partial-sum slots per CTA
 
 __device__ __forceinline__ int row_slot(const RowAddr& a, int row) { return a.slots ? a.slots[row] : row; }
 
@@ -28,6 +27,8 @@ __device__ __forceinline__ int row_slot(const RowAddr& a, int row) { return a.sl
 constexpr int U = 4;
 
 __global__ void __launch_bounds__(kThreads) outer_rows_kernel(const __grid_constant__ OuterRowsParams p, int HG) {
+  pdl_wait();
+  pdl_launch();
   const int row = blockIdx.z;
   if (row >= live_rows(p.at.n_dev, p.at.n_host)) return;
   const int h0 = blockIdx.y * HG;
@@ -129,6 +130,8 @@ __global__ void __launch_bounds__(kThreads) outer_rows_kernel(const __grid_const
 // item = one 16-byte vector (p, 4 state columns c); the contraction over c closes
 // inside the CTA. Same two-batch prefetch as outer_rows.
 __global__ void __launch_bounds__(kThreads) ssm_cols_kernel(const __grid_constant__ SsmColsParams p, int PT, int HG) {
+  pdl_wait();
+  pdl_launch();
   const int row = blockIdx.z;
   if (row >= live_rows(p.at.n_dev, p.at.n_host)) return;
   const int h0 = blockIdx.y * HG;
@@ -225,6 +228,8 @@ __global__ void __launch_bounds__(kThreads) ssm_cols_kernel(const __grid_constan
 // so y[p] = sum_c c[c]*H_new[p,c] closes with log2(LC) shuffles.
 template <int LC>
 __global__ void __launch_bounds__(kThreads, 4) ssm_cols_fast(const __grid_constant__ SsmColsParams p, int PT, int HG) {
+  pdl_wait();
+  pdl_launch();
   const int row = blockIdx.z;
   if (row >= live_rows(p.at.n_dev, p.at.n_host)) return;
   constexpr int RP = kThreads / LC;  // state rows in flight per pass
@@ -311,6 +316,8 @@ __global__ void __launch_bounds__(kThreads, 4) ssm_cols_fast(const __grid_consta
 // h = hr, hr+RH, ... of each head in the group; the sum over h closes in shared memory.
 template <int L>
 __global__ void __launch_bounds__(kThreads, 4) outer_rows_fast(const __grid_constant__ OuterRowsParams p, int HG) {
+  pdl_wait();
+  pdl_launch();
   const int row = blockIdx.z;
   if (row >= live_rows(p.at.n_dev, p.at.n_host)) return;
   constexpr int RH = kThreads / L, KW = 4 * L;
@@ -411,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 4) outer_rows_fast(const __grid_cons
 
 constexpr int kItems = 2048;  // 16-byte vectors per CTA (8 per thread)
 
-void outer_rows(const OuterRowsParams& p, int rows_max, cudaStream_t s) {
+void outer_rows(const OuterRowsParams& p, int rows_max, cudaStream_t s, const LaunchCfg& ln) {
   B2E_CHECK(p.sh > 0 && p.sh <= kMaxSh, kErrInvalid, "outer_rows: head size (contracted axis) must be in 1..512");
   B2E_CHECK(p.sk > 0 && p.sk % 4 == 0, kErrInvalid, "outer_rows: carried axis must be a multiple of 4");
   B2E_CHECK(p.nh > 0 && p.nh <= 65535 && rows_max <= 65535, kErrInvalid, "outer_rows: grid too large");
@@ -431,17 +438,17 @@ void outer_rows(const OuterRowsParams& p, int rows_max, cudaStream_t s) {
   dim3 grid(ceil_div(p.sk, kKT), ceil_div(p.nh, HG), rows_max);
   const bool tiles = p.sk % kt == 0;  // every tile full width
   if (tiles && kt == 128)
-    outer_rows_fast<32><<<grid, kThreads, smem, s>>>(p, HG);
+    launch_k(ln, outer_rows_fast<32>, grid, dim3(kThreads), smem, s, p, HG);
   else if (tiles && kt == 64)
-    outer_rows_fast<16><<<grid, kThreads, smem, s>>>(p, HG);
+    launch_k(ln, outer_rows_fast<16>, grid, dim3(kThreads), smem, s, p, HG);
   else if (tiles && kt == 32)
-    outer_rows_fast<8><<<grid, kThreads, smem, s>>>(p, HG);
+    launch_k(ln, outer_rows_fast<8>, grid, dim3(kThreads), smem, s, p, HG);
   else
-    outer_rows_kernel<<<grid, kThreads, smem, s>>>(p, HG);
+    launch_k(ln, outer_rows_kernel, grid, dim3(kThreads), smem, s, p, HG);
   B2E_CUDA(cudaGetLastError());
 }
 
-void ssm_cols(const SsmColsParams& p, int rows_max, cudaStream_t s) {
+void ssm_cols(const SsmColsParams& p, int rows_max, cudaStream_t s, const LaunchCfg& ln) {
   B2E_CHECK(p.sc > 0 && p.sc % 4 == 0 && p.sc <= 4096, kErrInvalid, "ssm_cols: state width must be a multiple of 4, <= 4096");
   B2E_CHECK(p.sh > 0 && p.nh > 0 && p.nh <= 65535 && rows_max <= 65535, kErrInvalid, "ssm_cols: bad sizes");
   B2E_CHECK((reinterpret_cast<uintptr_t>(p.at.state) & 15) == 0 && (p.at.row_stride & 3) == 0, kErrInvalid,
@@ -460,13 +467,13 @@ void ssm_cols(const SsmColsParams& p, int rows_max, cudaStream_t s) {
   const bool aligned_bc = (reinterpret_cast<uintptr_t>(p.b) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.c) & 15) == 0 &&
                           p.b_rs % 4 == 0 && p.c_rs % 4 == 0;
   if (aligned_bc && LC == 32)
-    ssm_cols_fast<32><<<grid, kThreads, smem, s>>>(p, PT, HG);
+    launch_k(ln, ssm_cols_fast<32>, grid, dim3(kThreads), smem, s, p, PT, HG);
   else if (aligned_bc && LC == 16)
-    ssm_cols_fast<16><<<grid, kThreads, smem, s>>>(p, PT, HG);
+    launch_k(ln, ssm_cols_fast<16>, grid, dim3(kThreads), smem, s, p, PT, HG);
   else if (aligned_bc && LC == 8)
-    ssm_cols_fast<8><<<grid, kThreads, smem, s>>>(p, PT, HG);
+    launch_k(ln, ssm_cols_fast<8>, grid, dim3(kThreads), smem, s, p, PT, HG);
   else
-    ssm_cols_kernel<<<grid, kThreads, smem, s>>>(p, PT, HG);
+    launch_k(ln, ssm_cols_kernel, grid, dim3(kThreads), smem, s, p, PT, HG);
   B2E_CUDA(cudaGetLastError());
 }
 

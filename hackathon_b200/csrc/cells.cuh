@@ -50,7 +50,7 @@ struct SsmColsParams {
   float* out = nullptr; int o_rs = 0;            // [row][nh*sh]
 };
 
-void outer_rows(const OuterRowsParams& p, int rows_max, cudaStream_t s);
-void ssm_cols(const SsmColsParams& p, int rows_max, cudaStream_t s);
+void outer_rows(const OuterRowsParams& p, int rows_max, cudaStream_t s, const LaunchCfg& ln = {});
+void ssm_cols(const SsmColsParams& p, int rows_max, cudaStream_t s, const LaunchCfg& ln = {});
 
 }  // namespace b2e

@@ -137,28 +137,51 @@ __device__ __forceinline__ void st_stream(float4* p, float4 v) { __stcs(p, v); }
 
 inline int ceil_div(long a, long b) { return int((a + b - 1) / b); }
 
-// ------------------------------------------- programmatic dependent launch
-// The kernels of a tower's chain are launched with programmatic stream
-// serialization: a kernel may start while its predecessor drains, run its
-// independent prologue (barrier set-up, weight or state prefetch), and waits in
-// pdl_wait() before it reads anything the predecessor wrote or writes anything
-// the predecessor may still read. pdl_wait is per thread. pdl_launch lets the
-// successor start as soon as every CTA of this grid is resident.
+// ------------------------------------------------------------ launches
+// The engine launches the kernels of a tower's chain with programmatic stream
+// serialization (PDL): a kernel may become resident while its predecessor in
+// the stream still runs, set up (barriers, tensor memory), and then waits in
+// pdl_wait() until the predecessor has completed and its writes are visible.
+// Every kernel calls pdl_wait() before its first global read other than weights,
+// and in every thread that reads or writes global memory, so a kernel's
+// completion also implies its predecessors' (the chain stays transitive);
+// pdl_launch() after the wait lets the successor start its own set-up. In a
+// kernel launched without the attribute both are no-ops.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// How a kernel is launched: plain (the C-ABI operators on a caller's stream), or
+// with PDL and a scheduling priority (the engine's chains: the HBM-streaming
+// state kernels run at low priority so that the short latency-bound kernels of
+// the other towers get SMs while they stream).
+struct LaunchCfg {
+  bool pdl = false;
+  bool set_prio = false;
+  int prio = 0;
+};
+
 template <typename... KArgs, typename... Args>
-inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+inline void launch_k(const LaunchCfg& L, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (L.pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (L.set_prio) {
+    attr[n].id = cudaLaunchAttributePriority;
+    attr[n].val.priority = L.prio;
+    ++n;
+  }
+  cfg.attrs = n ? attr : nullptr;
+  cfg.numAttrs = n;
   B2E_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 

@@ -138,6 +138,14 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   B2E_CUDA(cudaMemset(d_io_, 0, io));
   B2E_CUDA(cudaStreamCreateWithFlags(&s0_, cudaStreamNonBlocking));
   B2E_CUDA(cudaEventCreateWithFlags(&fork_, cudaEventDisableTiming));
+  int prio_low = 0, prio_high = 0;
+  B2E_CUDA(cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high));
+  ln_.pdl = ln_bulk_.pdl = o.pdl;
+  if (o.priorities && prio_high != prio_low) {
+    ln_.set_prio = ln_bulk_.set_prio = true;
+    ln_.prio = prio_high;
+    ln_bulk_.prio = prio_low;
+  }
   seen_.assign(o.capacity, 0);
 
   arena_.reset_all(s0_);
@@ -248,6 +256,8 @@ void Engine::enqueue(int rows, cudaStream_t s) {
       c.slots = d_slots_ + size_t(l) * per;
       c.lp = opt_.lp;
       c.err = d_err_;
+      c.ln = ln_;
+      c.ln_bulk = ln_bulk_;
       tower_forward(towers_[t], ch, t, c, d_feats_ + size_t(l) * per * d_.F, d_preds_ + size_t(l) * per * 4);
       B2E_CUDA(cudaEventRecord(ch.done, ch.s));
     }
@@ -275,7 +285,8 @@ void Engine::launch(int n, cudaStream_t s) {
     }
     B2E_CUDA(cudaStreamEndCapture(s0_, &g));
     cudaGraphExec_t ex = nullptr;
-    B2E_CUDA(cudaGraphInstantiate(&ex, g, 0));
+    // node priorities (the state kernels' low priority) only apply with this flag
+    B2E_CUDA(cudaGraphInstantiate(&ex, g, cudaGraphInstantiateFlagUseNodePriority));
     B2E_CUDA(cudaGraphDestroy(g));
     it = graphs_.emplace(rows, ex).first;
   }

@@ -16,6 +16,8 @@ struct EngineOptions {
   bool graphs = true;     // replay the step from a CUDA graph per batch bucket
   int lanes = 1;          // independent row shares per tower for batches of >= lane_min_rows
   int lane_min_rows = 256;
+  bool pdl = false;        // programmatic dependent launch inside each tower's chain
+  bool priorities = true;  // state-streaming kernels at low priority, the rest high
 };
 
 class Engine {
@@ -85,6 +87,7 @@ class Engine {
   std::vector<Tower> towers_;
   std::vector<Chain> chains_;  // [lane][tower]
   int* d_nl_ = nullptr;        // live rows per lane (device)
+  LaunchCfg ln_, ln_bulk_;     // chain kernels / state-streaming kernels
   size_t o_ow_ = 0, o_ob_ = 0;
   const float *ow_ = nullptr, *ob_ = nullptr;
 

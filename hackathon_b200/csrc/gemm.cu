@@ -75,6 +75,8 @@ __device__ __forceinline__ float epilogue(const GemmParams& p, const GemmGroup& 
 
 template <int AT, int WT>
 __global__ void __launch_bounds__(TPB) gemm_tiled(const __grid_constant__ GemmParams p, bool vec_a, bool vec_w) {
+  pdl_wait();
+  pdl_launch();
   const GemmGroup& g = p.g[blockIdx.z];
   const int M = live_rows(p.M_dev, p.M_max);
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
@@ -153,6 +155,8 @@ __global__ void __launch_bounds__(TPB) gemm_tiled(const __grid_constant__ GemmPa
 // One warp per output column; MM = accumulators per lane (>= live rows).
 template <int AT, int WT, int MM>
 __global__ void __launch_bounds__(256) gemm_skinny(const __grid_constant__ GemmParams p, bool vec) {
+  pdl_wait();
+  pdl_launch();
   const GemmGroup& g = p.g[blockIdx.y];
   const int M = min(live_rows(p.M_dev, p.M_max), MM);
   if (M <= 0) return;
@@ -230,6 +234,80 @@ __global__ void __launch_bounds__(256) gemm_skinny(const __grid_constant__ GemmP
   }
 }
 
+// fp32 projections with few outputs (N <= NN: Mamba2's dt_proj, the mLSTM
+// input/forget gate projections): one warp per kNarrowRows rows computes every
+// output; each lane accumulates its 4-wide K slices against all NN W rows (W
+// stays in L1; rows n >= N read row N-1 and are not stored), then a butterfly
+// sum closes the dot products across the warp. The next slice of A is loaded
+// while the current one is multiplied.
+constexpr int kNarrowRows = 2;
+
+template <int NN>
+__global__ void __launch_bounds__(256) gemm_narrow(const __grid_constant__ GemmParams p) {
+  pdl_wait();
+  pdl_launch();
+  const GemmGroup& g = p.g[0];
+  const int M = live_rows(p.M_dev, p.M_max);
+  const int lane = threadIdx.x & 31;
+  const int r0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kNarrowRows;
+  if (r0 >= M) return;  // warp-uniform
+  const float* A = static_cast<const float*>(g.A);
+  const float* W = static_cast<const float*>(g.W);
+  const float* arow[kNarrowRows];
+#pragma unroll
+  for (int i = 0; i < kNarrowRows; ++i) arow[i] = A + size_t(min(r0 + i, M - 1)) * p.lda;
+  const float* wrow[NN];
+#pragma unroll
+  for (int n = 0; n < NN; ++n) wrow[n] = W + size_t(min(n, p.N - 1)) * p.ldw;
+  float acc[kNarrowRows][NN];
+#pragma unroll
+  for (int i = 0; i < kNarrowRows; ++i)
+#pragma unroll
+    for (int n = 0; n < NN; ++n) acc[i][n] = 0.f;
+  int k = lane * 4;
+  float4 a[kNarrowRows];
+#pragma unroll
+  for (int i = 0; i < kNarrowRows; ++i)
+    a[i] = k < p.K ? *reinterpret_cast<const float4*>(arow[i] + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (; k < p.K; k += 128) {
+    float4 an[kNarrowRows];
+    const int kn = k + 128;
+#pragma unroll
+    for (int i = 0; i < kNarrowRows; ++i)
+      an[i] = kn < p.K ? *reinterpret_cast<const float4*>(arow[i] + kn) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int n = 0; n < NN; ++n) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(wrow[n] + k));
+#pragma unroll
+      for (int i = 0; i < kNarrowRows; ++i)
+        acc[i][n] = fmaf(a[i].w, w.w, fmaf(a[i].z, w.z, fmaf(a[i].y, w.y, fmaf(a[i].x, w.x, acc[i][n]))));
+    }
+#pragma unroll
+    for (int i = 0; i < kNarrowRows; ++i) a[i] = an[i];
+  }
+#pragma unroll
+  for (int i = 0; i < kNarrowRows; ++i)
+#pragma unroll
+    for (int n = 0; n < NN; ++n) acc[i][n] = warp_sum(acc[i][n]);
+  // lane (i * NN + n) % 32 writes output (row r0 + i, column n)
+#pragma unroll
+  for (int i = 0; i < kNarrowRows; ++i)
+#pragma unroll
+    for (int n = 0; n < NN; ++n) {
+      if ((i * NN + n) % 32 != lane || n >= p.N || r0 + i >= M) continue;
+      const int m = r0 + i;
+      const float v = epilogue<kF32>(p, g, acc[i][n], m, n);
+      if (g.C) g.C[size_t(m) * p.ldc + n] = v;
+      if (g.C_lp) store_as(kF32, g.C_lp, size_t(m) * p.ldc_lp + n, v);
+    }
+}
+
+bool narrow_eligible(const GemmParams& p) {
+  return p.groups == 1 && p.a_type == kF32 && p.w_type == kF32 && p.N <= 16 && p.M_max > 16 && p.K % 4 == 0 &&
+         p.lda % 4 == 0 && p.ldw % 4 == 0 && (reinterpret_cast<uintptr_t>(p.g[0].A) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(p.g[0].W) & 15) == 0;
+}
+
 bool aligned(const void* ptr, int bytes) { return (reinterpret_cast<uintptr_t>(ptr) % bytes) == 0; }
 
 int sm_count() {
@@ -259,18 +337,18 @@ void launch(const GemmParams& p, cudaStream_t s) {
     dim3 grid(blocks, p.groups);
     const bool vec = vec_a && vec_w;
     if (p.M_max <= 1)
-      gemm_skinny<AT, WT, 1><<<grid, 32 * warps, 0, s>>>(p, vec);
+      launch_k(p.ln, gemm_skinny<AT, WT, 1>, grid, dim3(32 * warps), 0, s, p, vec);
     else if (p.M_max <= 2)
-      gemm_skinny<AT, WT, 2><<<grid, 32 * warps, 0, s>>>(p, vec);
+      launch_k(p.ln, gemm_skinny<AT, WT, 2>, grid, dim3(32 * warps), 0, s, p, vec);
     else if (p.M_max <= 4)
-      gemm_skinny<AT, WT, 4><<<grid, 32 * warps, 0, s>>>(p, vec);
+      launch_k(p.ln, gemm_skinny<AT, WT, 4>, grid, dim3(32 * warps), 0, s, p, vec);
     else if (p.M_max <= 8)
-      gemm_skinny<AT, WT, 8><<<grid, 32 * warps, 0, s>>>(p, vec);
+      launch_k(p.ln, gemm_skinny<AT, WT, 8>, grid, dim3(32 * warps), 0, s, p, vec);
     else
-      gemm_skinny<AT, WT, 16><<<grid, 32 * warps, 0, s>>>(p, vec);
+      launch_k(p.ln, gemm_skinny<AT, WT, 16>, grid, dim3(32 * warps), 0, s, p, vec);
   } else {
     dim3 grid(ceil_div(p.N, BN), ceil_div(p.M_max, BM), p.groups);
-    gemm_tiled<AT, WT><<<grid, TPB, 0, s>>>(p, vec_a, vec_w);
+    launch_k(p.ln, gemm_tiled<AT, WT>, grid, dim3(TPB), 0, s, p, vec_a, vec_w);
   }
 }
 
@@ -282,6 +360,14 @@ void gemm(const GemmParams& p, cudaStream_t s) {
   B2E_CHECK(p.M_max <= 65535 * BM, kErrInternal, "gemm: too many rows");
   if (gemm_tc_eligible(p)) {
     gemm_tc(p, s);
+    return;
+  }
+  if (narrow_eligible(p)) {
+    const int blocks = ceil_div(p.M_max, 8 * kNarrowRows);
+    if (p.N <= 8)
+      launch_k(p.ln, gemm_narrow<8>, dim3(blocks), dim3(256), 0, s, p);
+    else
+      launch_k(p.ln, gemm_narrow<16>, dim3(blocks), dim3(256), 0, s, p);
     return;
   }
   const int a = p.a_type, w = p.w_type;

@@ -65,6 +65,7 @@ struct GemmParams {
   int act = kActNone;
   int* err = nullptr;  // device error word for bounded-wait timeouts (tensor-core path)
   RowEpi row;          // needs the tensor-core path and N <= 256 (gemm_tc_row_eligible)
+  LaunchCfg ln;        // plain launch by default; the engine's chains set PDL and priority
 };
 
 // Enqueue on `stream`. Picks, in order: the tcgen05 tensor-core kernel

@@ -1,21 +1,27 @@
 // tcgen05 (5th-generation tensor core) GEMM for the CastLinear projections.
 //
 // C[m, n] = epilogue( sum_k A[m, k] * W[n, k] ), A and W both bf16 (or both f16)
-// in global memory, f32 accumulation in tensor memory. One CTA computes one
-// 128 x BN output tile (BN = 128, or 256 so that a tile holds whole rows):
-//   warp 0     one thread issues TMA loads of A and W tiles (rows x 64 K,
-//              128-byte swizzle) into a 3-stage shared-memory ring;
-//   warp 1     allocates BN TMEM columns; one thread issues tcgen05.mma
-//              (M=128, N=BN, K=16 per instruction) and commits each stage back
-//              to the producer and the finished accumulator to the epilogue;
+// in global memory, f32 accumulation in tensor memory. The projections here are
+// skinny (a few thousand rows, N and K of a few hundred), so the tensor core
+// computes the transposed tile: its 128-wide M side runs over output features
+// (W rows) and its N side over BR activation rows. One CTA owns BR rows x NT*128
+// features, so a tile of whole rows (N <= 256) needs only BR = 32 rows and a
+// step of 4096 rows still spreads over 128 CTAs.
+//   warp 0     one thread issues TMA loads of the W tile (NT*128 rows x 64 K)
+//              and the A tile (BR rows x 64 K), 128-byte swizzle, into a
+//              3-stage shared-memory ring;
+//   warp 1     allocates NT*BR TMEM columns; one thread issues tcgen05.mma
+//              (M=128 features, N=BR rows, K=16 per instruction) per 128-feature
+//              half and commits each stage back to the producer and the finished
+//              accumulator to the epilogue;
 //   warps 2-5  epilogue, in two phases. Phase 1: each warp reads its 32-lane
-//              TMEM quadrant (one thread per row) with tcgen05.ld, applies bias,
-//              CastLinear rounding and activation, and stages the tile in the
-//              now idle operand ring. Phase 2: each warp takes whole rows (lane
-//              = 16-byte column unit) and writes them with row-contiguous
-//              stores, adding the residual; optional row work (RowEpi: LayerNorm,
-//              a second residual, the next RMSNorm, a dot product) runs here with
-//              warp-shuffle reductions.
+//              TMEM quadrant (one thread per feature, 32 rows per tcgen05.ld),
+//              applies bias, CastLinear rounding and activation, and stages the
+//              tile row-major in the now idle operand ring. Phase 2: each warp
+//              takes whole rows (lane = 16-byte column unit) and writes them with
+//              row-contiguous stores, adding the residual; optional row work
+//              (RowEpi: LayerNorm, a second residual, the next RMSNorm, a dot
+//              product) runs here with warp-shuffle reductions.
 // Every mbarrier wait is bounded: past ~1 s the kernel records an error code,
 // stops issuing work, waits (bounded) for what it issued, frees its TMEM and
 // returns. TMA loads here never use cluster multicast.
@@ -30,16 +36,26 @@
 namespace b2e {
 namespace {
 
-constexpr int BM = 128, BK = 64, STAGES = 3, THREADS = 192;
-constexpr uint32_t TILE_A = BM * BK * 2;
+constexpr int FT = 128, BK = 64;  // FT: features per MMA (its M)
+constexpr int kEpiWarps = 8, kEpiThreads = 32 * kEpiWarps;
+constexpr int THREADS = 64 + kEpiThreads;  // producer warp, MMA warp, epilogue warps
+constexpr int kMaxStages = 8;                    // ring depth is chosen per launch
+constexpr size_t kSmemBarriers = 1024 + 256;     // 1024-byte alignment slack + barriers
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
 
-template <int BN>
+template <int NT, int BR>
 struct Cfg {
-  static constexpr uint32_t TILE_B = BN * BK * 2;
-  static constexpr uint32_t TMEM_COLS = BN;
-  static constexpr size_t SMEM = size_t(STAGES) * (TILE_A + TILE_B) + 1024 + 256;
-  static_assert(size_t(BM) * BN * 4 <= size_t(STAGES) * (TILE_A + TILE_B), "epilogue stage must fit the ring");
+  static constexpr int NOUT = NT * FT;                   // features per CTA
+  static constexpr uint32_t TILE_W = NOUT * BK * 2;      // NT x 16 KB
+  static constexpr uint32_t TILE_X = BR * BK * 2;        // BR x 128 B
+  static constexpr uint32_t STAGE = TILE_W + TILE_X;     // multiple of 1024 (swizzle atoms)
+  static constexpr uint32_t TMEM_COLS = NT * BR;         // power of two >= 32
+  // the epilogue stages BR x NOUT floats in the ring
+  static constexpr int MIN_STAGES = (BR * NOUT * 4 + STAGE - 1) / STAGE > 2 ? (BR * NOUT * 4 + STAGE - 1) / STAGE : 2;
+  static_assert(STAGE % 1024 == 0, "stage bases must stay 1024-byte aligned");
+  static_assert(TMEM_COLS >= 32 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation is a power of two >= 32");
+  static_assert(MIN_STAGES <= kMaxStages, "epilogue stage must fit the ring");
+  static size_t smem(int stages) { return size_t(stages) * STAGE + kSmemBarriers; }
 };
 
 enum TcError : int { kTcTimeoutProducer = 101, kTcTimeoutMma = 102, kTcTimeoutEpilogue = 103 };
@@ -62,6 +78,7 @@ struct TcEpi {
   int vec;  // every row start of bias/R/C/C_lp (and RowEpi buffers) is 16-byte (f32) / 8-byte (low) aligned
   RowEpi row;
   int row_on;
+  int stages;  // ring depth, MIN_STAGES..kMaxStages
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -118,10 +135,11 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16: f32 accumulator, A/B type, both K-major.
-__host__ __device__ constexpr uint32_t instr_desc(int lp, int bn) {
+// Instruction descriptor, kind::f16: f32 accumulator, A/B type, both K-major,
+// M = FT (128) features, N = n rows.
+__host__ __device__ constexpr uint32_t instr_desc(int lp, int n) {
   const uint32_t ab = lp == kBF16 ? 1u : 0u;
-  return (1u << 4) | (ab << 7) | (ab << 10) | (uint32_t(bn >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+  return (1u << 4) | (ab << 7) | (ab << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(FT >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
@@ -199,30 +217,49 @@ __device__ __forceinline__ void store4_lp(int t, void* p, size_t i, float4 x) {
 __device__ __forceinline__ float4 f4add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
 __device__ __forceinline__ float f4sum(float4 a) { return (a.x + a.y) + (a.z + a.w); }
 
-template <int BN>
-__global__ void __launch_bounds__(THREADS, BN == 128 ? 2 : 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                   const __grid_constant__ TcEpi e) {
-  using K = Cfg<BN>;
-  constexpr int UPR = BN / 4;    // 16-byte units per tile row
-  constexpr int UPL = UPR / 32;  // units per lane in phase 2
-  const int M = live_rows(e.M_dev, e.M_max);
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  if (m0 >= M) return;  // whole CTA, before any barrier or TMEM use
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * TILE_A;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * K::TILE_B);
-  uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
+// Row work of the epilogue, fixed per instantiation so that each loop carries
+// only the instructions it needs (the epilogue is issue-latency bound: one or
+// two warps per SM sub-partition work through dependent chains).
+enum RowMode : int {
+  kRowPlain = 0,  // C / C_lp (+ R)
+  kRowNorm = 1,   // + RMSNorm -> T / T_lp
+  kRowLnNorm = 2, // + LayerNorm, + R2, then RMSNorm -> T / T_lp
+  kRowDot = 3,    // + dot product -> dot_out
+};
+
+int row_mode(const RowEpi& r) {
+  if (r.dot_w) return kRowDot;
+  if (r.ln_w) return kRowLnNorm;
+  if (r.norm_w) return kRowNorm;
+  return kRowPlain;
+}
+
+template <int NT, int BR, int MODE>
+__global__ void __launch_bounds__(THREADS)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const TcEpi e) {
+  using K = Cfg<NT, BR>;
+  constexpr int NOUT = K::NOUT;
+  constexpr int UPR = NOUT / 4;  // 16-byte units per tile row
+  constexpr int UPL = UPR / 32;  // units per lane in phase 2
+  const int m0 = blockIdx.y * BR, n0 = blockIdx.x * NOUT;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte aligned base by pointer arithmetic on the shared array, so the
+  // compiler keeps shared-space accesses (no generic loads and stores that it
+  // must order against the global stores of the epilogue)
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int S = e.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(S) * K::STAGE);
+  uint64_t* empty = full + S;
+  uint64_t* done = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  // Set-up that touches no global data: it overlaps the previous kernel's tail.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -230,6 +267,8 @@ __global__ void __launch_bounds__(THREADS, BN == 128 ? 2 : 1)
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -240,194 +279,244 @@ __global__ void __launch_bounds__(THREADS, BN == 128 ? 2 : 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  // TMEM is held from here on; the successor may start only after this point.
+  pdl_wait();
+  pdl_launch();
+  const int M = live_rows(e.M_dev, e.M_max);
+  const bool live = m0 < M;  // uniform over the CTA
   const int nkb = (e.K + BK - 1) / BK;
 
-  if (warp == 0) {
+  if (!live) {
+    // no rows: nothing issued, nothing to wait for
+  } else if (warp == 0) {
     if (lane == 0) {
       // ---- TMA producer
       int issued = 0;
       for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (kb >= STAGES && !mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+        const int s = kb % S;
+        const uint32_t ph = (kb / S) & 1;
+        if (kb >= S && !mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
           if (!*abort_flag) atomicExch(e.err, kTcTimeoutProducer);
           *abort_flag = 1;
           break;
         }
-        mbar_expect_tx(&full[s], TILE_A + K::TILE_B);
-        tma_load_2d(sA + s * TILE_A, &ta, kb * BK, m0, &full[s]);
-        tma_load_2d(sB + s * K::TILE_B, &tb, kb * BK, n0, &full[s]);
+        uint8_t* st = smem + s * K::STAGE;
+        mbar_expect_tx(&full[s], K::STAGE);
+        tma_load_2d(st, &tw, kb * BK, n0, &full[s]);
+        tma_load_2d(st + K::TILE_W, &tx, kb * BK, m0, &full[s]);
         ++issued;
       }
       if (*abort_flag) {
         // drain: every load issued lands before the CTA leaves (bounded)
         volatile int never = 0;
-        for (int kb = max(0, issued - STAGES); kb < issued; ++kb)
-          mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1, &never);
+        for (int kb = max(0, issued - S); kb < issued; ++kb)
+          mbar_wait(&full[kb % S], (kb / S) & 1, &never);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---- MMA issuer
-      const uint32_t idesc = instr_desc(e.lp, BN);
+      // ---- MMA issuer: D_h[f, r] += W[h*128 + f, k] * A[r, k]
+      const uint32_t idesc = instr_desc(e.lp, BR);
       for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
+        const int s = kb % S;
+        const uint32_t ph = (kb / S) & 1;
         if (!mbar_wait(&full[s], ph, abort_flag)) {
           if (!*abort_flag) atomicExch(e.err, kTcTimeoutMma);
           *abort_flag = 1;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a0 = smem_u32(sA + s * TILE_A), b0 = smem_u32(sB + s * K::TILE_B);
+        const uint32_t w0 = smem_u32(smem + s * K::STAGE), x0 = w0 + K::TILE_W;
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)  // K=16 per instruction: +32 bytes inside the swizzled row
-          mma_f16(tmem, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), idesc, (kb | k) != 0);
+        for (int h = 0; h < NT; ++h)
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)  // K=16 per instruction: +32 bytes inside the swizzled row
+            mma_f16(tmem + uint32_t(h * BR), smem_desc(w0 + h * FT * 128 + k * 32), smem_desc(x0 + k * 32), idesc,
+                    (kb | k) != 0);
         mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
       }
       mma_commit(done);  // accumulator complete (covers every MMA issued)
     }
   } else {
-    // ---- epilogue: warps 2..5, TMEM lane quadrant = warp % 4
+    // ---- epilogue: warps 2..9. TMEM lane quadrant q = warp % 4 (features
+    // q*32..q*32+31); the two warps of a quadrant split its 32-row chunks.
+    // While the main loop runs, load what the row pass needs besides the
+    // accumulator: this warp's first kPre rows of R (and R2), and the column
+    // weights of the row work.
+    constexpr int kPre = 4;
+    const int rows = min(BR, M - m0);
+    float4 pre_r[kPre][UPL], pre_r2[kPre][UPL], w_a[UPL], w_b[UPL];
+    if (e.vec) {
+      const float* R = e.R;
+      const float* R2 = MODE == kRowLnNorm ? e.row.R2 : nullptr;
+#pragma unroll
+      for (int u = 0; u < UPL; ++u) {
+        const int n = n0 + (lane + 32 * u) * 4;
+        const bool in = n < e.N;
+#pragma unroll
+        for (int b = 0; b < kPre; ++b) {
+          const int r = warp - 2 + kEpiWarps * b;
+          const bool ok_r = in && r < rows;
+          pre_r[b][u] = (ok_r && R) ? *reinterpret_cast<const float4*>(R + size_t(m0 + r) * e.ldr + n)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+          pre_r2[b][u] = (ok_r && R2) ? *reinterpret_cast<const float4*>(R2 + size_t(m0 + r) * e.row.ldr2 + n)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const float* wa = MODE == kRowLnNorm ? e.row.ln_w : MODE == kRowNorm ? e.row.norm_w : MODE == kRowDot ? e.row.dot_w : nullptr;
+        const float* wb = MODE == kRowLnNorm ? e.row.norm_w : nullptr;
+        w_a[u] = (in && wa) ? *reinterpret_cast<const float4*>(wa + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+        w_b[u] = (in && wb) ? *reinterpret_cast<const float4*>(wb + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
     volatile int never = 0;  // the MMA thread always commits `done`, even after an abort
     const bool ok = mbar_wait(done, 0, &never);
     if (!ok) {
       atomicExch(e.err, kTcTimeoutEpilogue);
       *abort_flag = 1;
     }
-    // Both named barriers below are reached by all four epilogue warps whatever
+    // Both named barriers below are reached by all eight epilogue warps whatever
     // happens, so an error path cannot leave a warp waiting; `go` is read once.
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
     const bool go = ok && !*abort_flag;
-    const int q = warp & 3;
-    const int m = m0 + q * 32 + lane;
-    const bool row_ok = m < M;
+    const int q = warp & 3, half = (warp - 2) >> 2;
     if (go) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (e.vec) {
-      // Phase 1: bias, rounding, activation per column; tile to shared memory
-      // (the operand ring is idle once `done` fired). 16-byte unit u of tile row
-      // r lives at unit u ^ (r & 7): the 32 rows a warp writes fall in distinct
-      // bank groups.
-      float4* stage = reinterpret_cast<float4*>(sA);  // BM x BN floats
-      for (int c0 = 0; go && c0 < BN; c0 += 32) {
-        if (n0 + c0 >= e.N) break;  // warp-uniform
-        float v[32];
-        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
-        const int nb = n0 + c0;
-        const int r = q * 32 + lane;
+    // Phase 1: per feature (this thread's TMEM lane) bias, rounding, activation;
+    // the tile goes to shared memory row-major (BR x NOUT floats; the operand
+    // ring is idle once `done` fired). For a fixed row the 32 lanes write 32
+    // consecutive floats: no bank conflicts.
+    float* stage = reinterpret_cast<float*>(smem);
+    constexpr int CH = BR / 32;  // 32-row chunks per 128-feature half
+#pragma unroll 1
+    for (int k = half; k < NT * CH; k += 2) {
+      const int h = k / CH, c = (k % CH) * 32;
+      const int fb = h * FT + q * 32;
+      if (!go || n0 + fb >= e.N) continue;  // warp-uniform
+      const int n = n0 + fb + lane;
+      const float b = (e.bias && n < e.N) ? load_as(e.bias_type, e.bias, n) : 0.0f;
+      float v[32];
+      tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(h * BR + c), v);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          if (e.bias && nb + j < e.N) x = f4add(x, load4(e.bias_type, e.bias, nb + j));
-          if (e.round_out) x = round4_lp(e.lp, x);
-          if (e.act == kActRelu) {
-            x.x = fmaxf(x.x, 0.f); x.y = fmaxf(x.y, 0.f); x.z = fmaxf(x.z, 0.f); x.w = fmaxf(x.w, 0.f);
-          }
-          const int unit = (c0 + j) >> 2;
-          stage[r * UPR + (unit ^ (r & 7))] = x;
+      for (int j = 0; j < 32; j += 4) {
+        float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        if (e.bias) x = make_float4(x.x + b, x.y + b, x.z + b, x.w + b);
+        if (e.round_out) x = round4_lp(e.lp, x);
+        if (e.act == kActRelu) {
+          x.x = fmaxf(x.x, 0.f); x.y = fmaxf(x.y, 0.f); x.z = fmaxf(x.z, 0.f); x.w = fmaxf(x.w, 0.f);
         }
+        float* col = stage + size_t(c + j) * NOUT + fb + lane;
+        col[0] = x.x;
+        col[NOUT] = x.y;
+        col[2 * NOUT] = x.z;
+        col[3 * NOUT] = x.w;
       }
-      // Phase 2: whole rows per warp; lane l owns units l, l+32, ... of a row.
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      const RowEpi& re = e.row;
-      for (int r = warp - 2; go && r < BM; r += 4) {
-        const int mm = m0 + r;
-        if (mm >= M) break;  // rows only grow
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+    // Phase 2: whole rows per warp (rows warp-2, warp+6, ...); lane l owns
+    // 16-byte units l, l+32, ... of a row.
+    const float4* stage4 = reinterpret_cast<const float4*>(smem);
+    if (go && e.vec) {
+      const float* R = e.R;
+      float* C = e.C;
+      void* C_lp = e.C_lp;
+      const int ldr = e.ldr, ldc = e.ldc, ldc_lp = e.ldc_lp, N = e.N, lp = e.lp;
+      const float invN = 1.0f / float(N);
+      const RowEpi re = e.row;
+      // One row: x = staged + R, row work, stores. rr/rr2: R and R2 of the row.
+      auto row = [&](int r, const float4 (&rr)[UPL], const float4 (&rr2)[UPL]) {
+        const size_t mm = size_t(m0 + r);
         float4 x[UPL];
         bool in[UPL];
 #pragma unroll
         for (int u = 0; u < UPL; ++u) {
           const int unit = lane + 32 * u;
-          const int n = n0 + unit * 4;
-          in[u] = n < e.N;
-          x[u] = in[u] ? stage[r * UPR + (unit ^ (r & 7))] : make_float4(0.f, 0.f, 0.f, 0.f);
-          if (in[u] && e.R) x[u] = f4add(x[u], *reinterpret_cast<const float4*>(e.R + size_t(mm) * e.ldr + n));
+          in[u] = n0 + unit * 4 < N;
+          x[u] = in[u] ? f4add(stage4[r * UPR + unit], rr[u]) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        if (e.row_on) {
-          const float invN = 1.0f / float(e.N);
-          if (re.ln_w) {  // LayerNorm(bias=False): two-pass mean and biased variance
-            float s = 0.f;
+        if constexpr (MODE == kRowLnNorm) {
+          // LayerNorm(bias=False): two-pass mean and biased variance, then + R2
+          float sm = 0.f;
 #pragma unroll
-            for (int u = 0; u < UPL; ++u) s += f4sum(x[u]);
-            const float mu = warp_sum(s) * invN;
-            float q2 = 0.f;
+          for (int u = 0; u < UPL; ++u) sm += f4sum(x[u]);
+          const float mu = warp_sum(sm) * invN;
+          float q2 = 0.f;
 #pragma unroll
-            for (int u = 0; u < UPL; ++u)
-              if (in[u]) {
-                const float4 d = make_float4(x[u].x - mu, x[u].y - mu, x[u].z - mu, x[u].w - mu);
-                q2 += f4sum(make_float4(d.x * d.x, d.y * d.y, d.z * d.z, d.w * d.w));
-              }
-            const float rs = 1.0f / sqrtf(warp_sum(q2) * invN + re.ln_eps);
+          for (int u = 0; u < UPL; ++u)
+            if (in[u]) {
+              const float4 d = make_float4(x[u].x - mu, x[u].y - mu, x[u].z - mu, x[u].w - mu);
+              q2 += f4sum(make_float4(d.x * d.x, d.y * d.y, d.z * d.z, d.w * d.w));
+            }
+          const float rs = 1.0f / sqrtf(warp_sum(q2) * invN + re.ln_eps);
 #pragma unroll
-            for (int u = 0; u < UPL; ++u)
-              if (in[u]) {
-                const int n = n0 + (lane + 32 * u) * 4;
-                const float4 w = *reinterpret_cast<const float4*>(re.ln_w + n);
-                x[u] = make_float4((x[u].x - mu) * rs * w.x, (x[u].y - mu) * rs * w.y, (x[u].z - mu) * rs * w.z,
-                                   (x[u].w - mu) * rs * w.w);
-              }
-          }
-          if (re.R2) {
-#pragma unroll
-            for (int u = 0; u < UPL; ++u)
-              if (in[u])
-                x[u] = f4add(x[u], *reinterpret_cast<const float4*>(re.R2 + size_t(mm) * re.ldr2 + n0 + (lane + 32 * u) * 4));
-          }
+          for (int u = 0; u < UPL; ++u)
+            if (in[u]) {
+              const float4 w = w_a[u];
+              x[u] = f4add(make_float4((x[u].x - mu) * rs * w.x, (x[u].y - mu) * rs * w.y, (x[u].z - mu) * rs * w.z,
+                                       (x[u].w - mu) * rs * w.w), rr2[u]);
+            }
         }
 #pragma unroll
         for (int u = 0; u < UPL; ++u)
           if (in[u]) {
             const int n = n0 + (lane + 32 * u) * 4;
-            if (e.C) *reinterpret_cast<float4*>(e.C + size_t(mm) * e.ldc + n) = x[u];
-            if (e.C_lp) store4_lp(e.lp, e.C_lp, size_t(mm) * e.ldc_lp + n, x[u]);
+            if (C) *reinterpret_cast<float4*>(C + mm * ldc + n) = x[u];
+            if (C_lp) store4_lp(lp, C_lp, mm * ldc_lp + n, x[u]);
           }
-        if (e.row_on && re.norm_w) {  // nn.RMSNorm of the finished row
+        if constexpr (MODE == kRowNorm || MODE == kRowLnNorm) {  // nn.RMSNorm of the finished row
           float ss = 0.f;
 #pragma unroll
           for (int u = 0; u < UPL; ++u)
             ss += f4sum(make_float4(x[u].x * x[u].x, x[u].y * x[u].y, x[u].z * x[u].z, x[u].w * x[u].w));
-          const float inv = 1.0f / sqrtf(warp_sum(ss) * (1.0f / float(e.N)) + re.norm_eps);
+          const float inv = 1.0f / sqrtf(warp_sum(ss) * invN + re.norm_eps);
 #pragma unroll
           for (int u = 0; u < UPL; ++u)
             if (in[u]) {
               const int n = n0 + (lane + 32 * u) * 4;
-              const float4 w = *reinterpret_cast<const float4*>(re.norm_w + n);
+              const float4 w = MODE == kRowLnNorm ? w_b[u] : w_a[u];
               const float4 t = make_float4(x[u].x * inv * w.x, x[u].y * inv * w.y, x[u].z * inv * w.z, x[u].w * inv * w.w);
-              if (re.T) *reinterpret_cast<float4*>(re.T + size_t(mm) * re.ldt + n) = t;
-              if (re.T_lp) store4_lp(e.lp, re.T_lp, size_t(mm) * re.ldt + n, t);
+              if (re.T) *reinterpret_cast<float4*>(re.T + mm * re.ldt + n) = t;
+              if (re.T_lp) store4_lp(lp, re.T_lp, mm * re.ldt + n, t);
             }
         }
-        if (e.row_on && re.dot_w) {  // output_proj: v . w + b
+        if constexpr (MODE == kRowDot) {  // output_proj: v . w + b
           float d = 0.f;
 #pragma unroll
           for (int u = 0; u < UPL; ++u)
-            if (in[u]) {
-              const float4 w = *reinterpret_cast<const float4*>(re.dot_w + n0 + (lane + 32 * u) * 4);
-              d += f4sum(make_float4(x[u].x * w.x, x[u].y * w.y, x[u].z * w.z, x[u].w * w.w));
-            }
+            if (in[u]) d += f4sum(make_float4(x[u].x * w_a[u].x, x[u].y * w_a[u].y, x[u].z * w_a[u].z, x[u].w * w_a[u].w));
           d = warp_sum(d);
-          if (lane == 0) re.dot_out[size_t(mm) * re.dot_ld + re.dot_col] = d + re.dot_b[0];
+          if (lane == 0) re.dot_out[mm * re.dot_ld + re.dot_col] = d + re.dot_b[0];
         }
-      }
-    } else {
-      for (int c0 = 0; go && c0 < BN; c0 += 32) {
-        if (n0 + c0 >= e.N) break;  // warp-uniform
-        float v[32];
-        tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
-        if (!row_ok) continue;
-        const int nb = n0 + c0;
+      };
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int n = nb + j;
-          if (n >= e.N) continue;
-          float x = v[j];
-          if (e.bias) x += load_as(e.bias_type, e.bias, n);
-          if (e.round_out) x = round_to(e.lp, x);
-          if (e.act == kActRelu) x = fmaxf(x, 0.0f);
-          if (e.R) x += e.R[size_t(m) * e.ldr + n];
-          if (e.C) e.C[size_t(m) * e.ldc + n] = x;
-          if (e.C_lp) store_as(e.lp, e.C_lp, size_t(m) * e.ldc_lp + n, x);
+      for (int b = 0; b < kPre; ++b) {
+        const int r = warp - 2 + kEpiWarps * b;
+        if (r < rows) row(r, pre_r[b], pre_r2[b]);
+      }
+      for (int r = warp - 2 + kEpiWarps * kPre; r < rows; r += kEpiWarps) {
+        float4 rr[UPL], rr2[UPL];
+#pragma unroll
+        for (int u = 0; u < UPL; ++u) {
+          const int n = n0 + (lane + 32 * u) * 4;
+          const bool in = n < N;
+          rr[u] = (in && R) ? *reinterpret_cast<const float4*>(R + size_t(m0 + r) * ldr + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+          rr2[u] = (in && MODE == kRowLnNorm && re.R2)
+                       ? *reinterpret_cast<const float4*>(re.R2 + size_t(m0 + r) * re.ldr2 + n)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        row(r, rr, rr2);
+      }
+    } else if (go) {
+      // unaligned rows (plain epilogue only: row work needs aligned rows)
+      for (int r = warp - 2; r < rows; r += kEpiWarps) {
+        const int mm = m0 + r;
+        for (int u = 0; u < UPL; ++u)
+          for (int i = 0; i < 4; ++i) {
+            const int f = (lane + 32 * u) * 4 + i, n = n0 + f;
+            if (n >= e.N) continue;
+            float x = stage[size_t(r) * NOUT + f];
+            if (e.R) x += e.R[size_t(mm) * e.ldr + n];
+            if (e.C) e.C[size_t(mm) * e.ldc + n] = x;
+            if (e.C_lp) store_as(e.lp, e.C_lp, size_t(mm) * e.ldc_lp + n, x);
+          }
       }
     }
   }
@@ -471,17 +560,69 @@ void make_map(CUtensorMap* m, const void* base, int lp, uint64_t inner, uint64_t
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
 
-template <int BN>
-void launch_tc(const GemmParams& p, bool vec, cudaStream_t s) {
-  CUtensorMap ta, tb;
-  make_map(&ta, p.g[0].A, p.w_type, uint64_t(p.K), uint64_t(p.M_max), uint64_t(p.lda), BM);
-  make_map(&tb, p.g[0].W, p.w_type, uint64_t(p.K), uint64_t(p.N), uint64_t(p.ldw), BN);
+constexpr size_t kSmemPerSm = 228 * 1024;   // shared memory of one SM
+constexpr size_t kSmemPerCta = 227 * 1024;  // largest dynamic allocation of one CTA
+constexpr size_t kSmemReserved = 1024;      // the system's share of each resident CTA
+
+// One candidate tile shape: CTAs, resident CTAs per SM, ring depth, and a cost
+// estimate in microseconds: each wave pays a fixed latency (TMA round trips,
+// epilogue, launch), and each SM moves its CTAs' operand and output bytes.
+struct TilePlan {
+  int nt = 0, br = 0, stages = 0;
+  double cost = 1e30;
+};
+
+template <int NT, int BR>
+void plan(const GemmParams& p, TilePlan& best) {
+  using K = Cfg<NT, BR>;
+  const long ctas = long(ceil_div(p.N, K::NOUT)) * ceil_div(p.M_max, BR);
+  const int nkb = ceil_div(p.K, BK);
+  const int cap = std::min(kMaxStages, std::max(nkb, K::MIN_STAGES));
+  for (int occ = 3; occ >= 1; --occ) {
+    const size_t per_cta = std::min(kSmemPerCta, kSmemPerSm / occ - kSmemReserved);
+    if (per_cta < K::smem(K::MIN_STAGES)) continue;
+    const int st = std::min<int>(cap, int((per_cta - kSmemBarriers) / K::STAGE));
+    if (occ > 1 && ctas <= 148L * (occ - 1)) continue;  // fewer CTAs per SM suffice: keep the deeper ring
+    const long waves = (ctas + 148L * occ - 1) / (148L * occ);
+    const long per_sm = (ctas + 147) / 148;
+    const double bytes = double(nkb) * K::STAGE + double(BR) * K::NOUT * 4;
+    const double cost = 3.0 * waves + per_sm * bytes / 150e3;  // 150 GB/s per SM, in us
+    if (cost < best.cost) best = {NT, BR, st, cost};
+    return;
+  }
+}
+
+template <int NT, int BR, int MODE>
+void launch_tc(const GemmParams& p, bool vec, int stages, cudaStream_t s) {
+  using K = Cfg<NT, BR>;
+  CUtensorMap tw, tx;
+  make_map(&tw, p.g[0].W, p.w_type, uint64_t(p.K), uint64_t(p.N), uint64_t(p.ldw), K::NOUT);
+  make_map(&tx, p.g[0].A, p.w_type, uint64_t(p.K), uint64_t(p.M_max), uint64_t(p.lda), BR);
   const GemmGroup& g = p.g[0];
   TcEpi e{g.bias, p.bias_type, g.C, p.ldc, g.C_lp, p.ldc_lp, g.R, p.ldr, p.M_max, p.M_dev,
-          p.N, p.K, p.w_type, p.round_out, p.act, p.err, vec ? 1 : 0, p.row, p.row.active() ? 1 : 0};
-  dim3 grid(ceil_div(p.N, BN), ceil_div(p.M_max, BM));
-  gemm_tc_kernel<BN><<<grid, THREADS, Cfg<BN>::SMEM, s>>>(ta, tb, e);
-  B2E_CUDA(cudaGetLastError());
+          p.N, p.K, p.w_type, p.round_out, p.act, p.err, vec ? 1 : 0, p.row, p.row.active() ? 1 : 0, stages};
+  dim3 grid(ceil_div(p.N, K::NOUT), ceil_div(p.M_max, BR));
+  launch_k(p.ln, gemm_tc_kernel<NT, BR, MODE>, grid, dim3(THREADS), K::smem(stages), s, tw, tx, e);
+}
+
+template <int NT, int BR>
+void launch_mode(const GemmParams& p, bool vec, int stages, cudaStream_t s) {
+  switch (row_mode(p.row)) {
+    case kRowNorm: return launch_tc<NT, BR, kRowNorm>(p, vec, stages, s);
+    case kRowLnNorm: return launch_tc<NT, BR, kRowLnNorm>(p, vec, stages, s);
+    case kRowDot: return launch_tc<NT, BR, kRowDot>(p, vec, stages, s);
+    default: return launch_tc<NT, BR, kRowPlain>(p, vec, stages, s);
+  }
+}
+
+template <int NT>
+void launch_nt(const GemmParams& p, bool vec, const TilePlan& t, cudaStream_t s) {
+  if (t.br == 128)
+    launch_mode<NT, 128>(p, vec, t.stages, s);
+  else if (t.br == 64)
+    launch_mode<NT, 64>(p, vec, t.stages, s);
+  else
+    launch_mode<NT, 32>(p, vec, t.stages, s);
 }
 
 bool row_buffers_ok(const GemmParams& p) {
@@ -489,14 +630,34 @@ bool row_buffers_ok(const GemmParams& p) {
   return (!r.ln_w || aligned16(r.ln_w)) && (!r.R2 || (aligned16(r.R2) && r.ldr2 % 4 == 0)) &&
          (!r.norm_w || aligned16(r.norm_w)) && (!r.T || (aligned16(r.T) && r.ldt % 4 == 0)) &&
          (!r.T_lp || (aligned8(r.T_lp) && r.ldt % 4 == 0)) &&
-         (!r.dot_w || (aligned16(r.dot_w) && r.dot_b && r.dot_out));
+         (!r.dot_w || (aligned16(r.dot_w) && r.dot_b && r.dot_out)) &&
+         (!r.ln_w || r.norm_w) && (!r.R2 || r.ln_w);  // LayerNorm (+R2) runs only ahead of an RMSNorm
+}
+
+template <int NT, int BR, int MODE>
+void set_smem1() {
+  using K = Cfg<NT, BR>;
+  const size_t mx = std::min(kSmemPerCta, K::smem(kMaxStages));
+  B2E_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<NT, BR, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(mx)));
+}
+
+template <int NT, int BR>
+void set_smem() {
+  set_smem1<NT, BR, kRowPlain>();
+  set_smem1<NT, BR, kRowNorm>();
+  set_smem1<NT, BR, kRowLnNorm>();
+  set_smem1<NT, BR, kRowDot>();
 }
 
 }  // namespace
 
 void gemm_tc_init() {
-  B2E_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg<128>::SMEM)));
-  B2E_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg<256>::SMEM)));
+  set_smem<1, 32>();
+  set_smem<1, 64>();
+  set_smem<1, 128>();
+  set_smem<2, 32>();
+  set_smem<2, 64>();
+  set_smem<2, 128>();
 }
 
 bool gemm_tc_eligible(const GemmParams& p) {
@@ -515,12 +676,26 @@ void gemm_tc(const GemmParams& p, cudaStream_t s) {
   const bool vec = p.N % 4 == 0 && (!g.bias || aligned16(g.bias)) && (!g.C || (aligned16(g.C) && p.ldc % 4 == 0)) &&
                    (!g.R || (aligned16(g.R) && p.ldr % 4 == 0)) &&
                    (!g.C_lp || (aligned8(g.C_lp) && p.ldc_lp % 4 == 0));
-  if (p.row.active()) {
-    B2E_CHECK(gemm_tc_row_eligible(p) && vec, kErrInternal, "gemm_tc: row epilogue needs N <= 256 and aligned rows");
-    launch_tc<256>(p, vec, s);
-  } else {
-    launch_tc<128>(p, vec, s);
+  // A row epilogue needs whole rows in one CTA: 128 features for N <= 128,
+  // else 256. Otherwise every shape competes on the cost estimate.
+  const bool row = p.row.active();
+  if (row) B2E_CHECK(gemm_tc_row_eligible(p) && vec, kErrInternal, "gemm_tc: row epilogue needs N <= 256 and aligned rows");
+  TilePlan t;
+  if (!row || p.N <= FT) {
+    plan<1, 32>(p, t);
+    plan<1, 64>(p, t);
+    plan<1, 128>(p, t);
   }
+  if (!row || p.N > FT) {
+    plan<2, 32>(p, t);
+    plan<2, 64>(p, t);
+    plan<2, 128>(p, t);
+  }
+  B2E_CHECK(t.nt != 0, kErrInternal, "gemm_tc: no tile shape fits");
+  if (t.nt == 2)
+    launch_nt<2>(p, vec, t, s);
+  else
+    launch_nt<1>(p, vec, t, s);
 }
 
 }  // namespace b2e

@@ -100,6 +100,8 @@ struct RmsP {
 constexpr int kRowsPerCta = 8;
 
 __global__ void __launch_bounds__(256) k_rmsnorm(const RmsP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (!row_live(p.rc, r)) return;
@@ -132,6 +134,8 @@ struct OutP {
   const float* x; const float* w; const float* b; int H; float* preds; int ld; int col;
 };
 __global__ void __launch_bounds__(256) k_output_proj(const OutP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (!row_live(p.rc, r)) return;
@@ -160,6 +164,8 @@ struct Mamba2PreP {
   float *xs, *bs, *cs, *dt, *dc;
 };
 __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre(const Mamba2PreP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   const long long slot = row_slot(p.rc, r);
@@ -188,6 +194,8 @@ struct Mamba2PostP {
   const float* d; const float* nw; void* A; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_mamba2_post(const Mamba2PostP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float g[];
@@ -276,15 +284,15 @@ class Mamba2Layer : public Layer {
     linear(c, in, kF32, H_, dtw_, kF32, dtb_, nh_, H_, b.dtp, nh_);   // dt_proj, fp32 kept (mamba2.py:81)
     Mamba2PreP pp{rc, b.proj, n1_, mi_, bc_, nh_, b.dtp, xc_, sxc_, bcs_, sbc_, ccs_, scc_,
                   wx_, bx_, wb_, bb_, wc_, bcv_, a_, b.xs, b.bs, b.cs, b.dt, b.dc};
-    k_mamba2_pre<<<c.rows, kRowThreads, 0, c.s>>>(pp);
+    launch_k(c.ln, k_mamba2_pre, dim3(c.rows), dim3(kRowThreads), 0, c.s, pp);
     SsmColsParams sp;
     sp.at = {ssm_, sssm_, c.slots, nullptr, c.rows, c.n_dev};
     sp.nh = nh_; sp.sh = hs_; sp.sc = bc_;
     sp.x = b.xs; sp.x_rs = mi_; sp.b = b.bs; sp.b_rs = bc_; sp.c = b.cs; sp.c_rs = bc_;
     sp.dt = b.dt; sp.dt_rs = nh_; sp.decay = b.dc; sp.dc_rs = nh_; sp.out = b.ys; sp.o_rs = mi_;
-    ssm_cols(sp, c.rows, c.s);
+    ssm_cols(sp, c.rows, c.s, c.ln_bulk);
     Mamba2PostP po{rc, b.ys, b.xs, b.proj, n1_, mi_, hs_, dd_, nw_, b.A, lp_};
-    k_mamba2_post<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(po);
+    launch_k(c.ln, k_mamba2_post, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, po);
     linear(c, b.A, lp_, mi_, out_, lp_, nullptr, H_, mi_, out, H_, kActNone, residual, H_, nullptr, 0, post);  // out_proj (mamba2.py:165)
     B2E_CUDA(cudaGetLastError());
   }
@@ -312,6 +320,8 @@ struct RetPreP {
   float* kr; float* qs;
 };
 __global__ void __launch_bounds__(kRowThreads) k_retnet_pre(const RetPreP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   const long long slot = row_slot(p.rc, r);
@@ -344,6 +354,8 @@ struct RetPostP {
   const float* o; const float* proj; int H, nh, hs; void* A; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_retnet_post(const RetPostP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float inv[];  // per head
@@ -405,16 +417,16 @@ class RetNetLayer : public Layer {
     linear(c, in_lp ? in_lp : in, in_lp ? lp_ : kF32, H_, w1_, lp_, nullptr, 4 * H_, H_, b.proj, 4 * H_);  // q, k, v, g (retnet.py:66-69)
     RetPreP pp{rc, b.proj, H_, nh_, hs_, pos_, spos_, sc_, ssc_, angle_, decay_,
                float(std::pow(double(hs_), -0.5)), b.kr, b.qs};
-    k_retnet_pre<<<c.rows, kRowThreads, 0, c.s>>>(pp);
+    launch_k(c.ln, k_retnet_pre, dim3(c.rows), dim3(kRowThreads), 0, c.s, pp);
     OuterRowsParams op;
     op.at = {S_, sS_, c.slots, nullptr, c.rows, c.n_dev};
     op.nh = nh_; op.sh = hs_; op.sk = hs_;
     op.f = decay_; op.f_rs = 0; op.f_hs = 1;
     op.kv = b.kr; op.k_rs = H_; op.v = b.proj + 2 * H_; op.v_rs = 4 * H_;
     op.q = b.qs; op.q_rs = H_; op.out = b.o; op.o_rs = H_;
-    outer_rows(op, c.rows, c.s);
+    outer_rows(op, c.rows, c.s, c.ln_bulk);
     RetPostP po{rc, b.o, b.proj, H_, nh_, hs_, b.A, lp_};
-    k_retnet_post<<<c.rows, kRowThreads, nh_ * sizeof(float), c.s>>>(po);
+    launch_k(c.ln, k_retnet_post, dim3(c.rows), dim3(kRowThreads), nh_ * sizeof(float), c.s, po);
     linear(c, b.A, lp_, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_, nullptr, 0, post);  // out_proj (retnet.py:170)
     B2E_CUDA(cudaGetLastError());
   }
@@ -441,6 +453,8 @@ struct HawkConvP {
   float* conv; long long cs; const float* w; const float* b; float* xc;
 };
 __global__ void __launch_bounds__(kRowThreads) k_hawk_conv(const HawkConvP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   float* st = p.conv + row_slot(p.rc, r) * p.cs;
@@ -455,6 +469,8 @@ struct RglruP {
   float* h; long long hs; const float* a; void* A; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_rglru(const RglruP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   float* h = p.h + row_slot(p.rc, r) * p.hs;
@@ -515,7 +531,7 @@ class HawkLayer : public Layer {
     const RowCtx rc{c.n_dev, c.rows, c.slots};
     linear(c, in_lp ? in_lp : in, in_lp ? lp_ : kF32, H_, w1_, lp_, nullptr, 2 * H_, H_, b.proj, 2 * H_);  // gate_proj, recurrent_proj (hawk.py:77-78)
     HawkConvP cp{rc, b.proj, H_, conv_, sconv_, cw_, cb_, b.xc};
-    k_hawk_conv<<<c.rows, kRowThreads, 0, c.s>>>(cp);
+    launch_k(c.ln, k_hawk_conv, dim3(c.rows), dim3(kRowThreads), 0, c.s, cp);
     // RG-LRU gates: two BlockLinears of 4 diagonal blocks, fp32 (hawk.py:31-32, modules.py:71-79)
     GemmParams g;
     g.groups = 8;
@@ -530,7 +546,7 @@ class HawkLayer : public Layer {
     g.lda = H_; g.ldw = bs_; g.ldc = 2 * H_;
     gemm(g, c.s);
     RglruP rp{rc, b.gates, b.xc, b.proj, H_, h_, sh_, a_, b.A, lp_};
-    k_rglru<<<c.rows, kRowThreads, 0, c.s>>>(rp);
+    launch_k(c.ln, k_rglru, dim3(c.rows), dim3(kRowThreads), 0, c.s, rp);
     linear(c, b.A, lp_, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_, nullptr, 0, post);  // out_proj (hawk.py:84)
     B2E_CUDA(cudaGetLastError());
   }
@@ -559,6 +575,8 @@ struct SlstmPreP {
   float* axc; float* axn;  // [row][2H]: per block j, [input_j | h_j]
 };
 __global__ void __launch_bounds__(kRowThreads) k_slstm_pre(const SlstmPreP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float xn[];
@@ -592,6 +610,8 @@ struct SlstmPostP {
   float* x1; void* xn2; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float sm[];
@@ -642,6 +662,8 @@ struct MlstmPreP {
   float* xca; float* qkv;     // [row][mi], [row][3mi] = [q | k | v]
 };
 __global__ void __launch_bounds__(kRowThreads) k_mlstm_pre(const MlstmPreP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float xs[];  // conv+silu output (mi)
@@ -682,6 +704,8 @@ struct MlstmGatesP {
   float* g2; float* den;  // g2 row: [i (nh) | f (nh)]
 };
 __global__ void __launch_bounds__(kRowThreads) k_mlstm_gates(const MlstmGatesP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   const long long slot = row_slot(p.rc, r);
@@ -724,6 +748,8 @@ struct MlstmPostP {
   const float *gnw, *gnb, *skip; void* A; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_mlstm_post(const MlstmPostP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float o[];
@@ -747,6 +773,8 @@ struct XFinalP {
   const float* x2; int H; const float* w; const float* res; float* out;
 };
 __global__ void __launch_bounds__(kRowThreads) k_xlstm_final(const XFinalP p) {
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float x[];
@@ -874,7 +902,7 @@ class XLSTMLayer : public Layer {
     const RowCtx rc{c.n_dev, c.rows, c.slots};
     // ---- sLSTM block (xlstm.py:304-318)
     SlstmPreP sp{rc, in, H_, nbl_, bs_, slnw_, sconv_, ssconv_, scw_, scb_, sh_, ssh_, b.axc, b.axn};
-    k_slstm_pre<<<c.rows, kRowThreads, H_ * sizeof(float), c.s>>>(sp);
+    launch_k(c.ln, k_slstm_pre, dim3(c.rows), dim3(kRowThreads), H_ * sizeof(float), c.s, sp);
     // i, f from the conv branch, z, o from the normed input, each + BlockLinear(h) + bias (xlstm.py:312-315)
     for (int g0 = 0; g0 < 4 * nbl_; g0 += kMaxGroups) {
       GemmParams gp;
@@ -889,17 +917,18 @@ class XLSTMLayer : public Layer {
       }
       gp.M_max = c.rows; gp.M_dev = c.n_dev; gp.N = bs_; gp.K = 2 * bs_;
       gp.lda = 2 * H_; gp.ldw = 2 * bs_; gp.ldc = 4 * H_;
+      gp.ln = c.ln;
       gemm(gp, c.s);
     }
     SlstmPostP so{rc, b.G, in, H_, nbl_, sh_, sc_, sn_, sm_, ssh_, ssc_, ssn_, ssm_, sgnw_, sgnb_, mlnw_, b.x1, b.xn2, lp_};
-    k_slstm_post<<<c.rows, kRowThreads, 2 * H_ * sizeof(float), c.s>>>(so);
+    launch_k(c.ln, k_slstm_post, dim3(c.rows), dim3(kRowThreads), 2 * H_ * sizeof(float), c.s, so);
     // ---- mLSTM block (xlstm.py:198-219)
     linear(c, b.xn2, lp_, H_, mw1_, lp_, nullptr, 2 * mi_, H_, b.proj, 2 * mi_);  // x_proj, gate_proj
     MlstmPreP mp{rc, b.proj, mi_, mconv_, smconv_, mcw_, mcb_, wq_, wk_, wv_, b.xca, b.qkv};
-    k_mlstm_pre<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(mp);
+    launch_k(c.ln, k_mlstm_pre, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, mp);
     linear(c, b.qkv, kF32, 3 * mi_, gw_, kF32, gb_, 2 * nh_, 3 * mi_, b.ifp, 2 * nh_);  // igate/fgate, fp32 kept
     MlstmGatesP gp{rc, b.ifp, b.qkv, mi_, nh_, hs_, n_, sn2_, m_, sm2_, b.g2, b.den};
-    k_mlstm_gates<<<c.rows, kRowThreads, 0, c.s>>>(gp);
+    launch_k(c.ln, k_mlstm_gates, dim3(c.rows), dim3(kRowThreads), 0, c.s, gp);
     OuterRowsParams op;
     op.at = {C_, sC_, c.slots, nullptr, c.rows, c.n_dev};
     op.nh = nh_; op.sh = hs_; op.sk = hs_;
@@ -909,9 +938,9 @@ class XLSTMLayer : public Layer {
     op.v = b.qkv + 2 * mi_; op.v_rs = 3 * mi_;
     op.q = b.qkv; op.q_rs = 3 * mi_;
     op.out = b.num; op.o_rs = mi_;
-    outer_rows(op, c.rows, c.s);
+    outer_rows(op, c.rows, c.s, c.ln_bulk);
     MlstmPostP pp{rc, b.num, b.den, b.xca, b.proj, mi_, nh_, ongw_, ongb_, skip_, b.A, lp_};
-    k_mlstm_post<<<c.rows, kRowThreads, mi_ * sizeof(float), c.s>>>(pp);
+    launch_k(c.ln, k_mlstm_post, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, pp);
     if (post) {
       // proj_down + skip, final LayerNorm, Block residual and the Block's norm2,
       // all in the GEMM epilogue (xlstm.py:217-219, 365; inference_model.py:65-67)
@@ -924,7 +953,7 @@ class XLSTMLayer : public Layer {
     } else {
       linear(c, b.A, lp_, mi_, down_, lp_, nullptr, H_, mi_, b.x2, H_, kActNone, b.x1, H_);  // proj_down + skip
       XFinalP fp{rc, b.x2, H_, fnw_, residual, out};
-      k_xlstm_final<<<c.rows, kRowThreads, H_ * sizeof(float), c.s>>>(fp);
+      launch_k(c.ln, k_xlstm_final, dim3(c.rows), dim3(kRowThreads), H_ * sizeof(float), c.s, fp);
     }
     B2E_CUDA(cudaGetLastError());
   }
@@ -959,14 +988,14 @@ std::unique_ptr<Layer> Layer::make(int kind, const Dims& d, int lp) {
 
 void rmsnorm_rows(const StepCtx& c, const float* x, const float* w, float eps, int H, float* out, void* out_lp) {
   RmsP p{{c.n_dev, c.rows, c.slots}, x, w, out, H, eps, out_lp, c.lp};
-  k_rmsnorm<<<ceil_div(c.rows, kRowsPerCta), 256, 0, c.s>>>(p);
+  launch_k(c.ln, k_rmsnorm, dim3(ceil_div(c.rows, kRowsPerCta)), dim3(256), 0, c.s, p);
   B2E_CUDA(cudaGetLastError());
 }
 
 void output_proj_rows(const StepCtx& c, const float* x, const float* w, const float* b, int H, float* preds, int ld,
                       int col) {
   OutP p{{c.n_dev, c.rows, c.slots}, x, w, b, H, preds, ld, col};
-  k_output_proj<<<ceil_div(c.rows, kRowsPerCta), 256, 0, c.s>>>(p);
+  launch_k(c.ln, k_output_proj, dim3(ceil_div(c.rows, kRowsPerCta)), dim3(256), 0, c.s, p);
   B2E_CUDA(cudaGetLastError());
 }
 
@@ -997,6 +1026,7 @@ void linear(const StepCtx& c, const void* A, int at, int lda, const void* W, int
   p.bias_type = wt;  // CastLinear stores its bias in the weight's type (example_model.py:85-88)
   p.round_out = wt != kF32;
   p.act = act;
+  p.ln = c.ln;
   if (row) {
     p.row = *row;
     B2E_CHECK(gemm_tc_row_eligible(p), kErrInternal, "fused row epilogue requested for an ineligible projection");

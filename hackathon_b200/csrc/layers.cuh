@@ -36,6 +36,8 @@ struct StepCtx {
   const int* slots = nullptr;  // row -> state slot (device)
   int lp = kF32;              // CastLinear storage type; kF32 = the fp32 path
   int* err = nullptr;         // device error word (bounded waits in tensor-core GEMMs)
+  LaunchCfg ln;               // launch of every kernel of the chain
+  LaunchCfg ln_bulk;          // launch of the HBM-streaming state kernels
 };
 
 class Layer {
