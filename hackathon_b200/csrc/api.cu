@@ -8,6 +8,7 @@
 #include "cells.cuh"
 #include "engine.cuh"
 #include "gemm.cuh"
+#include "stream.cuh"
 
 using namespace b2e;
 
@@ -78,7 +79,7 @@ EngineOptions to_opts(const b2e_engine_options* o) {
   if (o->lanes > 0) e.lanes = o->lanes;
   if (o->lane_min_rows > 0) e.lane_min_rows = o->lane_min_rows;
   e.pdl = (o->flags & B2E_FLAG_PDL) != 0;
-  e.priorities = !(o->flags & B2E_FLAG_NO_PRIORITIES);
+  e.priorities = (o->flags & B2E_FLAG_PRIORITIES) != 0;
   return e;
 }
 
@@ -321,6 +322,7 @@ int b2e_layer_create(int32_t kind, const b2e_model_config* cfg, const b2e_engine
     h->pdl = o.pdl;
     B2E_CUDA(cudaSetDevice(o.device));
     gemm_tc_init();
+    stream_init();
     WeightSource src;
     fill_source(src, tensors, n_tensors);
     h->layer = Layer::make(kind, h->d, o.lp);

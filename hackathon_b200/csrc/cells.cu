@@ -6,6 +6,7 @@
 // per SM - enough to cover HBM latency at full bandwidth. The small per-row
 // operands (q, i*k, v or dt*b, c, x) are staged once in shared memory.
 #include "cells.cuh"
+#include "stream.cuh"
 
 #include <algorithm>
 
@@ -425,6 +426,10 @@ void outer_rows(const OuterRowsParams& p, int rows_max, cudaStream_t s, const La
   B2E_CHECK((reinterpret_cast<uintptr_t>(p.at.state) & 15) == 0 && (p.at.row_stride & 3) == 0, kErrInvalid,
             "outer_rows: state must be 16-byte aligned per row");
   if (rows_max <= 0) return;
+  if (outer_rows_bulk_ok(p)) {
+    outer_rows_bulk(p, rows_max, s, ln);
+    return;
+  }
   const int kt = std::min(kKT, p.sk);
   const int per_head = p.sh * (kt / 4);
   const int L = kt / 4, RH = kThreads / L;
@@ -454,6 +459,10 @@ void ssm_cols(const SsmColsParams& p, int rows_max, cudaStream_t s, const Launch
   B2E_CHECK((reinterpret_cast<uintptr_t>(p.at.state) & 15) == 0 && (p.at.row_stride & 3) == 0, kErrInvalid,
             "ssm_cols: state must be 16-byte aligned per row");
   if (rows_max <= 0) return;
+  if (ssm_cols_bulk_ok(p)) {
+    ssm_cols_bulk(p, rows_max, s, ln);
+    return;
+  }
   const int LC = p.sc / 4;
   const int PT = std::min(p.sh, std::max(1, kItems / LC));
   auto smem_of = [&](int hg) {

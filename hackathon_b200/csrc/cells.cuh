@@ -37,6 +37,7 @@ struct OuterRowsParams {
   const float* v = nullptr; int v_rs = 0;            // [row][nh*sk]
   const float* q = nullptr; int q_rs = 0;            // [row][nh*sh]
   float* out = nullptr; int o_rs = 0;                // [row][nh*sk]
+  int* err = nullptr;                                // device error word for the bulk path's bounded waits, or null
 };
 
 struct SsmColsParams {
@@ -48,8 +49,11 @@ struct SsmColsParams {
   const float* dt = nullptr; int dt_rs = 0;      // [row][nh]
   const float* decay = nullptr; int dc_rs = 0;   // [row][nh]
   float* out = nullptr; int o_rs = 0;            // [row][nh*sh]
+  int* err = nullptr;                            // as in OuterRowsParams
 };
 
+// Both dispatch to the bulk-copy streaming kernels (stream.cuh) when the
+// operands allow, else to the register-streaming kernels here.
 void outer_rows(const OuterRowsParams& p, int rows_max, cudaStream_t s, const LaunchCfg& ln = {});
 void ssm_cols(const SsmColsParams& p, int rows_max, cudaStream_t s, const LaunchCfg& ln = {});
 

@@ -14,6 +14,7 @@
 
 #include "engine.cuh"
 #include "gemm.cuh"
+#include "stream.cuh"
 
 namespace b2e {
 
@@ -47,6 +48,7 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   B2E_CHECK(o.lp == kF32 || o.lp == kBF16 || o.lp == kF16, kErrInvalid, "unknown linear dtype");
   B2E_CUDA(cudaSetDevice(o.device));
   gemm_tc_init();
+  stream_init();
   const int H = d.H, P = d.P, F = d.F, lp = o.lp;
 
   // ---- weights (strict key names of MultiTowerModel.state_dict())

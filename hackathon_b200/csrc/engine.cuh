@@ -17,7 +17,7 @@ struct EngineOptions {
   int lanes = 1;          // independent row shares per tower for batches of >= lane_min_rows
   int lane_min_rows = 256;
   bool pdl = false;        // programmatic dependent launch inside each tower's chain
-  bool priorities = true;  // state-streaming kernels at low priority, the rest high
+  bool priorities = false;  // state-streaming kernels at low priority, the rest high
 };
 
 class Engine {

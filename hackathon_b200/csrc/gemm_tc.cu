@@ -32,6 +32,7 @@
 #include <mutex>
 
 #include "gemm.cuh"
+#include "mbarrier.cuh"
 
 namespace b2e {
 namespace {
@@ -41,7 +42,6 @@ constexpr int kEpiWarps = 8, kEpiThreads = 32 * kEpiWarps;
 constexpr int THREADS = 64 + kEpiThreads;  // producer warp, MMA warp, epilogue warps
 constexpr int kMaxStages = 8;                    // ring depth is chosen per launch
 constexpr size_t kSmemBarriers = 1024 + 256;     // 1024-byte alignment slack + barriers
-constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
 
 template <int NT, int BR>
 struct Cfg {
@@ -80,40 +80,6 @@ struct TcEpi {
   int row_on;
   int stages;  // ring depth, MIN_STAGES..kMaxStages
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: true when the phase completed, false on timeout or abort.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
-  const long long t0 = clock64();
-  while (!mbar_try(b, parity)) {
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) return false;
-  }
-  return true;
-}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -563,6 +529,10 @@ bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0;
 constexpr size_t kSmemPerSm = 228 * 1024;   // shared memory of one SM
 constexpr size_t kSmemPerCta = 227 * 1024;  // largest dynamic allocation of one CTA
 constexpr size_t kSmemReserved = 1024;      // the system's share of each resident CTA
+// A GEMM CTA stays within what an SM has left beside one bulk state-streaming
+// CTA (stream.cu, ~113 KB), so the projections of one tower can run on the
+// same SMs while another tower's state streams.
+constexpr size_t kSmemGemmCap = 116 * 1024 - 128;
 
 // One candidate tile shape: CTAs, resident CTAs per SM, ring depth, and a cost
 // estimate in microseconds: each wave pays a fixed latency (TMA round trips,
@@ -579,7 +549,7 @@ void plan(const GemmParams& p, TilePlan& best) {
   const int nkb = ceil_div(p.K, BK);
   const int cap = std::min(kMaxStages, std::max(nkb, K::MIN_STAGES));
   for (int occ = 3; occ >= 1; --occ) {
-    const size_t per_cta = std::min(kSmemPerCta, kSmemPerSm / occ - kSmemReserved);
+    const size_t per_cta = std::min(kSmemGemmCap, kSmemPerSm / occ - kSmemReserved);
     if (per_cta < K::smem(K::MIN_STAGES)) continue;
     const int st = std::min<int>(cap, int((per_cta - kSmemBarriers) / K::STAGE));
     if (occ > 1 && ctas <= 148L * (occ - 1)) continue;  // fewer CTAs per SM suffice: keep the deeper ring

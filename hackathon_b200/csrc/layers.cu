@@ -290,6 +290,7 @@ class Mamba2Layer : public Layer {
     sp.nh = nh_; sp.sh = hs_; sp.sc = bc_;
     sp.x = b.xs; sp.x_rs = mi_; sp.b = b.bs; sp.b_rs = bc_; sp.c = b.cs; sp.c_rs = bc_;
     sp.dt = b.dt; sp.dt_rs = nh_; sp.decay = b.dc; sp.dc_rs = nh_; sp.out = b.ys; sp.o_rs = mi_;
+    sp.err = c.err;
     ssm_cols(sp, c.rows, c.s, c.ln_bulk);
     Mamba2PostP po{rc, b.ys, b.xs, b.proj, n1_, mi_, hs_, dd_, nw_, b.A, lp_};
     launch_k(c.ln, k_mamba2_post, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, po);
@@ -424,6 +425,7 @@ class RetNetLayer : public Layer {
     op.f = decay_; op.f_rs = 0; op.f_hs = 1;
     op.kv = b.kr; op.k_rs = H_; op.v = b.proj + 2 * H_; op.v_rs = 4 * H_;
     op.q = b.qs; op.q_rs = H_; op.out = b.o; op.o_rs = H_;
+    op.err = c.err;
     outer_rows(op, c.rows, c.s, c.ln_bulk);
     RetPostP po{rc, b.o, b.proj, H_, nh_, hs_, b.A, lp_};
     launch_k(c.ln, k_retnet_post, dim3(c.rows), dim3(kRowThreads), nh_ * sizeof(float), c.s, po);
@@ -938,6 +940,7 @@ class XLSTMLayer : public Layer {
     op.v = b.qkv + 2 * mi_; op.v_rs = 3 * mi_;
     op.q = b.qkv; op.q_rs = 3 * mi_;
     op.out = b.num; op.o_rs = mi_;
+    op.err = c.err;
     outer_rows(op, c.rows, c.s, c.ln_bulk);
     MlstmPostP pp{rc, b.num, b.den, b.xca, b.proj, mi_, nh_, ongw_, ongb_, skip_, b.A, lp_};
     launch_k(c.ln, k_mlstm_post, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, pp);
