@@ -155,8 +155,9 @@ def barrier(world: int):
         dist.barrier()
 
 
-def make_batches(wl, n_symbols, world, rank, count, seed=0):
-    """(slots per micro-batch on this rank, capacity) for `count` micro-batches."""
+def make_batches(wl, n_symbols, world, rank, count, seed=0, backlog=None):
+    """(slots per micro-batch on this rank, capacity) for `count` micro-batches.
+    `backlog`: Zipf arrivals generated (default max(10M, 4M per GPU))."""
     from hackathon_b200 import batcher as B
 
     mine, slot_of = B.shard_slots(n_symbols, world, rank)
@@ -172,7 +173,7 @@ def make_batches(wl, n_symbols, world, rank, count, seed=0):
         return out[:count], len(mine)
     # A deep backlog keeps >= max_batch symbols pending, so every micro-batch is
     # full: 10M arrivals (BASELINE config 5's stream), at least 4M per GPU.
-    need = max(10_000_000, 4_000_000 * world)
+    need = backlog or max(10_000_000, 4_000_000 * world)
     stream = B.zipf_stream(n_symbols, need, wl["zipf"], seed)
     own = stream[B.owner(stream, world) == rank]
     out = [slot_of[own[idx]].astype(np.int32)

@@ -282,7 +282,7 @@ int b2e_linear(const void* x, int32_t x_dtype, int32_t m, int32_t k, const void*
     B2E_CHECK(w_dtype == kF32 || w_dtype == kBF16 || w_dtype == kF16, kErrInvalid, "unknown weight dtype");
     B2E_CHECK(x_dtype == kF32 || x_dtype == w_dtype, kErrInvalid, "x must be f32 or the weight's dtype");
     B2E_CHECK(act == kActNone || act == kActRelu, kErrInvalid, "unknown activation");
-    if (d_err) gemm_tc_init();
+    gemm_tc_init();
     GemmParams p;
     p.g[0].A = x;
     p.g[0].W = w;

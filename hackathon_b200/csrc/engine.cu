@@ -26,6 +26,18 @@ __global__ void k_split_rows(const int* n_dev, int* n_lane, int lanes, int per) 
   if (l < lanes) n_lane[l] = max(0, min(per, *n_dev - l * per));
 }
 
+// Features rounded to the CastLinear type (the x.to(weight.dtype) of input_up,
+// example_model.py:92-95), rows padded with zeros from F to fpad columns.
+template <int T>
+__global__ void k_feats_lp(const float* f, int F, void* out, int fpad, const int* n_dev) {
+  const long long total = (long long)(*n_dev) * fpad;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / fpad;
+    const int c = int(i - r * fpad);
+    LowP<T>::store(out, size_t(i), c < F ? f[r * F + c] : 0.0f);
+  }
+}
+
 __global__ void k_validate(const int* slots, int n, int capacity, int* n_dev, int* err) {
   __shared__ int bad;
   if (threadIdx.x == 0) bad = 0;
@@ -53,12 +65,14 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
 
   // ---- weights (strict key names of MultiTowerModel.state_dict())
   towers_.resize(4);
+  fpad_ = lp == kF32 ? F : (F + 7) & ~7;
+  std::vector<const float*> upw(4), upb(4);
   for (int t = 0; t < 4; ++t) {
     Tower& tw = towers_[t];
     tw.kind = t;  // tower order xLSTM, Mamba2, RetNet, Hawk (model/inference_model.py:107-112)
     const std::string tp = "towers." + std::to_string(t) + ".";
-    tw.o_upw = pack_.add(src.get(tp + "input_up.weight", long(P) * F), size_t(P) * F, lp);
-    tw.o_upb = pack_.add(src.get(tp + "input_up.bias", P), P, lp);
+    upw[t] = src.get(tp + "input_up.weight", long(P) * F);
+    upb[t] = src.get(tp + "input_up.bias", P);
     tw.o_dnw = pack_.add(src.get(tp + "input_down.weight", long(H) * P), size_t(H) * P, lp);
     tw.o_dnb = pack_.add(src.get(tp + "input_down.bias", H), H, lp);
     tw.blocks.resize(d.depth);
@@ -75,6 +89,18 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
       bl.o_f2b = pack_.add(src.get(bp + "mlp.fc2.bias", H), H, lp);
     }
   }
+  {
+    const int fp = fpad_;
+    o_upw_ = pack_.reserve(size_t(4) * P * fp * dtype_size(lp), [=](uint8_t* d) {
+      std::vector<float> row(fp, 0.0f);
+      for (int t = 0; t < 4; ++t)
+        for (int r = 0; r < P; ++r) {
+          std::copy(upw[t] + size_t(r) * F, upw[t] + size_t(r + 1) * F, row.begin());
+          convert_f32(row.data(), d + (size_t(t) * P + r) * fp * dtype_size(lp), fp, lp);
+        }
+    });
+    o_upb_ = pack_.add_rows({{upb[0], size_t(P)}, {upb[1], size_t(P)}, {upb[2], size_t(P)}, {upb[3], size_t(P)}}, lp);
+  }
   o_ow_ = pack_.add(src.get("output_proj.weight", H), H, kF32);  // fp32 kept (example_model.py:106)
   o_ob_ = pack_.add(src.get("output_proj.bias", 1), 1, kF32);
   src.check_all_used();
@@ -86,7 +112,6 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   arena_.allocate(o.capacity);
 
   for (auto& tw : towers_) {
-    tw.upw = pack_.ptr(tw.o_upw); tw.upb = pack_.ptr(tw.o_upb);
     tw.dnw = pack_.ptr(tw.o_dnw); tw.dnb = pack_.ptr(tw.o_dnb);
     for (auto& bl : tw.blocks) {
       bl.n1 = pack_.ptr<float>(bl.o_n1); bl.n2 = pack_.ptr<float>(bl.o_n2);
@@ -122,6 +147,10 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
     B2E_CUDA(cudaEventCreateWithFlags(&ch.done, cudaEventDisableTiming));
   }
   ow_ = pack_.ptr<float>(o_ow_);
+  upw_ = pack_.ptr(o_upw_);
+  upb_ = pack_.ptr(o_upb_);
+  B2E_CUDA(cudaMalloc(&d_up_, size_t(o.max_batch) * 4 * P * dtype_size(lp)));
+  if (lp != kF32) B2E_CUDA(cudaMalloc(&d_feats_lp_, size_t(o.max_batch) * fpad_ * dtype_size(lp)));
   ob_ = pack_.ptr<float>(o_ob_);
 
   // ---- step I/O
@@ -166,6 +195,8 @@ Engine::~Engine() {
   if (fork_) cudaEventDestroy(fork_);
   if (s0_) cudaStreamDestroy(s0_);
   if (d_io_) cudaFree(d_io_);
+  if (d_up_) cudaFree(d_up_);
+  if (d_feats_lp_) cudaFree(d_feats_lp_);
   if (h_io_) cudaFreeHost(h_io_);
 }
 
@@ -179,7 +210,8 @@ int Engine::lanes_for(int rows) const {
   return (opt_.lanes > 1 && rows >= opt_.lane_min_rows) ? opt_.lanes : 1;
 }
 
-void Engine::tower_forward(const Tower& tw, Chain& ch, int idx, const StepCtx& c, const float* feats, float* preds) {
+void Engine::tower_forward(const Tower& tw, Chain& ch, int idx, const StepCtx& c, const void* up, int ld_up,
+                           float* preds) {
   const int H = d_.H, P = d_.P, F = d_.F, lp = opt_.lp;
   const bool low = lp != kF32;
   // GEMM inputs are written in the CastLinear type (the cast CastLinear applies,
@@ -187,8 +219,8 @@ void Engine::tower_forward(const Tower& tw, Chain& ch, int idx, const StepCtx& c
   float* u32 = low ? nullptr : ch.u;
   void* ulp = low ? static_cast<void*>(ch.u) : nullptr;
   const float eps = 1.1920928955078125e-07f;  // nn.RMSNorm(eps=None) in float32
-  // input_up, ReLU, input_down (model/inference_model.py:88-90)
-  linear(c, feats, kF32, F, tw.upw, lp, tw.upb, P, F, u32, P, kActRelu, nullptr, 0, ulp, P);
+  // input_down of relu(input_up(features)) (model/inference_model.py:88-90); the
+  // four towers' input_up ran as one projection before the fork
   const bool fuse = fused_rows(c, H);
   const size_t nb = tw.blocks.size();
   if (fuse) {
@@ -199,9 +231,9 @@ void Engine::tower_forward(const Tower& tw, Chain& ch, int idx, const StepCtx& c
     r0.T = ch.t;
     r0.T_lp = ch.tl;
     r0.ldt = H;
-    linear(c, ch.u, lp, P, tw.dnw, lp, tw.dnb, H, P, ch.x, H, kActNone, nullptr, 0, nullptr, 0, &r0);
+    linear(c, up, lp, ld_up, tw.dnw, lp, tw.dnb, H, P, ch.x, H, kActNone, nullptr, 0, nullptr, 0, &r0);
   } else {
-    linear(c, ch.u, lp, P, tw.dnw, lp, tw.dnb, H, P, ch.x, H);
+    linear(c, up, lp, ld_up, tw.dnw, lp, tw.dnb, H, P, ch.x, H);
   }
   for (size_t bi = 0; bi < nb; ++bi) {
     const Block& bl = tw.blocks[bi];
@@ -246,6 +278,27 @@ void Engine::enqueue(int rows, cudaStream_t s) {
   const int per = (rows + L - 1) / L;
   k_split_rows<<<1, 32, 0, s>>>(d_n_, d_nl_, L, per);
   B2E_CUDA(cudaGetLastError());
+  // input_up of the four towers, one projection over all rows
+  const int P = d_.P, F = d_.F, lp = opt_.lp;
+  StepCtx c0;
+  c0.s = s;
+  c0.rows = rows;
+  c0.n_dev = d_n_;
+  c0.slots = d_slots_;
+  c0.lp = lp;
+  c0.err = d_err_;
+  c0.ln = ln_;
+  if (lp != kF32) {
+    const int blocks = std::max(1, std::min(ceil_div(long(rows) * fpad_, 256 * 4), 148 * 4));
+    if (lp == kBF16)
+      k_feats_lp<kBF16><<<blocks, 256, 0, s>>>(d_feats_, F, d_feats_lp_, fpad_, d_n_);
+    else
+      k_feats_lp<kF16><<<blocks, 256, 0, s>>>(d_feats_, F, d_feats_lp_, fpad_, d_n_);
+    B2E_CUDA(cudaGetLastError());
+    linear(c0, d_feats_lp_, lp, fpad_, upw_, lp, upb_, 4 * P, fpad_, nullptr, 0, kActRelu, nullptr, 0, d_up_, 4 * P);
+  } else {
+    linear(c0, d_feats_, kF32, F, upw_, kF32, upb_, 4 * P, F, static_cast<float*>(d_up_), 4 * P, kActRelu);
+  }
   B2E_CUDA(cudaEventRecord(fork_, s));
   for (int l = 0; l < L; ++l) {
     for (int t = 0; t < 4; ++t) {
@@ -260,7 +313,8 @@ void Engine::enqueue(int rows, cudaStream_t s) {
       c.err = d_err_;
       c.ln = ln_;
       c.ln_bulk = ln_bulk_;
-      tower_forward(towers_[t], ch, t, c, d_feats_ + size_t(l) * per * d_.F, d_preds_ + size_t(l) * per * 4);
+      const void* up = static_cast<const uint8_t*>(d_up_) + (size_t(l) * per * 4 * P + size_t(t) * P) * dtype_size(lp);
+      tower_forward(towers_[t], ch, t, c, up, 4 * P, d_preds_ + size_t(l) * per * 4);
       B2E_CUDA(cudaEventRecord(ch.done, ch.s));
     }
   }

@@ -60,8 +60,8 @@ class Engine {
   };
   struct Tower {
     int kind;
-    size_t o_upw, o_upb, o_dnw, o_dnb;
-    const void *upw, *upb, *dnw, *dnb;
+    size_t o_dnw, o_dnb;
+    const void *dnw, *dnb;
     std::vector<Block> blocks;
   };
   // One tower over one lane (a contiguous share of the step's rows): its own
@@ -76,7 +76,7 @@ class Engine {
   int bucket(int n) const;
   void launch(int n, cudaStream_t s);   // graph replay or eager enqueue
   void enqueue(int rows, cudaStream_t s);
-  void tower_forward(const Tower& t, Chain& ch, int idx, const StepCtx& c, const float* feats, float* preds);
+  void tower_forward(const Tower& t, Chain& ch, int idx, const StepCtx& c, const void* up, int ld_up, float* preds);
   int lanes_for(int rows) const;
   void check_host_slots(const int* slots, int n);
 
@@ -87,6 +87,15 @@ class Engine {
   std::vector<Tower> towers_;
   std::vector<Chain> chains_;  // [lane][tower]
   int* d_nl_ = nullptr;        // live rows per lane (device)
+  // input_up of all four towers as one projection: W [4P][fpad] (features
+  // padded with zero columns to a multiple of 8 for the tensor cores), bias
+  // [4P], input = the step's features in the CastLinear type [rows][fpad],
+  // output [rows][4P] (tower t: columns t*P..)
+  int fpad_ = 0;
+  size_t o_upw_ = 0, o_upb_ = 0;
+  const void *upw_ = nullptr, *upb_ = nullptr;
+  void* d_feats_lp_ = nullptr;
+  void* d_up_ = nullptr;
   LaunchCfg ln_, ln_bulk_;     // chain kernels / state-streaming kernels
   size_t o_ow_ = 0, o_ob_ = 0;
   const float *ow_ = nullptr, *ob_ = nullptr;

@@ -302,6 +302,83 @@ __global__ void __launch_bounds__(256) gemm_narrow(const __grid_constant__ GemmP
     }
 }
 
+// Same problem with W staged once per CTA in shared memory (when it fits): a
+// persistent grid of warps walks the rows, each lane streaming its 4-wide K
+// slices of A and reading W from shared memory, so the A stream cannot evict W.
+constexpr size_t kNarrowSmemMax = 100 * 1024;
+
+template <int NN>
+__global__ void __launch_bounds__(256) gemm_narrow_smem(const __grid_constant__ GemmParams p) {
+  extern __shared__ __align__(16) float ws[];  // [N][K]
+  const float* W = static_cast<const float*>(p.g[0].W);
+  const int K4 = p.K >> 2, N = p.N;
+  // weights (no predecessor writes them), eight 16-byte loads in flight per thread
+  for (int i0 = threadIdx.x; i0 < N * K4; i0 += blockDim.x * 8) {
+    float4 t[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = i0 + j * blockDim.x, n = i / K4;
+      if (i < N * K4) t[j] = __ldg(reinterpret_cast<const float4*>(W + size_t(n) * p.ldw) + (i - n * K4));
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (i0 + j * blockDim.x < N * K4) reinterpret_cast<float4*>(ws)[i0 + j * blockDim.x] = t[j];
+  }
+  pdl_wait();
+  pdl_launch();
+  const int M = live_rows(p.M_dev, p.M_max);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const float* A = static_cast<const float*>(p.g[0].A);
+  const int lda = p.lda;
+  const float4* ws4 = reinterpret_cast<const float4*>(ws);
+  constexpr int R = 2, U = 4;  // rows per warp, K iterations whose loads go out together
+  const int wstride = gridDim.x * (blockDim.x >> 5) * R;
+  for (int m = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * R; m < M; m += wstride) {
+    float acc[R][NN];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int n = 0; n < NN; ++n) acc[r][n] = 0.f;
+    const float4* a4[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) a4[r] = reinterpret_cast<const float4*>(A + size_t(min(m + r, M - 1)) * lda);
+    for (int kc = lane; kc < K4; kc += 32 * U) {
+      float4 a[R][U];
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          a[r][j] = kc + 32 * j < K4 ? a4[r][kc + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const int k4 = min(kc + 32 * j, K4 - 1);  // past K: a is zero
+#pragma unroll
+        for (int n = 0; n < NN; ++n) {
+          const float4 w = ws4[min(n, N - 1) * K4 + k4];
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+            acc[r][n] = fmaf(a[r][j].w, w.w, fmaf(a[r][j].z, w.z, fmaf(a[r][j].y, w.y, fmaf(a[r][j].x, w.x, acc[r][n]))));
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int n = 0; n < NN; ++n) acc[r][n] = warp_sum(acc[r][n]);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int n = 0; n < NN; ++n)
+        if (r * NN + n == lane && n < N && m + r < M) {
+          const GemmGroup& g = p.g[0];
+          const float v = epilogue<kF32>(p, g, acc[r][n], m + r, n);
+          if (g.C) g.C[size_t(m + r) * p.ldc + n] = v;
+          if (g.C_lp) store_as(kF32, g.C_lp, size_t(m + r) * p.ldc_lp + n, v);
+        }
+  }
+}
+
 bool narrow_eligible(const GemmParams& p) {
   return p.groups == 1 && p.a_type == kF32 && p.w_type == kF32 && p.N <= 16 && p.M_max > 16 && p.K % 4 == 0 &&
          p.lda % 4 == 0 && p.ldw % 4 == 0 && (reinterpret_cast<uintptr_t>(p.g[0].A) & 15) == 0 &&
@@ -354,12 +431,26 @@ void launch(const GemmParams& p, cudaStream_t s) {
 
 }  // namespace
 
+void gemm_simt_init() {
+  B2E_CUDA(cudaFuncSetAttribute(gemm_narrow_smem<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kNarrowSmemMax)));
+  B2E_CUDA(cudaFuncSetAttribute(gemm_narrow_smem<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kNarrowSmemMax)));
+}
+
 void gemm(const GemmParams& p, cudaStream_t s) {
   B2E_CHECK(p.groups >= 1 && p.groups <= kMaxGroups, kErrInternal, "gemm: bad group count");
   B2E_CHECK(p.M_max > 0 && p.N > 0 && p.K > 0, kErrInternal, "gemm: empty problem");
   B2E_CHECK(p.M_max <= 65535 * BM, kErrInternal, "gemm: too many rows");
   if (gemm_tc_eligible(p)) {
     gemm_tc(p, s);
+    return;
+  }
+  if (narrow_eligible(p) && size_t(p.N) * p.K * 4 <= kNarrowSmemMax) {
+    const size_t smem = size_t(p.N) * p.K * 4;
+    const int blocks = std::min(ceil_div(p.M_max, 16), 2 * sm_count());
+    if (p.N <= 8)
+      launch_k(p.ln, gemm_narrow_smem<8>, dim3(blocks), dim3(256), smem, s, p);
+    else
+      launch_k(p.ln, gemm_narrow_smem<16>, dim3(blocks), dim3(256), smem, s, p);
     return;
   }
   if (narrow_eligible(p)) {

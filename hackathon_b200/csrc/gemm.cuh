@@ -74,7 +74,8 @@ struct GemmParams {
 // kernel for M_max <= 16, and the tiled SIMT kernel otherwise.
 void gemm(const GemmParams& p, cudaStream_t stream);
 
-void gemm_tc_init();  // once per device, before any capture
+void gemm_tc_init();    // once per device, before any capture (also runs gemm_simt_init)
+void gemm_simt_init();  // kernel attributes of the SIMT kernels
 bool gemm_tc_eligible(const GemmParams& p);
 bool gemm_tc_row_eligible(const GemmParams& p);  // eligible, and N fits one 256-wide tile
 void gemm_tc(const GemmParams& p, cudaStream_t stream);

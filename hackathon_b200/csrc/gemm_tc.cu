@@ -622,6 +622,7 @@ void set_smem() {
 }  // namespace
 
 void gemm_tc_init() {
+  gemm_simt_init();
   set_smem<1, 32>();
   set_smem<1, 64>();
   set_smem<1, 128>();

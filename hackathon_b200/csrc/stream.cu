@@ -155,7 +155,7 @@ struct SsmIssue {
     *reinterpret_cast<long long*>(sc + kSlot) = slot;
     if (active) {
       mbar_expect_tx(bar, sbytes + xb + 2 * cb);
-      bulk_load(st, p.at.state + slot * p.at.row_stride + size_t(h) * p.sh * p.sc, sbytes, bar);
+      bulk_load_hint(st, p.at.state + slot * p.at.row_stride + size_t(h) * p.sh * p.sc, sbytes, bar, l2_evict_first());
       bulk_load(st + kStateMax, p.x + size_t(row) * p.x_rs + size_t(h) * p.sh, xb, bar);
       bulk_load(st + kStateMax + xb, p.b + size_t(row) * p.b_rs, cb, bar);
       bulk_load(st + kStateMax + xb + cb, p.c + size_t(row) * p.c_rs, cb, bar);
@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) ssm_bulk_kernel(const __grid_
         int row, h;
         is.item(k, row, h);
         const long long slot = *reinterpret_cast<const long long*>(reinterpret_cast<const float*>(st + kScalarOff) + kSlot);
-        bulk_store(p.at.state + slot * p.at.row_stride + size_t(h) * p.sh * p.sc, st, sbytes);
+        bulk_store_hint(p.at.state + slot * p.at.row_stride + size_t(h) * p.sh * p.sc, st, sbytes, l2_evict_first());
       });
 }
 
@@ -257,7 +257,7 @@ struct OuterIssue {
     *reinterpret_cast<long long*>(sc + kSlot) = slot;
     if (active) {
       mbar_expect_tx(bar, sbytes + 2 * qb + vb);
-      bulk_load(st, p.at.state + slot * p.at.row_stride + size_t(h0) * p.sh * p.sk, sbytes, bar);
+      bulk_load_hint(st, p.at.state + slot * p.at.row_stride + size_t(h0) * p.sh * p.sk, sbytes, bar, l2_evict_first());
       uint8_t* o = st + kStateMax;
       bulk_load(o, p.q + size_t(row) * p.q_rs + size_t(h0) * p.sh, qb, bar);
       bulk_load(o + qb, p.kv + size_t(row) * p.k_rs + size_t(h0) * p.sh, qb, bar);
@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) outer_bulk_kernel(const __gri
         int row, h0;
         is.item(k, row, h0);
         const long long slot = *reinterpret_cast<const long long*>(reinterpret_cast<const float*>(st + kScalarOff) + kSlot);
-        bulk_store(p.at.state + slot * p.at.row_stride + size_t(h0) * p.sh * p.sk, st, sbytes);
+        bulk_store_hint(p.at.state + slot * p.at.row_stride + size_t(h0) * p.sh * p.sk, st, sbytes, l2_evict_first());
       });
 }
 
