@@ -33,6 +33,7 @@
 
 #include "gemm.cuh"
 #include "mbarrier.cuh"
+#include "stream.cuh"
 
 namespace b2e {
 namespace {
@@ -530,9 +531,9 @@ constexpr size_t kSmemPerSm = 228 * 1024;   // shared memory of one SM
 constexpr size_t kSmemPerCta = 227 * 1024;  // largest dynamic allocation of one CTA
 constexpr size_t kSmemReserved = 1024;      // the system's share of each resident CTA
 // A GEMM CTA stays within what an SM has left beside one bulk state-streaming
-// CTA (stream.cu, ~113 KB), so the projections of one tower can run on the
-// same SMs while another tower's state streams.
-constexpr size_t kSmemGemmCap = 116 * 1024 - 128;
+// CTA (stream.cuh), so the projections of one tower can run on the same SMs
+// while another tower's state streams.
+constexpr size_t kSmemGemmCap = kSmemPerSm - (stream_cfg::kStreamSmem + kSmemReserved) - kSmemReserved;
 
 // One candidate tile shape: CTAs, resident CTAs per SM, ring depth, and a cost
 // estimate in microseconds: each wave pays a fixed latency (TMA round trips,

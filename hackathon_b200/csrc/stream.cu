@@ -9,15 +9,12 @@
 namespace b2e {
 namespace {
 
-constexpr int kCW = 8;                        // compute warps
+using namespace stream_cfg;
 constexpr int kCT = 32 * kCW;                 // compute threads (named barrier 1)
 constexpr int kBulkThreads = 32 + kCT;        // + the producer warp
-constexpr int kStages = 3;
-constexpr uint32_t kStateMax = 32 * 1024;     // state bytes of one item
-constexpr uint32_t kOpsMax = 4 * 1024;        // operand bytes of one item
 constexpr uint32_t kStageBytes = kStateMax + kOpsMax;
 constexpr size_t kRingBytes = size_t(kStages) * kStageBytes;
-constexpr size_t kBulkSmem = 128 + kRingBytes + 256 + size_t(kCW) * 32 * 16;  // align, ring, barriers, partials
+constexpr size_t kBulkSmem = kStreamSmem;
 enum BulkError : int { kBulkTimeoutProducer = 111, kBulkTimeoutConsumer = 112 };
 
 // Shared-memory ring: kStages stages of [state | operands], full/empty barriers,
@@ -182,8 +179,10 @@ __global__ void __launch_bounds__(kBulkThreads, 1) ssm_bulk_kernel(const __grid_
     return;
   }
   const uint32_t sbytes = is.sbytes, xb = is.xb, cb = is.cb;
-  constexpr int RPW = 32 / LC;  // state rows per warp step
-  const int cw = warp - 1, c4 = lane % LC, rsub = lane / LC;
+  // A state row (LC float4) is covered by LR lanes holding Q = LC/LR vectors
+  // each; a warp takes RPW = 32/LR rows per step.
+  constexpr int LR = LC < 8 ? LC : 8, Q = LC / LR, RPW = 32 / LR;
+  const int cw = warp - 1, c0 = lane % LR, rsub = lane / LR;
   consume(
       r, my, p.err, threadIdx.x - 32,
       [&](int k, uint8_t* st) -> bool {
@@ -197,27 +196,36 @@ __global__ void __launch_bounds__(kBulkThreads, 1) ssm_bulk_kernel(const __grid_
         }
         float4* H = reinterpret_cast<float4*>(st);
         const float* xs = reinterpret_cast<const float*>(st + kStateMax);
-        const float4 b4 = reinterpret_cast<const float4*>(st + kStateMax + xb)[c4];
-        const float4 cv = reinterpret_cast<const float4*>(st + kStateMax + xb + cb)[c4];
         const float dt = sc[0], dc = sc[1];
+        float4 db[Q], cv[Q];  // dt*b and c at this lane's columns c0 + LR*q
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+          const float4 b4 = reinterpret_cast<const float4*>(st + kStateMax + xb)[c0 + LR * q];
+          db[q] = make_float4(dt * b4.x, dt * b4.y, dt * b4.z, dt * b4.w);
+          cv[q] = reinterpret_cast<const float4*>(st + kStateMax + xb + cb)[c0 + LR * q];
+        }
         for (int base = cw * RPW; base < p.sh; base += kCW * RPW) {  // warp-uniform
           const int pp = base + rsub;
           const bool ok = pp < p.sh;
           float dot = 0.f;
           if (ok) {
-            const float4 cur = H[pp * LC + c4];
             const float xp = xs[pp];
-            float4 nv;  // decay*h + (dt*b)*x  (model/kernels.py:163-171)
-            nv.x = fmaf(dc, cur.x, (dt * b4.x) * xp);
-            nv.y = fmaf(dc, cur.y, (dt * b4.y) * xp);
-            nv.z = fmaf(dc, cur.z, (dt * b4.z) * xp);
-            nv.w = fmaf(dc, cur.w, (dt * b4.w) * xp);
-            H[pp * LC + c4] = nv;
-            dot = fmaf(cv.w, nv.w, fmaf(cv.z, nv.z, fmaf(cv.y, nv.y, cv.x * nv.x)));
+#pragma unroll
+            for (int q = 0; q < Q; ++q) {
+              float4* hp = H + pp * LC + c0 + LR * q;
+              const float4 cur = *hp;
+              float4 nv;  // decay*h + (dt*b)*x  (model/kernels.py:163-171)
+              nv.x = fmaf(dc, cur.x, db[q].x * xp);
+              nv.y = fmaf(dc, cur.y, db[q].y * xp);
+              nv.z = fmaf(dc, cur.z, db[q].z * xp);
+              nv.w = fmaf(dc, cur.w, db[q].w * xp);
+              *hp = nv;
+              dot += fmaf(cv[q].w, nv.w, fmaf(cv[q].z, nv.z, fmaf(cv[q].y, nv.y, cv[q].x * nv.x)));
+            }
           }
 #pragma unroll
-          for (int o = LC / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-          if (ok && c4 == 0) out[pp] = dot;
+          for (int o = LR / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+          if (ok && c0 == 0) out[pp] = dot;
         }
         return true;
       },

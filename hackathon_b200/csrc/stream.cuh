@@ -13,6 +13,15 @@
 
 namespace b2e {
 
+namespace stream_cfg {
+constexpr int kCW = 8;                      // compute warps (and one producer warp)
+constexpr int kStages = 3;                  // ring depth
+constexpr unsigned kStateMax = 32 * 1024;   // state bytes of one item
+constexpr unsigned kOpsMax = 4 * 1024;      // operand bytes of one item
+// dynamic shared memory of one CTA: alignment slack, ring, barriers, partials
+constexpr size_t kStreamSmem = 128 + size_t(kStages) * (kStateMax + kOpsMax) + 256 + size_t(kCW) * 32 * 16;
+}  // namespace stream_cfg
+
 void stream_init();  // per device (idempotent); the engine calls it before any capture
 bool outer_rows_bulk_ok(const OuterRowsParams& p);
 bool ssm_cols_bulk_ok(const SsmColsParams& p);
