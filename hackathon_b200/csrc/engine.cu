@@ -172,11 +172,8 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   int prio_low = 0, prio_high = 0;
   B2E_CUDA(cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high));
   ln_.pdl = ln_bulk_.pdl = o.pdl;
-  if (o.priorities && prio_high != prio_low) {
-    ln_.set_prio = ln_bulk_.set_prio = true;
-    ln_.prio = prio_high;
-    ln_bulk_.prio = prio_low;
-  }
+  prio_hi_ = prio_high;
+  prio_lo_ = prio_low;
   seen_.assign(o.capacity, 0);
 
   arena_.reset_all(s0_);
@@ -313,6 +310,11 @@ void Engine::enqueue(int rows, cudaStream_t s) {
       c.err = d_err_;
       c.ln = ln_;
       c.ln_bulk = ln_bulk_;
+      if (opt_.priorities && prio_hi_ != prio_lo_) {
+        // the xLSTM tower's chain is the longest: its kernels take SM slots first
+        c.ln.set_prio = c.ln_bulk.set_prio = true;
+        c.ln.prio = c.ln_bulk.prio = t == 0 ? prio_hi_ : prio_lo_;
+      }
       const void* up = static_cast<const uint8_t*>(d_up_) + (size_t(l) * per * 4 * P + size_t(t) * P) * dtype_size(lp);
       tower_forward(towers_[t], ch, t, c, up, 4 * P, d_preds_ + size_t(l) * per * 4);
       B2E_CUDA(cudaEventRecord(ch.done, ch.s));

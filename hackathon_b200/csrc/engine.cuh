@@ -17,7 +17,7 @@ struct EngineOptions {
   int lanes = 1;          // independent row shares per tower for batches of >= lane_min_rows
   int lane_min_rows = 256;
   bool pdl = false;        // programmatic dependent launch inside each tower's chain
-  bool priorities = false;  // state-streaming kernels at low priority, the rest high
+  bool priorities = true;   // the xLSTM tower's chain at high launch priority, the others low
 };
 
 class Engine {
@@ -97,6 +97,7 @@ class Engine {
   void* d_feats_lp_ = nullptr;
   void* d_up_ = nullptr;
   LaunchCfg ln_, ln_bulk_;     // chain kernels / state-streaming kernels
+  int prio_hi_ = 0, prio_lo_ = 0;
   size_t o_ow_ = 0, o_ob_ = 0;
   const float *ow_ = nullptr, *ob_ = nullptr;
 

@@ -656,92 +656,160 @@ __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) 
     store_as(p.at, p.xn2, size_t(r) * p.H + e, (x1[e] - gm[0]) * gr[0] * p.mlnw[e]);
 }
 
-struct MlstmPreP {
+// The mLSTM block between x_proj/gate_proj and the cell's state update, for
+// kMidRows rows per CTA (xlstm.py:92-132, 198-213): conv1d + SiLU, the q/k/v
+// BlockLinears (4x4 blocks), the input/forget gate projections over cat(q,k,v)
+// (fp32, weights shared by the CTA's rows through L1), the stabilized gates and
+// the normalizer state. Outputs: xca (conv+SiLU), q | k/sqrt(hs) | v, (i, f)
+// gate values and the h-denominator per head; the conv, n and m leaves updated.
+struct MlstmMidP {
   RowCtx rc;
-  const float* proj; int mi;  // proj row: [x_mlstm (mi) | x_gate (mi)]
+  const float* proj; int mi, nh, hs;          // proj row: [x_mlstm (mi) | x_gate (mi)]
   float* conv; long long cs; const float* cw; const float* cb;
-  const float *wq, *wk, *wv;  // (mi/4, 4, 4)
-  float* xca; float* qkv;     // [row][mi], [row][3mi] = [q | k | v]
+  const float *wq, *wk, *wv;                  // (mi/4, 4, 4)
+  const float* gw; const float* gb;           // [2nh][3mi] (igate rows, then fgate rows), [2nh]
+  float* n; long long n_s; float* m; long long m_s;
+  float* xca; float* qkv; float* g2; float* den;  // [row][mi], [row][3mi], [row][2nh] (i | f), [row][nh]
+  int rows_per_cta;
 };
-__global__ void __launch_bounds__(kRowThreads) k_mlstm_pre(const MlstmPreP p) {
+__global__ void __launch_bounds__(kRowThreads, 3) k_mlstm_mid(const MlstmMidP p) {
   pdl_wait();
   pdl_launch();
-  const int r = blockIdx.x;
-  if (!row_live(p.rc, r)) return;
-  extern __shared__ float xs[];  // conv+silu output (mi)
-  float* st = p.conv + row_slot(p.rc, r) * p.cs;
-  const float* xm = p.proj + size_t(r) * 2 * p.mi;
-  for (int c = threadIdx.x; c < p.mi; c += blockDim.x) {
-    const float v = siluf_(conv_step(p.cw, p.cb, st, p.mi, c, xm[c]));  // xlstm.py:206-207
-    xs[c] = v;
-    p.xca[size_t(r) * p.mi + c] = v;
+  const int r0 = blockIdx.x * p.rows_per_cta;
+  const int nr = min(p.rows_per_cta, live_rows(p.rc.n_dev, p.rc.rows) - r0);
+  if (nr <= 0) return;
+  extern __shared__ float smid[];  // [rows][3mi] q | k | v (k unscaled), [rows][mi] conv+SiLU, [rows][2nh] gate pre-activations
+  const int mi = p.mi, nh = p.nh, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  float* xcs = smid + size_t(p.rows_per_cta) * 3 * mi;
+  float* gpre = xcs + size_t(p.rows_per_cta) * mi;
+  // conv1d + SiLU (xlstm.py:206-207), consecutive channels on consecutive lanes
+  for (int it = tid; it < nr * mi; it += blockDim.x) {
+    const int rr = it / mi, c = it - rr * mi, r = r0 + rr;
+    float* st = p.conv + row_slot(p.rc, r) * p.cs;
+    const float v = siluf_(conv_step(p.cw, p.cb, st, mi, c, p.proj[size_t(r) * 2 * mi + c]));
+    xcs[rr * mi + c] = v;
+    p.xca[size_t(r) * mi + c] = v;
   }
   __syncthreads();
-  float* q = p.qkv + size_t(r) * 3 * p.mi;
-  float* k = q + p.mi;
-  float* v = k + p.mi;
-  for (int e = threadIdx.x; e < p.mi; e += blockDim.x) {
-    // BlockLinear with 4x4 blocks: out[4b+kk] = sum_h x[4b+h] * W[b][kk][h] (xlstm.py:209-211)
-    const int blk = e >> 2, kk = e & 3;
-    const float* wq = p.wq + size_t(blk) * 16 + kk * 4;
-    const float* wk = p.wk + size_t(blk) * 16 + kk * 4;
-    const float* wv = p.wv + size_t(blk) * 16 + kk * 4;
-    const float* xc = xs + blk * 4;
-    const float* x0 = xm + blk * 4;
-    float aq = 0.f, ak = 0.f, av = 0.f;
+  // q/k from the conv branch, v from x_mlstm: BlockLinear with 4x4 blocks,
+  // out[4b+kk] = sum_h x[4b+h] * W[b][kk][h] (xlstm.py:209-211); one output per
+  // thread, its weight row W[b][kk][:] one 16-byte load
+  for (int it = tid; it < nr * mi; it += blockDim.x) {
+    const int rr = it / mi, e = it - rr * mi, r = r0 + rr;
+    const float4 xc = reinterpret_cast<const float4*>(xcs + rr * mi)[e >> 2];
+    const float4 x0 = reinterpret_cast<const float4*>(p.proj + size_t(r) * 2 * mi)[e >> 2];
+    const float4 wq = __ldg(reinterpret_cast<const float4*>(p.wq) + e);
+    const float4 wk = __ldg(reinterpret_cast<const float4*>(p.wk) + e);
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(p.wv) + e);
+    const float aq = fmaf(xc.w, wq.w, fmaf(xc.z, wq.z, fmaf(xc.y, wq.y, xc.x * wq.x)));
+    const float ak = fmaf(xc.w, wk.w, fmaf(xc.z, wk.z, fmaf(xc.y, wk.y, xc.x * wk.x)));
+    const float av = fmaf(x0.w, wv.w, fmaf(x0.z, wv.z, fmaf(x0.y, wv.y, x0.x * wv.x)));
+    float* q = smid + size_t(rr) * 3 * mi;
+    q[e] = aq;
+    q[mi + e] = ak;
+    q[2 * mi + e] = av;
+    p.qkv[size_t(r) * 3 * mi + e] = aq;
+    p.qkv[size_t(r) * 3 * mi + 2 * mi + e] = av;
+  }
+  __syncthreads();
+  // igate / fgate projections of cat(q, k, v) (xlstm.py:119-120): one warp per
+  // gate, its weight row in registers (U vectors per lane at a time) against
+  // every row of the CTA
+  constexpr int RM = 4, U = 6;
+  const int k4n = (3 * mi) >> 2;
+  for (int g = warp; g < 2 * nh; g += nw) {
+    const float4* w4 = reinterpret_cast<const float4*>(p.gw + size_t(g) * 3 * mi);
+    float acc[RM] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = lane; k0 < k4n; k0 += 32 * U) {
+      float4 w[U];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      aq = fmaf(xc[h], wq[h], aq);
-      ak = fmaf(xc[h], wk[h], ak);
-      av = fmaf(x0[h], wv[h], av);
+      for (int u = 0; u < U; ++u) w[u] = k0 + 32 * u < k4n ? __ldg(w4 + k0 + 32 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int rr = 0; rr < RM; ++rr) {
+        if (rr >= nr) break;
+        const float4* a = reinterpret_cast<const float4*>(smid + size_t(rr) * 3 * mi);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (k0 + 32 * u >= k4n) break;
+          const float4 x = a[k0 + 32 * u];
+          acc[rr] = fmaf(x.w, w[u].w, fmaf(x.z, w[u].z, fmaf(x.y, w[u].y, fmaf(x.x, w[u].x, acc[rr]))));
+        }
+      }
     }
-    q[e] = aq; k[e] = ak; v[e] = av;
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      const float v = warp_sum(acc[rr]);
+      if (lane == 0 && rr < nr) gpre[rr * 2 * nh + g] = v + p.gb[g];
+    }
+  }
+  __syncthreads();
+  // MLSTMCell gates and normalizer (xlstm.py:92-103, 121-132): one warp per head,
+  // every row's state loads issued together
+  const float sq = sqrtf(float(p.hs));
+  for (int h = warp; h < nh; h += nw) {
+    long long slot[RM];
+    float mn[RM], i_g[RM], f_g[RM], qn[RM];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      slot[rr] = rr < nr ? row_slot(p.rc, r0 + rr) : 0;
+      mn[rr] = rr < nr ? p.m[slot[rr] * p.m_s + h] : 0.f;  // old m, replaced below
+    }
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      const float ig = rr < nr ? gpre[rr * 2 * nh + h] : 0.f, fg = rr < nr ? gpre[rr * 2 * nh + nh + h] : 0.f;
+      const float lf = logsigmoidf_(fg), mo = mn[rr];
+      mn[rr] = fmaxf(ig, mo + lf);
+      i_g[rr] = expf(ig - mn[rr]);
+      f_g[rr] = expf(lf + mo - mn[rr]);
+      qn[rr] = 0.f;
+    }
+    for (int j0 = 0; j0 < p.hs; j0 += 128) {
+      float nold[RM][4];
+#pragma unroll
+      for (int rr = 0; rr < RM; ++rr)
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int j = j0 + lane + 32 * t;
+          nold[rr][t] = (rr < nr && j < p.hs) ? p.n[slot[rr] * p.n_s + h * p.hs + j] : 0.f;
+        }
+#pragma unroll
+      for (int rr = 0; rr < RM; ++rr) {
+        if (rr >= nr) break;
+        const float* q = smid + size_t(rr) * 3 * mi;
+        float* nst = p.n + slot[rr] * p.n_s;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int j = j0 + lane + 32 * t;
+          if (j >= p.hs) break;
+          const int e = h * p.hs + j;
+          const float ks = q[mi + e] / sq;  // k / sqrt(head_size) (xlstm.py:99)
+          const float nv = f_g[rr] * nold[rr][t] + i_g[rr] * ks;
+          p.qkv[size_t(r0 + rr) * 3 * mi + mi + e] = ks;
+          nst[e] = nv;
+          qn[rr] = fmaf(q[e], nv, qn[rr]);
+        }
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      const float v = warp_sum(qn[rr]);
+      if (lane == 0 && rr < nr) {
+        const int r = r0 + rr;
+        p.m[slot[rr] * p.m_s + h] = mn[rr];
+        p.g2[size_t(r) * 2 * nh + h] = i_g[rr];
+        p.g2[size_t(r) * 2 * nh + nh + h] = f_g[rr];
+        p.den[size_t(r) * nh + h] = fmaxf(fabsf(v), expf(-mn[rr])) + 1e-6f;  // xlstm.py:130-132
+      }
+    }
   }
 }
 
-struct MlstmGatesP {
-  RowCtx rc;
-  const float* ifp; float* qkv; int mi, nh, hs;  // ifp row: [igate (nh) | fgate (nh)]
-  float* n; long long n_s; float* m; long long m_s;
-  float* g2; float* den;  // g2 row: [i (nh) | f (nh)]
-};
-__global__ void __launch_bounds__(kRowThreads) k_mlstm_gates(const MlstmGatesP p) {
-  pdl_wait();
-  pdl_launch();
-  const int r = blockIdx.x;
-  if (!row_live(p.rc, r)) return;
-  const long long slot = row_slot(p.rc, r);
-  const float* ip = p.ifp + size_t(r) * 2 * p.nh;
-  float* q = p.qkv + size_t(r) * 3 * p.mi;
-  float* k = q + p.mi;
-  float* nst = p.n + slot * p.n_s;
-  float* mst = p.m + slot * p.m_s;
-  const float sq = sqrtf(float(p.hs));
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int h = w; h < p.nh; h += nw) {
-    // MLSTMCell.forward (xlstm.py:92-103, 121-126)
-    const float ig = ip[h], fg = ip[p.nh + h], m = mst[h];
-    const float lf = logsigmoidf_(fg);
-    const float mn = fmaxf(ig, m + lf);
-    const float i_g = expf(ig - mn);
-    const float f_g = expf(lf + m - mn);
-    float qn = 0.f;
-    for (int j = lane; j < p.hs; j += 32) {
-      const int e = h * p.hs + j;
-      const float ks = k[e] / sq;  // k / sqrt(head_size) (xlstm.py:99)
-      const float nv = f_g * nst[e] + i_g * ks;
-      k[e] = ks;
-      nst[e] = nv;
-      qn = fmaf(q[e], nv, qn);
-    }
-    qn = warp_sum(qn);
-    if (lane == 0) {
-      mst[h] = mn;
-      p.g2[size_t(r) * 2 * p.nh + h] = i_g;
-      p.g2[size_t(r) * 2 * p.nh + p.nh + h] = f_g;
-      p.den[size_t(r) * p.nh + h] = fmaxf(fabsf(qn), expf(-mn)) + 1e-6f;  // xlstm.py:130-132
-    }
-  }
+constexpr size_t kMidSmemMax = 96 * 1024;
+// Rows per k_mlstm_mid CTA: up to 4, within kMidSmemMax of shared memory.
+int mid_rows(int mi, int nh) {
+  const size_t per = size_t(4 * mi + 2 * nh) * sizeof(float);
+  B2E_CHECK(per <= kMidSmemMax, kErrInvalid, "mLSTM inner size too large for one CTA");
+  return int(std::max<size_t>(1, std::min<size_t>(4, kMidSmemMax / per)));  // 4 = RM in k_mlstm_mid
 }
 
 struct MlstmPostP {
@@ -795,6 +863,7 @@ class XLSTMLayer : public Layer {
   XLSTMLayer(const Dims& d, int lp) : d_(d), lp_(lp) {
     H_ = d.H; nbl_ = d.slstm_heads(); bs_ = d.slstm_bs();
     mi_ = d.mlstm_inner(); nh_ = d.mlstm_heads(); hs_ = d.mlstm_hs();
+    B2E_CUDA(cudaFuncSetAttribute(k_mlstm_mid, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmemMax)));
   }
   void declare_state(StateArena& a) override {
     // (xlstm.py:331-336, 276-282, 232-236, 150-156) in init_state order
@@ -872,7 +941,7 @@ class XLSTMLayer : public Layer {
     ssm_ = a.stride(l_sm_); smconv_ = a.stride(l_mconv_); sC_ = a.stride(l_C_); sn2_ = a.stride(l_n_);
     sm2_ = a.stride(l_m_);
   }
-  struct Buf { float *axc, *axn, *G, *x1, *xn2, *proj, *xca, *qkv, *ifp, *g2, *den, *num, *A, *x2; };
+  struct Buf { float *axc, *axn, *G, *x1, *xn2, *proj, *xca, *qkv, *g2, *den, *num, *A, *x2; };
   Buf carve(uint8_t* base, int rows) const {
     Carver c{base};
     Buf b;
@@ -885,7 +954,6 @@ class XLSTMLayer : public Layer {
     b.proj = c.take<float>(R * 2 * mi_);
     b.xca = c.take<float>(R * mi_);
     b.qkv = c.take<float>(R * 3 * mi_);
-    b.ifp = c.take<float>(R * 2 * nh_);
     b.g2 = c.take<float>(R * 2 * nh_);
     b.den = c.take<float>(R * nh_);
     b.num = c.take<float>(R * mi_);
@@ -926,11 +994,11 @@ class XLSTMLayer : public Layer {
     launch_k(c.ln, k_slstm_post, dim3(c.rows), dim3(kRowThreads), 2 * H_ * sizeof(float), c.s, so);
     // ---- mLSTM block (xlstm.py:198-219)
     linear(c, b.xn2, lp_, H_, mw1_, lp_, nullptr, 2 * mi_, H_, b.proj, 2 * mi_);  // x_proj, gate_proj
-    MlstmPreP mp{rc, b.proj, mi_, mconv_, smconv_, mcw_, mcb_, wq_, wk_, wv_, b.xca, b.qkv};
-    launch_k(c.ln, k_mlstm_pre, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, mp);
-    linear(c, b.qkv, kF32, 3 * mi_, gw_, kF32, gb_, 2 * nh_, 3 * mi_, b.ifp, 2 * nh_);  // igate/fgate, fp32 kept
-    MlstmGatesP gp{rc, b.ifp, b.qkv, mi_, nh_, hs_, n_, sn2_, m_, sm2_, b.g2, b.den};
-    launch_k(c.ln, k_mlstm_gates, dim3(c.rows), dim3(kRowThreads), 0, c.s, gp);
+    const int rpc = mid_rows(mi_, nh_);
+    MlstmMidP mp{rc, b.proj, mi_, nh_, hs_, mconv_, smconv_, mcw_, mcb_, wq_, wk_, wv_, gw_, gb_,
+                 n_, sn2_, m_, sm2_, b.xca, b.qkv, b.g2, b.den, rpc};
+    launch_k(c.ln, k_mlstm_mid, dim3(ceil_div(c.rows, rpc)), dim3(kRowThreads),
+             size_t(rpc) * (4 * mi_ + 2 * nh_) * sizeof(float), c.s, mp);
     OuterRowsParams op;
     op.at = {C_, sC_, c.slots, nullptr, c.rows, c.n_dev};
     op.nh = nh_; op.sh = hs_; op.sk = hs_;

@@ -51,7 +51,7 @@ extern "C" {
  * The four fp32-kept linears (example_model.py:106), BlockLinear, convs and norms
  * stay float32 in every mode. */
 #define B2E_FLAG_PDL 1           /* launch chain kernels with programmatic dependent launch */
-#define B2E_FLAG_PRIORITIES 2    /* launch the state-streaming kernels at low priority, the rest high */
+#define B2E_FLAG_NO_PRIORITIES 2 /* launch every chain at the same priority (default: the xLSTM tower's, the longest, first) */
 
 #define B2E_DTYPE_F32 0
 #define B2E_DTYPE_BF16 1
@@ -83,7 +83,7 @@ typedef struct b2e_engine_options {
   int32_t use_graphs;   /* 1: replay each step from a CUDA graph per batch bucket */
   int32_t lanes;        /* independent row shares per tower for large batches; 0 = default (1) */
   int32_t lane_min_rows;/* batches from this many rows use `lanes`; 0 = default (256) */
-  int32_t flags;        /* 0 = defaults; B2E_FLAG_PDL, B2E_FLAG_PRIORITIES turn scheduling options on */
+  int32_t flags;        /* 0 = defaults; B2E_FLAG_PDL turns PDL on, B2E_FLAG_NO_PRIORITIES turns priorities off */
 } b2e_engine_options;
 
 /* A named float32 host tensor, keyed like MultiTowerModel.state_dict(). */
