@@ -311,9 +311,10 @@ void Engine::enqueue(int rows, cudaStream_t s) {
       c.ln = ln_;
       c.ln_bulk = ln_bulk_;
       if (opt_.priorities && prio_hi_ != prio_lo_) {
-        // the xLSTM tower's chain is the longest: its kernels take SM slots first
+        // the xLSTM and Mamba2 towers' chains are the longest: their kernels
+        // take SM slots first
         c.ln.set_prio = c.ln_bulk.set_prio = true;
-        c.ln.prio = c.ln_bulk.prio = t == 0 ? prio_hi_ : prio_lo_;
+        c.ln.prio = c.ln_bulk.prio = t <= 1 ? prio_hi_ : prio_lo_;
       }
       const void* up = static_cast<const uint8_t*>(d_up_) + (size_t(l) * per * 4 * P + size_t(t) * P) * dtype_size(lp);
       tower_forward(towers_[t], ch, t, c, up, 4 * P, d_preds_ + size_t(l) * per * 4);

@@ -158,7 +158,8 @@ __global__ void k_set_rows(int* n, int v) { *n = v; }
 struct Mamba2PreP {
   RowCtx rc;
   const float* proj; int ldp; int mi, bc, nh;  // proj row: [x (mi) | z (mi) | b (bc) | c (bc)]
-  const float* dtp;                            // dt_proj output [row][nh]
+  const float* tin; int H;                     // the layer input (norm1 output, f32) [row][H]
+  const float* dtw; const float* dtb;          // dt_proj (fp32 kept): [nh][H], [nh]
   float* xconv; long long xcs; float* bconv; long long bcs; float* cconv; long long ccs;
   const float *wx, *bx, *wb, *bb, *wc, *bcv, *a;
   float *xs, *bs, *cs, *dt, *dc;
@@ -180,11 +181,20 @@ __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre(const Mamba2PreP p) 
     p.bs[size_t(r) * p.bc + c] = siluf_(conv_step(p.wb, p.bb, sb, p.bc, c, pr[2 * p.mi + c]));
     p.cs[size_t(r) * p.bc + c] = siluf_(conv_step(p.wc, p.bcv, sc, p.bc, c, pr[2 * p.mi + p.bc + c]));
   }
-  // dt = softplus(dt_proj(t)); decay = exp(a * dt) (mamba2.py:92-97)
-  for (int h = threadIdx.x; h < p.nh; h += blockDim.x) {
-    const float d = softplusf_(p.dtp[size_t(r) * p.nh + h]);
-    p.dt[size_t(r) * p.nh + h] = d;
-    p.dc[size_t(r) * p.nh + h] = expf(p.a[h] * d);
+  // dt = softplus(dt_proj(t)); decay = exp(a * dt) (mamba2.py:81, 92-97): one
+  // warp per head, a dot product of length H over the row's input
+  const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const float* tr = p.tin + size_t(r) * p.H;
+  for (int h = threadIdx.x >> 5; h < p.nh; h += nw) {
+    const float* w = p.dtw + size_t(h) * p.H;
+    float acc = 0.f;
+    for (int k = lane; k < p.H; k += 32) acc = fmaf(tr[k], w[k], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      const float d = softplusf_(acc + p.dtb[h]);
+      p.dt[size_t(r) * p.nh + h] = d;
+      p.dc[size_t(r) * p.nh + h] = expf(p.a[h] * d);
+    }
   }
 }
 
@@ -254,12 +264,11 @@ class Mamba2Layer : public Layer {
     xc_ = a.f32(l_xc_); bcs_ = a.f32(l_bc_); ccs_ = a.f32(l_cc_); ssm_ = a.f32(l_ssm_);
     sxc_ = a.stride(l_xc_); sbc_ = a.stride(l_bc_); scc_ = a.stride(l_cc_); sssm_ = a.stride(l_ssm_);
   }
-  struct Buf { float *proj, *dtp, *xs, *bs, *cs, *dt, *dc, *ys, *A; };
+  struct Buf { float *proj, *xs, *bs, *cs, *dt, *dc, *ys, *A; };
   Buf carve(uint8_t* base, int rows) const {
     Carver c{base};
     Buf b;
     b.proj = c.take<float>(size_t(rows) * n1_);
-    b.dtp = c.take<float>(size_t(rows) * nh_);
     b.xs = c.take<float>(size_t(rows) * mi_);
     b.bs = c.take<float>(size_t(rows) * bc_);
     b.cs = c.take<float>(size_t(rows) * bc_);
@@ -281,8 +290,7 @@ class Mamba2Layer : public Layer {
     const void* a1 = in_lp ? in_lp : in;
     const int a1t = in_lp ? lp_ : kF32;
     linear(c, a1, a1t, H_, w1_, lp_, nullptr, n1_, H_, b.proj, n1_);  // x, z, b, c (mamba2.py:77-80)
-    linear(c, in, kF32, H_, dtw_, kF32, dtb_, nh_, H_, b.dtp, nh_);   // dt_proj, fp32 kept (mamba2.py:81)
-    Mamba2PreP pp{rc, b.proj, n1_, mi_, bc_, nh_, b.dtp, xc_, sxc_, bcs_, sbc_, ccs_, scc_,
+    Mamba2PreP pp{rc, b.proj, n1_, mi_, bc_, nh_, in, H_, dtw_, dtb_, xc_, sxc_, bcs_, sbc_, ccs_, scc_,
                   wx_, bx_, wb_, bb_, wc_, bcv_, a_, b.xs, b.bs, b.cs, b.dt, b.dc};
     launch_k(c.ln, k_mamba2_pre, dim3(c.rows), dim3(kRowThreads), 0, c.s, pp);
     SsmColsParams sp;
