@@ -182,7 +182,8 @@ def make_batches(wl, n_symbols, world, rank, count, seed=0, backlog=None):
 
 
 def read_traffic_per_row(name: str):
-    """dram bytes per row of the dominant kernel from the committed ncu summary."""
+    """dram bytes per row of the dominant kernel from the committed ncu summary
+    profiles/<name>.txt (its `traffic_bytes_per_row:` line)."""
     p = REPO / "profiles" / f"{name}.txt"
     if not p.exists():
         return None
@@ -375,8 +376,9 @@ def main():
 
 
 def dominant_kernel_roofline(cfg, wl, dev, K):
-    """Mamba2's state step (ssm_cols) - the largest state stream of the step - timed
-    alone with CUDA events on its stream at one engine launch's shape."""
+    """Mamba2's state step - the largest state stream of the step, the bulk-copy
+    streaming kernel the engine runs (ssm_cols dispatches to it) - timed alone
+    with CUDA events on its stream at one engine launch's shape."""
     import torch
 
     from hackathon_b200 import kernels as KR
@@ -409,8 +411,8 @@ def dominant_kernel_roofline(cfg, wl, dev, K):
     t = e0.elapsed_time(e1) / n / 1e3
     per_row = 2 * nh * hs * bc * 4 + (nh * hs * 2 + 2 * bc + 2 * nh) * 4
     achieved = rows * per_row / t / 1e9
-    tr = read_traffic_per_row("ssm_cols")
-    return {"kernel": "ssm_cols (Mamba2 state step)", "bound": "hbm", "achieved": achieved, "peak": peak,
+    tr = read_traffic_per_row("ssm_bulk_d2")
+    return {"kernel": "ssm_bulk_kernel (Mamba2 state step, bulk-copy streaming)", "bound": "hbm", "achieved": achieved, "peak": peak,
             "unit": "GB/s", "frac": achieved / peak, "traffic": None if tr is None else tr * rows,
             "bytes_per_launch": rows * per_row, "launch_us": t * 1e6,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs" if pk.exists() else "fallback 6650 GB/s"}
