@@ -41,7 +41,7 @@ class ModelConfigC(C.Structure):
 class EngineOptionsC(C.Structure):
     _fields_ = [("device", C.c_int32), ("linear_dtype", C.c_int32), ("capacity", C.c_int32),
                 ("max_batch", C.c_int32), ("use_graphs", C.c_int32), ("lanes", C.c_int32),
-                ("lane_min_rows", C.c_int32), ("flags", C.c_int32)]
+                ("lane_min_rows", C.c_int32), ("flags", C.c_int32), ("lane_towers", C.c_int32)]
 
 
 class TensorC(C.Structure):
@@ -85,6 +85,17 @@ _SIGS = {
     "b2e_layer_slot_bytes": (C.c_int, [_P, _PI64]),
     "b2e_layer_read_slot": (C.c_int, [_P, _I32, _P, _I64]),
     "b2e_layer_write_slot": (C.c_int, [_P, _I32, _P, _I64]),
+    "b2e_ingest_create": (C.c_int, [_I32, _I32, C.POINTER(_P)]),
+    "b2e_ingest_destroy": (None, [_P]),
+    "b2e_ingest_feed": (C.c_int, [_P, _P, _I64, _PI32, _PI32]),
+    "b2e_ingest_next_other": (C.c_int, [_P, _P, _I64, _PI64]),
+    "b2e_ingest_push": (C.c_int, [_P, _I64, _P, _I64, _P, _PI32]),
+    "b2e_ingest_next_drop": (C.c_int, [_P, _PI32]),
+    "b2e_ingest_pending": (C.c_int, [_P, _PI64]),
+    "b2e_ingest_symbol_count": (C.c_int, [_P, _PI32]),
+    "b2e_ingest_symbol_name": (C.c_int, [_P, _I32, _P, _I64, _PI64]),
+    "b2e_ingest_take": (C.c_int, [_P, _I64, _P, _P, _P, _P, _PI32, _PI64]),
+    "b2e_encode_response": (C.c_int, [_P, _P, _I64, _I32, C.c_double, _P, _I64, _PI64]),
 }
 
 _lib = None

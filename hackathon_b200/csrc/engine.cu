@@ -299,12 +299,15 @@ void Engine::enqueue(int rows, cudaStream_t s) {
   B2E_CUDA(cudaEventRecord(fork_, s));
   for (int l = 0; l < L; ++l) {
     for (int t = 0; t < 4; ++t) {
+      // a tower outside lane_towers runs as one chain over all rows (lane 0)
+      const bool split = L > 1 && ((opt_.lane_towers >> t) & 1);
+      if (!split && l > 0) continue;
       Chain& ch = chains_[size_t(l) * 4 + t];
       B2E_CUDA(cudaStreamWaitEvent(ch.s, fork_, 0));
       StepCtx c;
       c.s = ch.s;
-      c.rows = per;
-      c.n_dev = d_nl_ + l;
+      c.rows = split ? per : rows;
+      c.n_dev = split ? d_nl_ + l : d_n_;
       c.slots = d_slots_ + size_t(l) * per;
       c.lp = opt_.lp;
       c.err = d_err_;
@@ -321,7 +324,9 @@ void Engine::enqueue(int rows, cudaStream_t s) {
       B2E_CUDA(cudaEventRecord(ch.done, ch.s));
     }
   }
-  for (int ci = 0; ci < 4 * L; ++ci) B2E_CUDA(cudaStreamWaitEvent(s, chains_[ci].done, 0));
+  for (int l = 0; l < L; ++l)
+    for (int t = 0; t < 4; ++t)
+      if (l == 0 || ((opt_.lane_towers >> t) & 1)) B2E_CUDA(cudaStreamWaitEvent(s, chains_[size_t(l) * 4 + t].done, 0));
 }
 
 void Engine::launch(int n, cudaStream_t s) {

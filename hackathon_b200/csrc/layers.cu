@@ -664,6 +664,175 @@ __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) 
     store_as(p.at, p.xn2, size_t(r) * p.H + e, (x1[e] - gm[0]) * gr[0] * p.mlnw[e]);
 }
 
+// The whole sLSTM block for kSlRows rows per CTA (xlstm.py:239-318) and the
+// mLSTM block's input LayerNorm (xlstm.py:182,202): LayerNorm, conv + SiLU, the
+// eight fp32 BlockLinears (i, f from the conv branch, z, o from the normed
+// input, each plus a BlockLinear of the old h), the stabilized cell, GroupNorm
+// and skip. One thread per hidden unit u holds the four gates of u for every
+// row of the CTA; the weights are packed k-major ([2bs][4][H]) so a warp's 32
+// units read 128 contiguous bytes per gate and k, shared by the CTA's rows.
+constexpr int kSlRows = 16;
+constexpr int kSlMaxGroups = 16;  // sLSTM heads (GroupNorm groups) per row
+constexpr size_t kSlSmemMax = 96 * 1024;
+struct SlstmFusedP {
+  RowCtx rc;
+  const float* t; int H, nbl, bs;
+  const float* lnw;
+  float* conv; long long cs; const float* cw; const float* cb;
+  float *hs_, *cs_, *ns_, *ms_; long long h_s, c_s, n_s, m_s;
+  const float* wt;    // [2bs][4][H]: k (input half, then state half), gate i f z o, unit
+  const float* bias;  // [4][H]
+  const float *gnw, *gnb, *mlnw;
+  float* x1; void* xn2; int at;
+};
+// HT: the hidden size when fixed at compile time (shared-memory row offsets
+// and weight strides become immediates), else 0.
+template <int RB, int HT>
+__global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
+  pdl_wait();
+  pdl_launch();
+  const int r0 = blockIdx.x * RB;
+  const int nr = min(RB, live_rows(p.rc.n_dev, p.rc.rows) - r0);
+  if (nr <= 0) return;
+  extern __shared__ float4 sl_raw[];
+  const int H = HT ? HT : p.H, u = threadIdx.x;  // blockDim.x == H
+  float* xc = reinterpret_cast<float*>(sl_raw);  // [RB][H] conv+SiLU branch, later the cell output y
+  float* xn = xc + RB * H;                       // [RB][H] input, then LayerNorm(input), later x1
+  float* hb = xn + RB * H;                       // [RB][H] old h
+  __shared__ float gm[RB * kSlMaxGroups], gr[RB * kSlMaxGroups];
+  __shared__ long long slot[RB];
+  if (u < RB) slot[u] = u < nr ? row_slot(p.rc, r0 + u) : 0;
+#pragma unroll
+  for (int r = 0; r < RB; ++r) xn[r * H + u] = r < nr ? p.t[size_t(r0 + r) * H + u] : 0.f;
+  __syncthreads();
+  group_stats(xn, RB, H, 1e-5f, gm, gr);  // LayerNorm(bias=False) per row (xlstm.py:287,307)
+  {
+    // every row's conv taps and h first, then the updates
+    float s0[RB], s1[RB], s2[RB], ho[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      if (r < nr) {
+        const float* st = p.conv + slot[r] * p.cs;
+        s0[r] = st[u];
+        s1[r] = st[H + u];
+        s2[r] = st[2 * H + u];
+        ho[r] = p.hs_[slot[r] * p.h_s + u];
+      } else {
+        s0[r] = s1[r] = s2[r] = ho[r] = 0.f;
+      }
+    }
+    const float w0 = p.cw[u], w1 = p.cw[H + u], w2 = p.cw[2 * H + u], w3 = p.cw[3 * H + u], cb = p.cb[u], lw = p.lnw[u];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      const float x = (xn[r * H + u] - gm[r]) * gr[r] * lw;
+      // CausalConv1d over [state, x] (model/modules.py:37-41) and SiLU (xlstm.py:309-310)
+      float acc = w0 * s0[r];
+      acc = fmaf(w1, s1[r], acc);
+      acc = fmaf(w2, s2[r], acc);
+      acc = fmaf(w3, x, acc);
+      xc[r * H + u] = r < nr ? siluf_(acc + cb) : 0.f;
+      xn[r * H + u] = x;
+      hb[r * H + u] = ho[r];
+      if (r < nr) {
+        float* st = p.conv + slot[r] * p.cs;
+        st[u] = s1[r];
+        st[H + u] = s2[r];
+        st[2 * H + u] = x;
+      }
+    }
+  }
+  __syncthreads();
+  // gates: acc[g][r] = sum_k W_g[u][k] * a_g[r][k] over k < bs (input half:
+  // the conv branch for i, f, the normed input for z, o) and bs <= k < 2bs
+  // (the old h of u's block, all gates) (xlstm.py:250-253, 312-315)
+  const int bs = p.bs, j0 = (u / bs) * bs;
+  float acc[4][RB];
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+#pragma unroll
+    for (int r = 0; r < RB; ++r) acc[g][r] = 0.f;
+  const float* wt = p.wt + u;
+  const size_t kst = size_t(4) * H;  // one k of the packed weights
+  for (int half = 0; half < 2; ++half) {
+    const float* a0 = (half ? hb : xc) + j0;
+    const float* a1 = (half ? hb : xn) + j0;
+    const float* wk = wt + size_t(half) * bs * kst;
+    for (int k = 0; k < bs; k += 4) {
+      float w[4][4];  // [kk][gate]
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) w[kk][g] = __ldg(wk + (k + kk) * kst + size_t(g) * H);
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const float4 a = *reinterpret_cast<const float4*>(a0 + r * H + k);
+        const float4 b = *reinterpret_cast<const float4*>(a1 + r * H + k);
+        acc[0][r] = fmaf(a.w, w[3][0], fmaf(a.z, w[2][0], fmaf(a.y, w[1][0], fmaf(a.x, w[0][0], acc[0][r]))));
+        acc[1][r] = fmaf(a.w, w[3][1], fmaf(a.z, w[2][1], fmaf(a.y, w[1][1], fmaf(a.x, w[0][1], acc[1][r]))));
+        acc[2][r] = fmaf(b.w, w[3][2], fmaf(b.z, w[2][2], fmaf(b.y, w[1][2], fmaf(b.x, w[0][2], acc[2][r]))));
+        acc[3][r] = fmaf(b.w, w[3][3], fmaf(b.z, w[2][3], fmaf(b.y, w[1][3], fmaf(b.x, w[0][3], acc[3][r]))));
+      }
+    }
+  }
+  __syncthreads();  // xc, xn, hb are free
+  {
+    const float bi = p.bias[u], bf = p.bias[H + u], bz = p.bias[2 * H + u], bo = p.bias[3 * H + u];
+    constexpr int RC = 8;  // rows whose state loads are in flight together
+#pragma unroll
+    for (int rc = 0; rc < RB; rc += RC) {
+      float co[RC], no[RC], mo[RC];
+#pragma unroll
+      for (int q = 0; q < RC; ++q) {
+        const int r = rc + q;
+        const bool on = r < nr;
+        co[q] = on ? p.cs_[slot[r] * p.c_s + u] : 0.f;
+        no[q] = on ? p.ns_[slot[r] * p.n_s + u] : 0.f;
+        mo[q] = on ? p.ms_[slot[r] * p.m_s + u] : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < RC; ++q) {
+        const int r = rc + q;
+        // SLSTMCell.forward (xlstm.py:247-262)
+        const float i = acc[0][r] + bi, f = acc[1][r] + bf, z = acc[2][r] + bz, o = acc[3][r] + bo;
+        const float lfm = mo[q] + logsigmoidf_(f);
+        const float mn = fmaxf(i, lfm);
+        const float og = sigmoidf_(o);
+        const float ig = expf(i - mn);
+        const float fg = expf(lfm - mn);
+        const float cn = fg * co[q] + ig * tanhf(z);
+        const float nv = fg * no[q] + ig;
+        const float yv = og * cn / (nv + 1e-6f);
+        xc[r * H + u] = yv;
+        if (r < nr) {
+          p.cs_[slot[r] * p.c_s + u] = cn;
+          p.ns_[slot[r] * p.n_s + u] = nv;
+          p.ms_[slot[r] * p.m_s + u] = mn;
+          p.hs_[slot[r] * p.h_s + u] = yv;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int gs = H / p.nbl, gu = u / gs;
+  group_stats(xc, RB * p.nbl, gs, 1e-5f, gm, gr);  // GroupNorm(num_heads) per row (xlstm.py:300,316)
+  {
+    const float gw = p.gnw[u], gb = p.gnb[u];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      const float t = r < nr ? p.t[size_t(r0 + r) * H + u] : 0.f;
+      const float v = (xc[r * H + u] - gm[r * p.nbl + gu]) * gr[r * p.nbl + gu] * gw + gb + t;  // + skip (xlstm.py:318)
+      xn[r * H + u] = v;
+      if (r < nr) p.x1[size_t(r0 + r) * H + u] = v;
+    }
+  }
+  __syncthreads();
+  group_stats(xn, RB, H, 1e-5f, gm, gr);  // mLSTM block LayerNorm (xlstm.py:182,202)
+  const float mw = p.mlnw[u];
+#pragma unroll
+  for (int r = 0; r < RB; ++r)
+    if (r < nr) store_as(p.at, p.xn2, size_t(r0 + r) * H + u, (xn[r * H + u] - gm[r]) * gr[r] * mw);
+}
+
 // The mLSTM block between x_proj/gate_proj and the cell's state update, for
 // kMidRows rows per CTA (xlstm.py:92-132, 198-213): conv1d + SiLU, the q/k/v
 // BlockLinears (4x4 blocks), the input/forget gate projections over cat(q,k,v)
@@ -872,7 +1041,18 @@ class XLSTMLayer : public Layer {
     H_ = d.H; nbl_ = d.slstm_heads(); bs_ = d.slstm_bs();
     mi_ = d.mlstm_inner(); nh_ = d.mlstm_heads(); hs_ = d.mlstm_hs();
     B2E_CUDA(cudaFuncSetAttribute(k_mlstm_mid, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmemMax)));
+    // the fused sLSTM kernel: one thread per hidden unit, 16-byte activation
+    // vectors inside a block, kSlRows rows of three activation planes in smem
+    fused_ = H_ % 32 == 0 && H_ >= kSlRows && H_ <= 512 && bs_ % 4 == 0 && nbl_ <= kSlMaxGroups &&
+             fused_smem() <= kSlSmemMax;
+    if (fused_) {
+      B2E_CUDA(cudaFuncSetAttribute(k_slstm_fused<kSlRows, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(fused_smem())));
+      B2E_CUDA(cudaFuncSetAttribute(k_slstm_fused<kSlRows, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(fused_smem())));
+    }
   }
+  size_t fused_smem() const { return size_t(3) * kSlRows * H_ * sizeof(float); }
   void declare_state(StateArena& a) override {
     // (xlstm.py:331-336, 276-282, 232-236, 150-156) in init_state order
     l_sconv_ = a.add_conv(H_, 3);
@@ -912,6 +1092,17 @@ class XLSTMLayer : public Layer {
             std::copy(b, b + bs, row + bs);
           }
     });
+    if (fused_) {
+      // Wt[k][g][u]: k < bs the input half, k >= bs the state half, u = j*bs + e
+      o_swt_ = w.reserve(size_t(4) * 2 * bs * H * 4, [=](uint8_t* dst) {
+        float* o = reinterpret_cast<float*>(dst);
+        const size_t Hs = H;
+        for (int k = 0; k < 2 * bs; ++k)
+          for (int g = 0; g < 4; ++g)
+            for (size_t u = 0; u < Hs; ++u)
+              o[(size_t(k) * 4 + g) * Hs + u] = k < bs ? win[g][u * bs + k] : wst[g][u * bs + (k - bs)];
+      });
+    }
     o_sbias_ = w.add_rows({{bst[0], H}, {bst[1], H}, {bst[2], H}, {bst[3], H}}, kF32);
     o_sgnw_ = w.add(s.get(p + "slstm.group_norm.weight", H), H, kF32);
     o_sgnb_ = w.add(s.get(p + "slstm.group_norm.bias", H), H, kF32);
@@ -938,6 +1129,7 @@ class XLSTMLayer : public Layer {
   void resolve(const WeightPack& w, const StateArena& a) override {
     slnw_ = w.ptr<float>(o_slnw_); scw_ = w.ptr<float>(o_scw_); scb_ = w.ptr<float>(o_scb_);
     swcat_ = w.ptr<float>(o_swcat_); sbias_ = w.ptr<float>(o_sbias_);
+    swt_ = fused_ ? w.ptr<float>(o_swt_) : nullptr;
     sgnw_ = w.ptr<float>(o_sgnw_); sgnb_ = w.ptr<float>(o_sgnb_);
     skip_ = w.ptr<float>(o_skip_); mlnw_ = w.ptr<float>(o_mlnw_); mw1_ = w.ptr(o_mw1_);
     wq_ = w.ptr<float>(o_wq_); wk_ = w.ptr<float>(o_wk_); wv_ = w.ptr<float>(o_wv_);
@@ -979,27 +1171,36 @@ class XLSTMLayer : public Layer {
     const Buf b = carve(scratch, c.rows);
     const RowCtx rc{c.n_dev, c.rows, c.slots};
     // ---- sLSTM block (xlstm.py:304-318)
-    SlstmPreP sp{rc, in, H_, nbl_, bs_, slnw_, sconv_, ssconv_, scw_, scb_, sh_, ssh_, b.axc, b.axn};
-    launch_k(c.ln, k_slstm_pre, dim3(c.rows), dim3(kRowThreads), H_ * sizeof(float), c.s, sp);
-    // i, f from the conv branch, z, o from the normed input, each + BlockLinear(h) + bias (xlstm.py:312-315)
-    for (int g0 = 0; g0 < 4 * nbl_; g0 += kMaxGroups) {
-      GemmParams gp;
-      gp.groups = std::min(kMaxGroups, 4 * nbl_ - g0);
-      for (int q = 0; q < gp.groups; ++q) {
-        const int gi = g0 + q, g = gi / nbl_, j = gi % nbl_;
-        GemmGroup& gg = gp.g[q];
-        gg.A = (g < 2 ? b.axc : b.axn) + size_t(j) * 2 * bs_;
-        gg.W = swcat_ + size_t(gi) * bs_ * 2 * bs_;
-        gg.bias = sbias_ + size_t(g) * H_ + j * bs_;
-        gg.C = b.G + size_t(g) * H_ + j * bs_;
+    if (fused_) {
+      SlstmFusedP fp{rc, in, H_, nbl_, bs_, slnw_, sconv_, ssconv_, scw_, scb_, sh_, sc_, sn_, sm_, ssh_, ssc_, ssn_, ssm_,
+                     swt_, sbias_, sgnw_, sgnb_, mlnw_, b.x1, b.xn2, lp_};
+      if (H_ == 256)
+        launch_k(c.ln, k_slstm_fused<kSlRows, 256>, dim3(ceil_div(c.rows, kSlRows)), dim3(H_), fused_smem(), c.s, fp);
+      else
+        launch_k(c.ln, k_slstm_fused<kSlRows, 0>, dim3(ceil_div(c.rows, kSlRows)), dim3(H_), fused_smem(), c.s, fp);
+    } else {
+      SlstmPreP sp{rc, in, H_, nbl_, bs_, slnw_, sconv_, ssconv_, scw_, scb_, sh_, ssh_, b.axc, b.axn};
+      launch_k(c.ln, k_slstm_pre, dim3(c.rows), dim3(kRowThreads), H_ * sizeof(float), c.s, sp);
+      // i, f from the conv branch, z, o from the normed input, each + BlockLinear(h) + bias (xlstm.py:312-315)
+      for (int g0 = 0; g0 < 4 * nbl_; g0 += kMaxGroups) {
+        GemmParams gp;
+        gp.groups = std::min(kMaxGroups, 4 * nbl_ - g0);
+        for (int q = 0; q < gp.groups; ++q) {
+          const int gi = g0 + q, g = gi / nbl_, j = gi % nbl_;
+          GemmGroup& gg = gp.g[q];
+          gg.A = (g < 2 ? b.axc : b.axn) + size_t(j) * 2 * bs_;
+          gg.W = swcat_ + size_t(gi) * bs_ * 2 * bs_;
+          gg.bias = sbias_ + size_t(g) * H_ + j * bs_;
+          gg.C = b.G + size_t(g) * H_ + j * bs_;
+        }
+        gp.M_max = c.rows; gp.M_dev = c.n_dev; gp.N = bs_; gp.K = 2 * bs_;
+        gp.lda = 2 * H_; gp.ldw = 2 * bs_; gp.ldc = 4 * H_;
+        gp.ln = c.ln;
+        gemm(gp, c.s);
       }
-      gp.M_max = c.rows; gp.M_dev = c.n_dev; gp.N = bs_; gp.K = 2 * bs_;
-      gp.lda = 2 * H_; gp.ldw = 2 * bs_; gp.ldc = 4 * H_;
-      gp.ln = c.ln;
-      gemm(gp, c.s);
+      SlstmPostP so{rc, b.G, in, H_, nbl_, sh_, sc_, sn_, sm_, ssh_, ssc_, ssn_, ssm_, sgnw_, sgnb_, mlnw_, b.x1, b.xn2, lp_};
+      launch_k(c.ln, k_slstm_post, dim3(c.rows), dim3(kRowThreads), 2 * H_ * sizeof(float), c.s, so);
     }
-    SlstmPostP so{rc, b.G, in, H_, nbl_, sh_, sc_, sn_, sm_, ssh_, ssc_, ssn_, ssm_, sgnw_, sgnb_, mlnw_, b.x1, b.xn2, lp_};
-    launch_k(c.ln, k_slstm_post, dim3(c.rows), dim3(kRowThreads), 2 * H_ * sizeof(float), c.s, so);
     // ---- mLSTM block (xlstm.py:198-219)
     linear(c, b.xn2, lp_, H_, mw1_, lp_, nullptr, 2 * mi_, H_, b.proj, 2 * mi_);  // x_proj, gate_proj
     const int rpc = mid_rows(mi_, nh_);
@@ -1042,6 +1243,9 @@ class XLSTMLayer : public Layer {
   int lp_, H_, nbl_, bs_, mi_, nh_, hs_;
   mutable size_t scratch_ = 0;
   int l_sconv_, l_sh_, l_sc_, l_sn_, l_sm_, l_mconv_, l_C_, l_n_, l_m_;
+  bool fused_ = false;
+  size_t o_swt_ = 0;
+  const float* swt_ = nullptr;
   size_t o_slnw_, o_scw_, o_scb_, o_swcat_, o_sbias_, o_sgnw_, o_sgnb_, o_skip_, o_mlnw_, o_mw1_, o_wq_, o_wk_,
       o_wv_, o_mcw_, o_mcb_, o_gw_, o_gb_, o_ongw_, o_ongb_, o_down_, o_fnw_;
   const float *slnw_, *scw_, *scb_, *swcat_, *sbias_, *sgnw_, *sgnb_, *skip_, *mlnw_, *wq_, *wk_, *wv_, *mcw_,

@@ -19,11 +19,11 @@ from .config import CONV_K, TOWER_KINDS, ModelConfig
 
 
 def _opts(device: int, linear_dtype: str, capacity: int, max_batch: int, graphs: bool, lanes: int = 0,
-          lane_min_rows: int = 0, flags: int = 0) -> _lib.EngineOptionsC:
+          lane_min_rows: int = 0, flags: int = 0, lane_towers: int = 0) -> _lib.EngineOptionsC:
     if linear_dtype not in _lib.DTYPES:
         raise ValueError(f"linear_dtype must be one of {sorted(_lib.DTYPES)}, got {linear_dtype!r}")
     return _lib.EngineOptionsC(int(device), _lib.DTYPES[linear_dtype], int(capacity), int(max_batch), int(graphs),
-                               int(lanes), int(lane_min_rows), int(flags))
+                               int(lanes), int(lane_min_rows), int(flags), int(lane_towers))
 
 
 def leaf_layout(kind: str, cfg: ModelConfig) -> List[Tuple[Tuple[int, ...], np.dtype]]:
@@ -73,14 +73,14 @@ class EnsembleEngine:
 
     def __init__(self, cfg: ModelConfig, state_dict: Dict[str, np.ndarray], *, device: int = 0,
                  linear_dtype: str = "fp32", capacity: int = 16, max_batch: int = 16, graphs: bool = True,
-                 lanes: int = 0, lane_min_rows: int = 0, flags: int = 0):
+                 lanes: int = 0, lane_min_rows: int = 0, flags: int = 0, lane_towers: int = 0):
         self.cfg, self.device, self.linear_dtype = cfg, device, linear_dtype
         self.capacity, self.max_batch = capacity, max_batch
         L = _lib.lib()
         arr, keep = _lib.tensor_array(state_dict)
         h = C.c_void_p()
         cc, oo = _lib.model_config_c(cfg), _opts(device, linear_dtype, capacity, max_batch, graphs, lanes,
-                                                 lane_min_rows, flags)
+                                                 lane_min_rows, flags, lane_towers)
         _lib.check(L.b2e_engine_create(C.byref(cc), C.byref(oo), arr, len(state_dict), C.byref(h)))
         del keep
         self._h = h

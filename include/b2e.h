@@ -23,6 +23,14 @@
  *   b2e_layer_*         one layer's forward(x, state, mask) with its own state
  *                       table (model/xlstm.py:355, model/mamba2.py:62,
  *                       model/retnet.py:38, model/hawk.py:60)
+ *   b2e_ingest_*        the client's request path up to process_batch:
+ *                       ProtocolHandler.decode of each newline-delimited line
+ *                       (protocol.py:86-103, SocketReader.read_all_available
+ *                       :134-160), _handle_request's per-symbol queues
+ *                       (client.py:156-173), _gather_requests (client.py:202-220)
+ *                       and process_batch's rounds (example_model.py:885-899)
+ *   b2e_encode_response ProtocolHandler.encode of an InferenceResponse
+ *                       (protocol.py:80-84, protocol.py:38-44)
  */
 #ifndef B2E_H
 #define B2E_H
@@ -84,6 +92,7 @@ typedef struct b2e_engine_options {
   int32_t lanes;        /* independent row shares per tower for large batches; 0 = default (1) */
   int32_t lane_min_rows;/* batches from this many rows use `lanes`; 0 = default (256) */
   int32_t flags;        /* 0 = defaults; B2E_FLAG_PDL turns PDL on, B2E_FLAG_NO_PRIORITIES turns priorities off */
+  int32_t lane_towers;  /* bit t set: tower t (0 xLSTM, 1 Mamba2, 2 RetNet, 3 Hawk) splits into `lanes`; 0 = every tower */
 } b2e_engine_options;
 
 /* A named float32 host tensor, keyed like MultiTowerModel.state_dict(). */
@@ -182,6 +191,57 @@ B2E_API int b2e_layer_reset_slots(b2e_layer* l, const int32_t* slots, int32_t n)
 B2E_API int b2e_layer_slot_bytes(const b2e_layer* l, int64_t* bytes);
 B2E_API int b2e_layer_read_slot(b2e_layer* l, int32_t slot, void* host, int64_t bytes);
 B2E_API int b2e_layer_write_slot(b2e_layer* l, int32_t slot, const void* host, int64_t bytes);
+
+/* ---- request ingest (host only; no GPU needed) ----
+ * Raw bytes from the server's socket go in; requests come out as flat arrays
+ * (symbol ids, unique ids, float32 feature rows) in process_batch's round order,
+ * with no per-request or per-float Python objects.
+ *
+ * b2e_ingest_feed splits the bytes into lines (a partial last line waits for
+ * the next feed). A line that json.loads would read as an "inference_request"
+ * message with exactly the fields of InferenceRequest (unique_ids: integers
+ * within int64, symbols: ASCII-escaped strings, features: rows of num_features
+ * numbers, timestamp: any value) is decoded natively: for i < min(len(unique_ids),
+ * len(symbols), len(features)) request i is appended to its symbol's queue, or,
+ * when that queue already holds max_queue requests, dropped and reported by
+ * b2e_ingest_next_drop (client.py:169-173). Every other non-empty line (other
+ * message types, malformed JSON, other field types, non-ASCII bytes) is kept
+ * whole for the caller's own decoder (b2e_ingest_next_other), and the feed
+ * stops right after it, so that what the caller does with it (a request it
+ * queues with b2e_ingest_push) comes before the lines after it; feed again
+ * (len 0 is fine) to go on.
+ * Symbols get dense ids in order of first sight; that order is the order of the
+ * reference's request_queues dict, so it is also process_batch's symbol order.
+ * b2e_ingest_take drains every queue at once (_gather_requests) and writes the
+ * rows round by round: round k holds the k-th queued request of every symbol
+ * that has one, symbols in id order (example_model.py:885-899). Buffers hold at
+ * least b2e_ingest_pending() rows (round_rows: that many entries). */
+typedef struct b2e_ingest b2e_ingest;
+B2E_API int b2e_ingest_create(int32_t num_features, int32_t max_queue, b2e_ingest** out);
+B2E_API void b2e_ingest_destroy(b2e_ingest* g);
+B2E_API int b2e_ingest_feed(b2e_ingest* g, const char* data, int64_t len, int32_t* n_requests, int32_t* n_other);
+/* The oldest kept line (without its newline); *len = -1 when there is none, or
+ * the line's length when cap is too small (nothing is consumed then). */
+B2E_API int b2e_ingest_next_other(b2e_ingest* g, char* buf, int64_t cap, int64_t* len);
+/* Queue one request the caller decoded itself (symbol: UTF-8 bytes); *queued
+ * = 0 when its symbol's queue was full (then reported as a drop). */
+B2E_API int b2e_ingest_push(b2e_ingest* g, int64_t unique_id, const char* symbol, int64_t symbol_len,
+                            const float* features, int32_t* queued);
+/* Symbol id of the oldest dropped request, or -1 when there is none. */
+B2E_API int b2e_ingest_next_drop(b2e_ingest* g, int32_t* symbol);
+B2E_API int b2e_ingest_pending(const b2e_ingest* g, int64_t* rows);
+B2E_API int b2e_ingest_symbol_count(const b2e_ingest* g, int32_t* n);
+/* UTF-8 name of a symbol id; *len as in b2e_ingest_next_other. */
+B2E_API int b2e_ingest_symbol_name(const b2e_ingest* g, int32_t symbol, char* buf, int64_t cap, int64_t* len);
+B2E_API int b2e_ingest_take(b2e_ingest* g, int64_t cap, int32_t* symbols, int64_t* unique_ids, float* features,
+                            int32_t* round_rows, int32_t* n_rounds, int64_t* n_rows);
+
+/* The bytes ProtocolHandler.encode(InferenceResponse(unique_ids, predictions,
+ * client_timestamp)) produces: json.dumps' layout and float repr (predictions
+ * widened float32 -> double as p.astype(float).tolist() does), newline
+ * included. *len = bytes written, or the size needed when cap is too small. */
+B2E_API int b2e_encode_response(const int64_t* unique_ids, const float* predictions, int64_t n, int32_t n_out,
+                                double client_timestamp, char* buf, int64_t cap, int64_t* len);
 
 #ifdef __cplusplus
 }

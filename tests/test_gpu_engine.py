@@ -261,13 +261,15 @@ def test_process_batch_on_gpu_matches_reference(capsys):
     client.close()
 
 
-def test_large_batch_split_into_lanes_matches_oracle():
+@pytest.mark.parametrize("lane_towers", [0, 0b0011, 0b0100])
+def test_large_batch_split_into_lanes_matches_oracle(lane_towers):
     """300 rows: the 512-row bucket runs as two lanes of 256 (the second with 44
-    live rows), each tower on its own stream per lane; every row still equals the
-    oracle, and two steps in a row keep the state consistent."""
+    live rows) for the towers in lane_towers (0: all), one chain over all rows
+    for the others; every row still equals the oracle, and two steps in a row
+    keep the state consistent."""
     cfg = C.ModelConfig(hidden_size=64, proj_size=128, tower_depth=2, num_heads=4, num_features=79)
     sd = Wt.generate_model(cfg, seed=3)
-    eng = EnsembleEngine(cfg, sd, capacity=400, max_batch=512, lanes=2)
+    eng = EnsembleEngine(cfg, sd, capacity=400, max_batch=512, lanes=2, lane_towers=lane_towers)
     orc = O.Oracle(cfg, sd)
     rng = np.random.default_rng(8)
     slots = rng.permutation(400)[:300].astype(np.int32)
