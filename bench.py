@@ -308,15 +308,20 @@ def main():
         eng.close()
         return
 
-    # ---- end to end through the C-ABI with host buffers (e2e)
+    # ---- end to end through the C-ABI with host buffers (e2e): b2e_engine_submit
+    # / b2e_engine_wait with two steps in flight, so a step's host->device copy
+    # and start overlap the previous step's end
     barrier(world)
     t0 = time.perf_counter()
     h2d = d2h = 0
     for k in range(K):
         i = Wm + K + k
-        eng.step(batches[i], feats[i])
-        h2d += 16 + 4 * len(batches[i]) + 4 * F * len(batches[i])
+        eng.submit(batches[i], feats[i])
+        if k:
+            eng.wait()
+        h2d += 4 + 4 * len(batches[i]) + 4 * F * len(batches[i])
         d2h += 16 * len(batches[i])
+    eng.wait()
     e2e_s = time.perf_counter() - t0
     e2e_rows = float(sum(len(batches[Wm + K + k]) for k in range(K)))
     e2e_max = allreduce(e2e_s, "max", world, dev)
@@ -342,7 +347,7 @@ def main():
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline(cfg, wl)
 
-    per_req = np.repeat(step_ms, [len(batches[Wm + k]) for k in range(K)])
+    per_req = np.repeat(step_ms, [len(batches[Wm + k]) for k in range(len(step_ms))])
     if rank == 0:
         line = {
             "metric": "requests/s (full 4-tower ensemble decode step, micro-batches <= %d)" % wl["max_batch"],

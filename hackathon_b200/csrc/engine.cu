@@ -153,22 +153,34 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   if (lp != kF32) B2E_CUDA(cudaMalloc(&d_feats_lp_, size_t(o.max_batch) * fpad_ * dtype_size(lp)));
   ob_ = pack_.ptr<float>(o_ob_);
 
-  // ---- step I/O
+  // ---- step I/O: kSets sets, so a host step's copies overlap the step before
   const size_t R = o.max_batch;
-  feats_off_ = (16 + 4 * R + 255) & ~size_t(255);
+  slots_off_ = 256;  // n at 0, lane row counts from 16
+  feats_off_ = (slots_off_ + 4 * R + 255) & ~size_t(255);
   preds_off_ = (feats_off_ + 4 * R * F + 255) & ~size_t(255);
   const size_t io = preds_off_ + 16 * R + 128;
-  B2E_CUDA(cudaMalloc(&d_io_, io));
-  B2E_CUDA(cudaMallocHost(&h_io_, io));
-  d_n_ = reinterpret_cast<int*>(d_io_);
-  d_slots_ = reinterpret_cast<int*>(d_io_ + 16);
-  d_feats_ = reinterpret_cast<float*>(d_io_ + feats_off_);
-  d_preds_ = reinterpret_cast<float*>(d_io_ + preds_off_);
-  d_err_ = reinterpret_cast<int*>(d_io_ + preds_off_ + 16 * R);
-  d_nl_ = d_err_ + 4;
-  B2E_CUDA(cudaMemset(d_io_, 0, io));
+  for (IoSet& st : io_) {
+    B2E_CUDA(cudaMalloc(&st.d_io, io));
+    B2E_CUDA(cudaMallocHost(&st.h_io, io));
+    B2E_CUDA(cudaMemset(st.d_io, 0, io));
+    st.d_n = reinterpret_cast<int*>(st.d_io);
+    st.d_nl = st.d_n + 4;
+    st.d_slots = reinterpret_cast<int*>(st.d_io + slots_off_);
+    st.d_feats = reinterpret_cast<float*>(st.d_io + feats_off_);
+    st.d_preds = reinterpret_cast<float*>(st.d_io + preds_off_);
+    B2E_CUDA(cudaEventCreateWithFlags(&st.in_ready, cudaEventDisableTiming));
+    B2E_CUDA(cudaEventCreateWithFlags(&st.stepped, cudaEventDisableTiming));
+    B2E_CUDA(cudaEventCreateWithFlags(&st.done, cudaEventDisableTiming));
+  }
+  B2E_CUDA(cudaMalloc(&d_err_, 256));
+  B2E_CUDA(cudaMemset(d_err_, 0, 256));
+  B2E_CUDA(cudaMalloc(&d_rs_, 4 * R));
+  B2E_CUDA(cudaMallocHost(&h_rs_, 4 * R));
   B2E_CUDA(cudaStreamCreateWithFlags(&s0_, cudaStreamNonBlocking));
+  B2E_CUDA(cudaStreamCreateWithFlags(&s_h2d_, cudaStreamNonBlocking));
+  B2E_CUDA(cudaStreamCreateWithFlags(&s_d2h_, cudaStreamNonBlocking));
   B2E_CUDA(cudaEventCreateWithFlags(&fork_, cudaEventDisableTiming));
+  B2E_CUDA(cudaEventCreateWithFlags(&last_step_, cudaEventDisableTiming));
   int prio_low = 0, prio_high = 0;
   B2E_CUDA(cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high));
   ln_.pdl = ln_bulk_.pdl = o.pdl;
@@ -177,24 +189,35 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   seen_.assign(o.capacity, 0);
 
   arena_.reset_all(s0_);
-  B2E_CUDA(cudaStreamSynchronize(s0_));
+  B2E_CUDA(cudaDeviceSynchronize());
 }
 
 Engine::~Engine() {
   cudaSetDevice(opt_.device);
-  if (s0_) cudaStreamSynchronize(s0_);
+  cudaDeviceSynchronize();
   for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
   for (auto& ch : chains_) {
     if (ch.s) cudaStreamDestroy(ch.s);
     if (ch.done) cudaEventDestroy(ch.done);
     if (ch.x) cudaFree(ch.x);
   }
+  for (IoSet& st : io_) {
+    if (st.d_io) cudaFree(st.d_io);
+    if (st.h_io) cudaFreeHost(st.h_io);
+    if (st.in_ready) cudaEventDestroy(st.in_ready);
+    if (st.stepped) cudaEventDestroy(st.stepped);
+    if (st.done) cudaEventDestroy(st.done);
+  }
   if (fork_) cudaEventDestroy(fork_);
+  if (last_step_) cudaEventDestroy(last_step_);
   if (s0_) cudaStreamDestroy(s0_);
-  if (d_io_) cudaFree(d_io_);
+  if (s_h2d_) cudaStreamDestroy(s_h2d_);
+  if (s_d2h_) cudaStreamDestroy(s_d2h_);
+  if (d_err_) cudaFree(d_err_);
+  if (d_rs_) cudaFree(d_rs_);
+  if (h_rs_) cudaFreeHost(h_rs_);
   if (d_up_) cudaFree(d_up_);
   if (d_feats_lp_) cudaFree(d_feats_lp_);
-  if (h_io_) cudaFreeHost(h_io_);
 }
 
 int Engine::bucket(int n) const {
@@ -270,31 +293,32 @@ void Engine::tower_forward(const Tower& tw, Chain& ch, int idx, const StepCtx& c
   if (!fuse) output_proj_rows(c, ch.x, ow_, ob_, H, preds, 4, idx);  // shared output_proj (model/inference_model.py:142)
 }
 
-void Engine::enqueue(int rows, cudaStream_t s) {
+void Engine::enqueue(int rows, int b, cudaStream_t s) {
+  const IoSet& io = io_[b];
   const int L = lanes_for(rows);
   const int per = (rows + L - 1) / L;
-  k_split_rows<<<1, 32, 0, s>>>(d_n_, d_nl_, L, per);
+  k_split_rows<<<1, 32, 0, s>>>(io.d_n, io.d_nl, L, per);
   B2E_CUDA(cudaGetLastError());
   // input_up of the four towers, one projection over all rows
   const int P = d_.P, F = d_.F, lp = opt_.lp;
   StepCtx c0;
   c0.s = s;
   c0.rows = rows;
-  c0.n_dev = d_n_;
-  c0.slots = d_slots_;
+  c0.n_dev = io.d_n;
+  c0.slots = io.d_slots;
   c0.lp = lp;
   c0.err = d_err_;
   c0.ln = ln_;
   if (lp != kF32) {
     const int blocks = std::max(1, std::min(ceil_div(long(rows) * fpad_, 256 * 4), 148 * 4));
     if (lp == kBF16)
-      k_feats_lp<kBF16><<<blocks, 256, 0, s>>>(d_feats_, F, d_feats_lp_, fpad_, d_n_);
+      k_feats_lp<kBF16><<<blocks, 256, 0, s>>>(io.d_feats, F, d_feats_lp_, fpad_, io.d_n);
     else
-      k_feats_lp<kF16><<<blocks, 256, 0, s>>>(d_feats_, F, d_feats_lp_, fpad_, d_n_);
+      k_feats_lp<kF16><<<blocks, 256, 0, s>>>(io.d_feats, F, d_feats_lp_, fpad_, io.d_n);
     B2E_CUDA(cudaGetLastError());
     linear(c0, d_feats_lp_, lp, fpad_, upw_, lp, upb_, 4 * P, fpad_, nullptr, 0, kActRelu, nullptr, 0, d_up_, 4 * P);
   } else {
-    linear(c0, d_feats_, kF32, F, upw_, kF32, upb_, 4 * P, F, static_cast<float*>(d_up_), 4 * P, kActRelu);
+    linear(c0, io.d_feats, kF32, F, upw_, kF32, upb_, 4 * P, F, static_cast<float*>(d_up_), 4 * P, kActRelu);
   }
   B2E_CUDA(cudaEventRecord(fork_, s));
   for (int l = 0; l < L; ++l) {
@@ -307,8 +331,8 @@ void Engine::enqueue(int rows, cudaStream_t s) {
       StepCtx c;
       c.s = ch.s;
       c.rows = split ? per : rows;
-      c.n_dev = split ? d_nl_ + l : d_n_;
-      c.slots = d_slots_ + size_t(l) * per;
+      c.n_dev = split ? io.d_nl + l : io.d_n;
+      c.slots = io.d_slots + size_t(l) * per;
       c.lp = opt_.lp;
       c.err = d_err_;
       c.ln = ln_;
@@ -320,7 +344,7 @@ void Engine::enqueue(int rows, cudaStream_t s) {
         c.ln.prio = c.ln_bulk.prio = t <= 1 ? prio_hi_ : prio_lo_;
       }
       const void* up = static_cast<const uint8_t*>(d_up_) + (size_t(l) * per * 4 * P + size_t(t) * P) * dtype_size(lp);
-      tower_forward(towers_[t], ch, t, c, up, 4 * P, d_preds_ + size_t(l) * per * 4);
+      tower_forward(towers_[t], ch, t, c, up, 4 * P, io.d_preds + size_t(l) * per * 4);
       B2E_CUDA(cudaEventRecord(ch.done, ch.s));
     }
   }
@@ -329,19 +353,20 @@ void Engine::enqueue(int rows, cudaStream_t s) {
       if (l == 0 || ((opt_.lane_towers >> t) & 1)) B2E_CUDA(cudaStreamWaitEvent(s, chains_[size_t(l) * 4 + t].done, 0));
 }
 
-void Engine::launch(int n, cudaStream_t s) {
+void Engine::launch(int n, int b, cudaStream_t s) {
   const int rows = bucket(n);
   if (!opt_.graphs) {
-    enqueue(rows, s);
+    enqueue(rows, b, s);
     return;
   }
-  auto it = graphs_.find(rows);
+  const long long key = (long long)rows * kSets + b;
+  auto it = graphs_.find(key);
   if (it == graphs_.end()) {
     // Capture on a private stream so the caller's stream is never in capture mode.
     cudaGraph_t g = nullptr;
     B2E_CUDA(cudaStreamBeginCapture(s0_, cudaStreamCaptureModeThreadLocal));
     try {
-      enqueue(rows, s0_);
+      enqueue(rows, b, s0_);
     } catch (...) {
       cudaStreamEndCapture(s0_, &g);
       if (g) cudaGraphDestroy(g);
@@ -349,20 +374,26 @@ void Engine::launch(int n, cudaStream_t s) {
     }
     B2E_CUDA(cudaStreamEndCapture(s0_, &g));
     cudaGraphExec_t ex = nullptr;
-    // node priorities (the state kernels' low priority) only apply with this flag
+    // node priorities (the chains' launch priorities) only apply with this flag
     B2E_CUDA(cudaGraphInstantiate(&ex, g, cudaGraphInstantiateFlagUseNodePriority));
     B2E_CUDA(cudaGraphDestroy(g));
-    it = graphs_.emplace(rows, ex).first;
+    it = graphs_.emplace(key, ex).first;
   }
   B2E_CUDA(cudaGraphLaunch(it->second, s));
 }
+
+void Engine::order_after_last_step(cudaStream_t s) {
+  if (last_stream_ && last_stream_ != s) B2E_CUDA(cudaStreamWaitEvent(s, last_step_, 0));
+}
+
+void Engine::drain() { B2E_CUDA(cudaDeviceSynchronize()); }
 
 int Engine::launches_per_step(int n) {
   B2E_CUDA(cudaSetDevice(opt_.device));
   cudaGraph_t g = nullptr;
   B2E_CUDA(cudaStreamBeginCapture(s0_, cudaStreamCaptureModeThreadLocal));
   try {
-    enqueue(bucket(n), s0_);
+    enqueue(bucket(n), 0, s0_);
   } catch (...) {
     cudaStreamEndCapture(s0_, &g);
     if (g) cudaGraphDestroy(g);
@@ -402,47 +433,74 @@ void Engine::check_host_slots(const int* slots, int n) {
 }
 
 void Engine::submit(const int* slots, const float* feats, int n) {
-  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a step is already in flight on this engine");
+  B2E_CHECK(int(host_fifo_.size()) < kSets, kErrInvalid,
+            "two host steps are already in flight on this engine: wait() for one first");
   check_host_slots(slots, n);
   B2E_CHECK(feats != nullptr, kErrInvalid, "null feature array");
   B2E_CUDA(cudaSetDevice(opt_.device));
+  const int b = next_set_;
+  next_set_ = (next_set_ + 1) % kSets;
+  IoSet& io = io_[b];
+  if (io.used) B2E_CUDA(cudaEventSynchronize(io.done));  // its pinned buffers are free
   const int F = d_.F;
-  std::memcpy(h_io_, &n, 4);
-  std::memcpy(h_io_ + 16, slots, size_t(n) * 4);
-  std::memcpy(h_io_ + feats_off_, feats, size_t(n) * F * 4);
-  B2E_CUDA(cudaMemcpyAsync(d_io_, h_io_, 16 + size_t(n) * 4, cudaMemcpyHostToDevice, s0_));
-  B2E_CUDA(cudaMemcpyAsync(d_feats_, h_io_ + feats_off_, size_t(n) * F * 4, cudaMemcpyHostToDevice, s0_));
-  launch(n, s0_);
-  B2E_CUDA(cudaMemcpyAsync(h_io_ + preds_off_, d_preds_, size_t(n) * 16, cudaMemcpyDeviceToHost, s0_));
-  pending_n_ = n;
+  std::memcpy(io.h_io, &n, 4);
+  std::memcpy(io.h_io + slots_off_, slots, size_t(n) * 4);
+  std::memcpy(io.h_io + feats_off_, feats, size_t(n) * F * 4);
+  // inputs on their own stream: they land while the step before still runs
+  B2E_CUDA(cudaMemcpyAsync(io.d_io, io.h_io, 4, cudaMemcpyHostToDevice, s_h2d_));
+  B2E_CUDA(cudaMemcpyAsync(io.d_slots, io.h_io + slots_off_, size_t(n) * 4, cudaMemcpyHostToDevice, s_h2d_));
+  B2E_CUDA(cudaMemcpyAsync(io.d_feats, io.h_io + feats_off_, size_t(n) * F * 4, cudaMemcpyHostToDevice, s_h2d_));
+  B2E_CUDA(cudaEventRecord(io.in_ready, s_h2d_));
+  order_after_last_step(s0_);
+  B2E_CUDA(cudaStreamWaitEvent(s0_, io.in_ready, 0));
+  launch(n, b, s0_);
+  B2E_CUDA(cudaEventRecord(io.stepped, s0_));
+  B2E_CUDA(cudaEventRecord(last_step_, s0_));
+  last_stream_ = s0_;
+  // predictions out on their own stream: the next step's graph does not wait for them
+  B2E_CUDA(cudaStreamWaitEvent(s_d2h_, io.stepped, 0));
+  B2E_CUDA(cudaMemcpyAsync(io.h_io + preds_off_, io.d_preds, size_t(n) * 16, cudaMemcpyDeviceToHost, s_d2h_));
+  B2E_CUDA(cudaEventRecord(io.done, s_d2h_));
+  io.used = true;
+  io.host_n = n;
+  host_fifo_.push_back(b);
 }
 
 void Engine::wait(float* preds) {
-  B2E_CHECK(pending_n_ >= 0, kErrInvalid, "no step in flight");
-  const int n = pending_n_;
-  pending_n_ = -1;
+  B2E_CHECK(!host_fifo_.empty(), kErrInvalid, "no step in flight");
+  const int b = host_fifo_.front();
+  host_fifo_.erase(host_fifo_.begin());
+  IoSet& io = io_[b];
+  const int n = io.host_n;
+  io.host_n = -1;
   B2E_CUDA(cudaSetDevice(opt_.device));
-  B2E_CUDA(cudaStreamSynchronize(s0_));
-  if (preds) std::memcpy(preds, h_io_ + preds_off_, size_t(n) * 16);
+  B2E_CUDA(cudaEventSynchronize(io.done));
+  if (preds) std::memcpy(preds, io.h_io + preds_off_, size_t(n) * 16);
 }
 
 void Engine::step_device(const int* d_slots, const float* d_feats, int n, float* d_preds, cudaStream_t s) {
-  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a host step is in flight on this engine");
+  B2E_CHECK(host_fifo_.empty(), kErrInvalid, "a host step is in flight on this engine");
   B2E_CHECK(n >= 1 && n <= opt_.max_batch, kErrCapacity, "batch outside 1..max_batch");
   B2E_CHECK(d_slots && d_feats && d_preds, kErrInvalid, "null device buffer");
   B2E_CUDA(cudaSetDevice(opt_.device));
-  if (d_slots != d_slots_) B2E_CUDA(cudaMemcpyAsync(d_slots_, d_slots, size_t(n) * 4, cudaMemcpyDeviceToDevice, s));
-  if (d_feats != d_feats_)
-    B2E_CUDA(cudaMemcpyAsync(d_feats_, d_feats, size_t(n) * d_.F * 4, cudaMemcpyDeviceToDevice, s));
-  k_validate<<<1, 256, 0, s>>>(d_slots_, n, opt_.capacity, d_n_, d_err_);
+  IoSet& io = io_[0];
+  order_after_last_step(s);
+  if (io.used) B2E_CUDA(cudaStreamWaitEvent(s, io.done, 0));
+  B2E_CUDA(cudaMemcpyAsync(io.d_slots, d_slots, size_t(n) * 4, cudaMemcpyDeviceToDevice, s));
+  B2E_CUDA(cudaMemcpyAsync(io.d_feats, d_feats, size_t(n) * d_.F * 4, cudaMemcpyDeviceToDevice, s));
+  k_validate<<<1, 256, 0, s>>>(io.d_slots, n, opt_.capacity, io.d_n, d_err_);
   B2E_CUDA(cudaGetLastError());
-  launch(n, s);
-  if (d_preds != d_preds_) B2E_CUDA(cudaMemcpyAsync(d_preds, d_preds_, size_t(n) * 16, cudaMemcpyDeviceToDevice, s));
+  launch(n, 0, s);
+  B2E_CUDA(cudaMemcpyAsync(d_preds, io.d_preds, size_t(n) * 16, cudaMemcpyDeviceToDevice, s));
+  B2E_CUDA(cudaEventRecord(io.done, s));
+  B2E_CUDA(cudaEventRecord(last_step_, s));
+  last_stream_ = s;
+  io.used = true;
 }
 
 int Engine::device_error() {
   B2E_CUDA(cudaSetDevice(opt_.device));
-  B2E_CUDA(cudaDeviceSynchronize());
+  drain();
   int e = 0;
   B2E_CUDA(cudaMemcpy(&e, d_err_, 4, cudaMemcpyDeviceToHost));
   B2E_CUDA(cudaMemset(d_err_, 0, 4));
@@ -450,31 +508,31 @@ int Engine::device_error() {
 }
 
 void Engine::reset_slots(const int* slots, int n) {
-  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a step is in flight on this engine");
+  B2E_CHECK(host_fifo_.empty(), kErrInvalid, "a step is in flight on this engine");
   B2E_CUDA(cudaSetDevice(opt_.device));
-  B2E_CUDA(cudaStreamSynchronize(s0_));
+  drain();
   for (int i0 = 0; i0 < n; i0 += opt_.max_batch) {
     const int m = std::min(opt_.max_batch, n - i0);
     for (int i = 0; i < m; ++i)
       B2E_CHECK(slots[i0 + i] >= 0 && slots[i0 + i] < opt_.capacity, kErrCapacity, "slot outside the state table");
-    std::memcpy(h_io_ + 16, slots + i0, size_t(m) * 4);
-    B2E_CUDA(cudaMemcpyAsync(d_slots_, h_io_ + 16, size_t(m) * 4, cudaMemcpyHostToDevice, s0_));
-    arena_.reset_slots(d_slots_, m, s0_);
+    std::memcpy(h_rs_, slots + i0, size_t(m) * 4);
+    B2E_CUDA(cudaMemcpyAsync(d_rs_, h_rs_, size_t(m) * 4, cudaMemcpyHostToDevice, s0_));
+    arena_.reset_slots(d_rs_, m, s0_);
     B2E_CUDA(cudaStreamSynchronize(s0_));
   }
 }
 
 void Engine::read_slot(int slot, void* host) {
-  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a step is in flight on this engine");
+  B2E_CHECK(host_fifo_.empty(), kErrInvalid, "a step is in flight on this engine");
   B2E_CUDA(cudaSetDevice(opt_.device));
-  B2E_CUDA(cudaDeviceSynchronize());
+  drain();
   arena_.read_slot(slot, host);
 }
 
 void Engine::write_slot(int slot, const void* host) {
-  B2E_CHECK(pending_n_ < 0, kErrInvalid, "a step is in flight on this engine");
+  B2E_CHECK(host_fifo_.empty(), kErrInvalid, "a step is in flight on this engine");
   B2E_CUDA(cudaSetDevice(opt_.device));
-  B2E_CUDA(cudaDeviceSynchronize());
+  drain();
   arena_.write_slot(slot, host);
 }
 

@@ -27,7 +27,9 @@ class Engine {
   ~Engine();
 
   // Host-buffer step: validates the slots, stages them and the features through
-  // pinned memory, enqueues the step, and (wait) copies predictions out.
+  // pinned memory, enqueues the step, and (wait) copies predictions out. Up to
+  // kSets steps may be in flight (wait() returns the oldest): a step's copies
+  // run on their own streams, beside the step before it.
   void submit(const int* slots, const float* feats, int n);
   void wait(float* preds);
   void step(const int* slots, const float* feats, int n, float* preds) {
@@ -51,6 +53,7 @@ class Engine {
   int device() const { return opt_.device; }
   int launches_per_step(int n);  // kernels one step of n rows enqueues
   cudaStream_t stream() const { return s0_; }
+  static constexpr int kSets = 2;  // step I/O buffer sets
 
  private:
   struct Block {
@@ -74,9 +77,28 @@ class Engine {
     cudaEvent_t done = nullptr;
   };
 
+  // One step's I/O on the device, [n | lane rows | slots] [feats] [preds], its
+  // pinned mirror, and the events that order the set's reuse.
+  struct IoSet {
+    uint8_t* d_io = nullptr;
+    uint8_t* h_io = nullptr;
+    int* d_n = nullptr;
+    int* d_nl = nullptr;  // live rows per lane
+    int* d_slots = nullptr;
+    float* d_feats = nullptr;
+    float* d_preds = nullptr;
+    cudaEvent_t in_ready = nullptr;  // inputs copied in
+    cudaEvent_t stepped = nullptr;   // the step's graph finished
+    cudaEvent_t done = nullptr;      // predictions copied out: the set is free
+    bool used = false;
+    int host_n = -1;                 // rows of the host step in flight on this set
+  };
+
   int bucket(int n) const;
-  void launch(int n, cudaStream_t s);   // graph replay or eager enqueue
-  void enqueue(int rows, cudaStream_t s);
+  void launch(int n, int b, cudaStream_t s);   // graph replay or eager enqueue, I/O set b
+  void enqueue(int rows, int b, cudaStream_t s);
+  void order_after_last_step(cudaStream_t s);  // `s` waits for the last step, wherever it ran
+  void drain();
   void tower_forward(const Tower& t, Chain& ch, int idx, const StepCtx& c, const void* up, int ld_up, float* preds);
   int lanes_for(int rows) const;
   void check_host_slots(const int* slots, int n);
@@ -87,7 +109,6 @@ class Engine {
   StateArena arena_;
   std::vector<Tower> towers_;
   std::vector<Chain> chains_;  // [lane][tower]
-  int* d_nl_ = nullptr;        // live rows per lane (device)
   // input_up of all four towers as one projection: W [4P][fpad] (features
   // padded with zero columns to a multiple of 8 for the tensor cores), bias
   // [4P], input = the step's features in the CastLinear type [rows][fpad],
@@ -102,20 +123,21 @@ class Engine {
   size_t o_ow_ = 0, o_ob_ = 0;
   const float *ow_ = nullptr, *ob_ = nullptr;
 
-  // step I/O: [n | pad | slots[max_batch]] [feats max_batch*F] [preds max_batch*4]
-  uint8_t* d_io_ = nullptr;
-  uint8_t* h_io_ = nullptr;
-  int* d_n_ = nullptr;
-  int* d_slots_ = nullptr;
-  float* d_feats_ = nullptr;
-  float* d_preds_ = nullptr;
+  IoSet io_[kSets];
+  size_t slots_off_ = 0, feats_off_ = 0, preds_off_ = 0;
+  int next_set_ = 0;
+  std::vector<int> host_fifo_;  // sets of the host steps in flight, oldest first
   int* d_err_ = nullptr;
-  size_t feats_off_ = 0, preds_off_ = 0;
-  int pending_n_ = -1;
+  int* d_rs_ = nullptr;         // slots of reset_slots
+  int* h_rs_ = nullptr;
 
-  cudaStream_t s0_ = nullptr;
+  cudaStream_t s0_ = nullptr;     // host steps
+  cudaStream_t s_h2d_ = nullptr;  // host steps' input copies
+  cudaStream_t s_d2h_ = nullptr;  // host steps' prediction copies
   cudaEvent_t fork_ = nullptr;
-  std::unordered_map<int, cudaGraphExec_t> graphs_;
+  cudaEvent_t last_step_ = nullptr;     // recorded after every step
+  cudaStream_t last_stream_ = nullptr;  // where it was recorded
+  std::unordered_map<long long, cudaGraphExec_t> graphs_;  // (bucket, set)
   std::vector<uint8_t> seen_;  // duplicate-slot check
 };
 

@@ -84,6 +84,7 @@ class EnsembleEngine:
         _lib.check(L.b2e_engine_create(C.byref(cc), C.byref(oo), arr, len(state_dict), C.byref(h)))
         del keep
         self._h = h
+        self._pending: List[int] = []
         nb = C.c_int64()
         _lib.check(L.b2e_engine_slot_bytes(h, C.byref(nb)))
         self.slot_bytes = nb.value
@@ -116,15 +117,17 @@ class EnsembleEngine:
         return out
 
     def submit(self, slots, feats) -> int:
+        """Start a host-buffer step; up to two may be outstanding (wait() returns the oldest)."""
         slots, feats = self._rows(slots, feats, self.cfg.num_features)
         _lib.check(_lib.lib().b2e_engine_submit(self._h, slots.ctypes.data, feats.ctypes.data, len(slots)))
-        self._pending = len(slots)
+        self._pending.append(len(slots))
         return len(slots)
 
     def wait(self) -> np.ndarray:
-        n = self._pending
-        out = np.empty((n, len(TOWER_KINDS)), np.float32)
+        n = self._pending[0] if self._pending else 0  # nothing in flight: the library refuses
+        out = np.empty((max(n, 1), len(TOWER_KINDS)), np.float32)[:n]
         _lib.check(_lib.lib().b2e_engine_wait(self._h, out.ctypes.data))
+        self._pending.pop(0)
         return out
 
     def step_device(self, slots_t, feats_t, preds_t, n: int, stream=None):

@@ -115,7 +115,10 @@ B2E_API void b2e_engine_destroy(b2e_engine* e);
 /* One step over n rows: slots[n] (distinct, < capacity), features[n * num_features]
  * and preds[n * 4] are HOST buffers; columns are xLSTM, Mamba2, RetNet, Hawk. */
 B2E_API int b2e_engine_step(b2e_engine* e, const int32_t* slots, const float* features, int32_t n, float* preds);
-/* The same step split in two, so several devices can run at once. */
+/* The same step split in two, so several devices run at once. Up to two submits
+ * may be outstanding on one engine (wait returns the oldest step's
+ * predictions): the second step's input copies and the first step's prediction
+ * copies run beside the steps themselves. */
 B2E_API int b2e_engine_submit(b2e_engine* e, const int32_t* slots, const float* features, int32_t n);
 B2E_API int b2e_engine_wait(b2e_engine* e, float* preds);
 /* Device-buffer step enqueued on `stream` (a cudaStream_t, NULL = default stream).
