@@ -198,6 +198,85 @@ __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre(const Mamba2PreP p) 
   }
 }
 
+// The same for kM2Rows rows per CTA: every row's conv taps and inputs are
+// loaded before any is updated (one round trip to memory per phase instead of
+// one per channel and row), conv and dt weights are shared by the CTA's rows.
+constexpr int kM2Rows = 4;
+__global__ void __launch_bounds__(kRowThreads) k_mamba2_pre_rows(const Mamba2PreP p) {
+  pdl_wait();
+  pdl_launch();
+  constexpr int RM = kM2Rows;
+  const int r0 = blockIdx.x * RM;
+  const int nr = min(RM, live_rows(p.rc.n_dev, p.rc.rows) - r0);
+  if (nr <= 0) return;
+  __shared__ long long sslot[RM];
+  if (threadIdx.x < nr) sslot[threadIdx.x] = row_slot(p.rc, r0 + threadIdx.x);
+  __syncthreads();
+  const int mi = p.mi, bc = p.bc;
+  // convs + SiLU (mamba2.py:84-89): channel i < mi of x, then bc of b, bc of c
+  for (int i = threadIdx.x; i < mi + 2 * bc; i += blockDim.x) {
+    const bool isx = i < mi, isb = !isx && i < mi + bc;
+    const int c = isx ? i : (isb ? i - mi : i - mi - bc), C = isx ? mi : bc;
+    float* base = isx ? p.xconv : (isb ? p.bconv : p.cconv);
+    const long long cs = isx ? p.xcs : (isb ? p.bcs : p.ccs);
+    const float* w = isx ? p.wx : (isb ? p.wb : p.wc);
+    const float* bias = isx ? p.bx : (isb ? p.bb : p.bcv);
+    float* out = isx ? p.xs : (isb ? p.bs : p.cs);
+    const int pi = isx ? i : mi + i;  // the proj row is [x | z | b | c]: b and c sit after z
+    float s0[RM], s1[RM], s2[RM], xv[RM];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      if (rr < nr) {
+        const float* st = base + sslot[rr] * cs;
+        s0[rr] = st[c];
+        s1[rr] = st[C + c];
+        s2[rr] = st[2 * C + c];
+        xv[rr] = p.proj[size_t(r0 + rr) * p.ldp + pi];
+      }
+    }
+    const float w0 = w[c], w1 = w[C + c], w2 = w[2 * C + c], w3 = w[3 * C + c], b0 = bias[c];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      if (rr < nr) {
+        // CausalConv1d over [state, x] (model/modules.py:37-41)
+        float acc = w0 * s0[rr];
+        acc = fmaf(w1, s1[rr], acc);
+        acc = fmaf(w2, s2[rr], acc);
+        acc = fmaf(w3, xv[rr], acc);
+        float* st = base + sslot[rr] * cs;
+        st[c] = s1[rr];
+        st[C + c] = s2[rr];
+        st[2 * C + c] = xv[rr];
+        out[size_t(r0 + rr) * C + c] = siluf_(acc + b0);
+      }
+    }
+  }
+  // dt = softplus(dt_proj(t)); decay = exp(a * dt) (mamba2.py:81, 92-97): one
+  // warp per head, its weight row read once for the CTA's rows
+  const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int h = threadIdx.x >> 5; h < p.nh; h += nw) {
+    const float* w = p.dtw + size_t(h) * p.H;
+    float acc[RM];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) acc[rr] = 0.f;
+    for (int k = lane; k < p.H; k += 32) {
+      const float wk = w[k];
+#pragma unroll
+      for (int rr = 0; rr < RM; ++rr)
+        if (rr < nr) acc[rr] = fmaf(p.tin[size_t(r0 + rr) * p.H + k], wk, acc[rr]);
+    }
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      const float v = warp_sum(acc[rr]);
+      if (lane == 0 && rr < nr) {
+        const float d = softplusf_(v + p.dtb[h]);
+        p.dt[size_t(r0 + rr) * p.nh + h] = d;
+        p.dc[size_t(r0 + rr) * p.nh + h] = expf(p.a[h] * d);
+      }
+    }
+  }
+}
+
 struct Mamba2PostP {
   RowCtx rc;
   const float* ys; const float* xs; const float* proj; int ldp; int mi, hs;
@@ -223,6 +302,52 @@ __global__ void __launch_bounds__(kRowThreads) k_mamba2_post(const Mamba2PostP p
   ss = block_sum(ss, red);
   const float inv = 1.0f / sqrtf(ss / float(p.mi) + 1e-5f);  // RMSNorm eps 1e-5 (mamba2.py:45)
   for (int c = threadIdx.x; c < p.mi; c += blockDim.x) store_as(p.at, p.A, size_t(r) * p.mi + c, g[c] * inv * p.nw[c]);
+}
+
+// The same, one warp per row with 16-byte vectors (mi a multiple of 128 and
+// hs of 4): RMSNorm's sum closes with shuffles, no shared memory or barrier.
+constexpr int kM2PostRows = 8;
+__global__ void __launch_bounds__(256) k_mamba2_post_w(const Mamba2PostP p) {
+  pdl_wait();
+  pdl_launch();
+  const int r = blockIdx.x * kM2PostRows + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (!row_live(p.rc, r)) return;
+  const int n4 = p.mi >> 2;
+  const float4* y = reinterpret_cast<const float4*>(p.ys + size_t(r) * p.mi);
+  const float4* x = reinterpret_cast<const float4*>(p.xs + size_t(r) * p.mi);
+  const float4* z = reinterpret_cast<const float4*>(p.proj + size_t(r) * p.ldp + p.mi);
+  constexpr int V = 8;  // float4 per lane held in registers (mi <= 1024)
+  float4 g[V];
+  float ss = 0.f;
+#pragma unroll
+  for (int t = 0; t < V; ++t) {
+    const int i = lane + 32 * t;
+    if (i < n4) {
+      const float4 yv = y[i], xv = x[i], zv = z[i];
+      const float dh = p.d[(4 * i) / p.hs];  // the 4 columns share a head (hs % 4 == 0)
+      // y = state_contrib + D*x; y *= silu(z) (mamba2.py:158-163)
+      g[t].x = fmaf(dh, xv.x, yv.x) * siluf_(zv.x);
+      g[t].y = fmaf(dh, xv.y, yv.y) * siluf_(zv.y);
+      g[t].z = fmaf(dh, xv.z, yv.z) * siluf_(zv.z);
+      g[t].w = fmaf(dh, xv.w, yv.w) * siluf_(zv.w);
+      ss = fmaf(g[t].x, g[t].x, fmaf(g[t].y, g[t].y, fmaf(g[t].z, g[t].z, fmaf(g[t].w, g[t].w, ss))));
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / float(p.mi) + 1e-5f);  // RMSNorm eps 1e-5 (mamba2.py:45)
+  const float4* nw4 = reinterpret_cast<const float4*>(p.nw);
+#pragma unroll
+  for (int t = 0; t < V; ++t) {
+    const int i = lane + 32 * t;
+    if (i < n4) {
+      const float4 w = nw4[i];
+      const size_t o = size_t(r) * p.mi + 4 * size_t(i);
+      store_as(p.at, p.A, o, g[t].x * inv * w.x);
+      store_as(p.at, p.A, o + 1, g[t].y * inv * w.y);
+      store_as(p.at, p.A, o + 2, g[t].z * inv * w.z);
+      store_as(p.at, p.A, o + 3, g[t].w * inv * w.w);
+    }
+  }
 }
 
 class Mamba2Layer : public Layer {
@@ -292,7 +417,7 @@ class Mamba2Layer : public Layer {
     linear(c, a1, a1t, H_, w1_, lp_, nullptr, n1_, H_, b.proj, n1_);  // x, z, b, c (mamba2.py:77-80)
     Mamba2PreP pp{rc, b.proj, n1_, mi_, bc_, nh_, in, H_, dtw_, dtb_, xc_, sxc_, bcs_, sbc_, ccs_, scc_,
                   wx_, bx_, wb_, bb_, wc_, bcv_, a_, b.xs, b.bs, b.cs, b.dt, b.dc};
-    launch_k(c.ln, k_mamba2_pre, dim3(c.rows), dim3(kRowThreads), 0, c.s, pp);
+    launch_k(c.ln, k_mamba2_pre_rows, dim3(ceil_div(c.rows, kM2Rows)), dim3(kRowThreads), 0, c.s, pp);
     SsmColsParams sp;
     sp.at = {ssm_, sssm_, c.slots, nullptr, c.rows, c.n_dev};
     sp.nh = nh_; sp.sh = hs_; sp.sc = bc_;
@@ -301,7 +426,10 @@ class Mamba2Layer : public Layer {
     sp.err = c.err;
     ssm_cols(sp, c.rows, c.s, c.ln_bulk);
     Mamba2PostP po{rc, b.ys, b.xs, b.proj, n1_, mi_, hs_, dd_, nw_, b.A, lp_};
-    launch_k(c.ln, k_mamba2_post, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, po);
+    if (mi_ % 128 == 0 && mi_ <= 1024 && hs_ % 4 == 0 && n1_ % 4 == 0)
+      launch_k(c.ln, k_mamba2_post_w, dim3(ceil_div(c.rows, kM2PostRows)), dim3(256), 0, c.s, po);
+    else
+      launch_k(c.ln, k_mamba2_post, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, po);
     linear(c, b.A, lp_, mi_, out_, lp_, nullptr, H_, mi_, out, H_, kActNone, residual, H_, nullptr, 0, post);  // out_proj (mamba2.py:165)
     B2E_CUDA(cudaGetLastError());
   }
@@ -856,43 +984,79 @@ __global__ void __launch_bounds__(kRowThreads, 3) k_mlstm_mid(const MlstmMidP p)
   const int nr = min(p.rows_per_cta, live_rows(p.rc.n_dev, p.rc.rows) - r0);
   if (nr <= 0) return;
   extern __shared__ float smid[];  // [rows][3mi] q | k | v (k unscaled), [rows][mi] conv+SiLU, [rows][2nh] gate pre-activations
+  constexpr int RM = 4, U = 6;     // rows per CTA at most; gate-weight vectors per lane at a time
   const int mi = p.mi, nh = p.nh, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   float* xcs = smid + size_t(p.rows_per_cta) * 3 * mi;
   float* gpre = xcs + size_t(p.rows_per_cta) * mi;
-  // conv1d + SiLU (xlstm.py:206-207), consecutive channels on consecutive lanes
-  for (int it = tid; it < nr * mi; it += blockDim.x) {
-    const int rr = it / mi, c = it - rr * mi, r = r0 + rr;
-    float* st = p.conv + row_slot(p.rc, r) * p.cs;
-    const float v = siluf_(conv_step(p.cw, p.cb, st, mi, c, p.proj[size_t(r) * 2 * mi + c]));
-    xcs[rr * mi + c] = v;
-    p.xca[size_t(r) * mi + c] = v;
+  __shared__ long long sslot[RM];
+  if (tid < nr) sslot[tid] = row_slot(p.rc, r0 + tid);
+  __syncthreads();
+  // conv1d + SiLU (xlstm.py:206-207), consecutive channels on consecutive
+  // lanes; every row's taps and input are loaded before any is updated
+  for (int c = tid; c < mi; c += blockDim.x) {
+    float s0[RM], s1[RM], s2[RM], xv[RM];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      if (rr < nr) {
+        const float* st = p.conv + sslot[rr] * p.cs;
+        s0[rr] = st[c];
+        s1[rr] = st[mi + c];
+        s2[rr] = st[2 * mi + c];
+        xv[rr] = p.proj[size_t(r0 + rr) * 2 * mi + c];
+      }
+    }
+    const float w0 = p.cw[c], w1 = p.cw[mi + c], w2 = p.cw[2 * mi + c], w3 = p.cw[3 * mi + c], cb = p.cb[c];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      if (rr < nr) {
+        // CausalConv1d over [state, x] (model/modules.py:37-41)
+        float acc = w0 * s0[rr];
+        acc = fmaf(w1, s1[rr], acc);
+        acc = fmaf(w2, s2[rr], acc);
+        acc = fmaf(w3, xv[rr], acc);
+        float* st = p.conv + sslot[rr] * p.cs;
+        st[c] = s1[rr];
+        st[mi + c] = s2[rr];
+        st[2 * mi + c] = xv[rr];
+        const float v = siluf_(acc + cb);
+        xcs[rr * mi + c] = v;
+        p.xca[size_t(r0 + rr) * mi + c] = v;
+      }
+    }
   }
   __syncthreads();
   // q/k from the conv branch, v from x_mlstm: BlockLinear with 4x4 blocks,
   // out[4b+kk] = sum_h x[4b+h] * W[b][kk][h] (xlstm.py:209-211); one output per
-  // thread, its weight row W[b][kk][:] one 16-byte load
-  for (int it = tid; it < nr * mi; it += blockDim.x) {
-    const int rr = it / mi, e = it - rr * mi, r = r0 + rr;
-    const float4 xc = reinterpret_cast<const float4*>(xcs + rr * mi)[e >> 2];
-    const float4 x0 = reinterpret_cast<const float4*>(p.proj + size_t(r) * 2 * mi)[e >> 2];
+  // thread, its weight row W[b][kk][:] one 16-byte load shared by the CTA's rows
+  for (int e = tid; e < mi; e += blockDim.x) {
     const float4 wq = __ldg(reinterpret_cast<const float4*>(p.wq) + e);
     const float4 wk = __ldg(reinterpret_cast<const float4*>(p.wk) + e);
     const float4 wv = __ldg(reinterpret_cast<const float4*>(p.wv) + e);
-    const float aq = fmaf(xc.w, wq.w, fmaf(xc.z, wq.z, fmaf(xc.y, wq.y, xc.x * wq.x)));
-    const float ak = fmaf(xc.w, wk.w, fmaf(xc.z, wk.z, fmaf(xc.y, wk.y, xc.x * wk.x)));
-    const float av = fmaf(x0.w, wv.w, fmaf(x0.z, wv.z, fmaf(x0.y, wv.y, x0.x * wv.x)));
-    float* q = smid + size_t(rr) * 3 * mi;
-    q[e] = aq;
-    q[mi + e] = ak;
-    q[2 * mi + e] = av;
-    p.qkv[size_t(r) * 3 * mi + e] = aq;
-    p.qkv[size_t(r) * 3 * mi + 2 * mi + e] = av;
+    float4 x0[RM];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr)
+      if (rr < nr) x0[rr] = reinterpret_cast<const float4*>(p.proj + size_t(r0 + rr) * 2 * mi)[e >> 2];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      if (rr < nr) {
+        const int r = r0 + rr;
+        const float4 xc = reinterpret_cast<const float4*>(xcs + rr * mi)[e >> 2];
+        const float aq = fmaf(xc.w, wq.w, fmaf(xc.z, wq.z, fmaf(xc.y, wq.y, xc.x * wq.x)));
+        const float ak = fmaf(xc.w, wk.w, fmaf(xc.z, wk.z, fmaf(xc.y, wk.y, xc.x * wk.x)));
+        const float av = fmaf(x0[rr].w, wv.w, fmaf(x0[rr].z, wv.z, fmaf(x0[rr].y, wv.y, x0[rr].x * wv.x)));
+        float* q = smid + size_t(rr) * 3 * mi;
+        q[e] = aq;
+        q[mi + e] = ak;
+        q[2 * mi + e] = av;
+        p.qkv[size_t(r) * 3 * mi + e] = aq;
+        p.qkv[size_t(r) * 3 * mi + 2 * mi + e] = av;
+      }
+    }
   }
   __syncthreads();
   // igate / fgate projections of cat(q, k, v) (xlstm.py:119-120): one warp per
   // gate, its weight row in registers (U vectors per lane at a time) against
   // every row of the CTA
-  constexpr int RM = 4, U = 6;
   const int k4n = (3 * mi) >> 2;
   for (int g = warp; g < 2 * nh; g += nw) {
     const float4* w4 = reinterpret_cast<const float4*>(p.gw + size_t(g) * 3 * mi);
@@ -928,7 +1092,7 @@ __global__ void __launch_bounds__(kRowThreads, 3) k_mlstm_mid(const MlstmMidP p)
     float mn[RM], i_g[RM], f_g[RM], qn[RM];
 #pragma unroll
     for (int rr = 0; rr < RM; ++rr) {
-      slot[rr] = rr < nr ? row_slot(p.rc, r0 + rr) : 0;
+      slot[rr] = rr < nr ? sslot[rr] : 0;
       mn[rr] = rr < nr ? p.m[slot[rr] * p.m_s + h] : 0.f;  // old m, replaced below
     }
 #pragma unroll
@@ -1012,6 +1176,50 @@ __global__ void __launch_bounds__(kRowThreads) k_mlstm_post(const MlstmPostP p) 
     const int g = e / hs;
     const float on = (o[e] - gm[g]) * gr[g] * p.gnw[e] + p.gnb[e];
     store_as(p.at, p.A, size_t(r) * p.mi + e, (on + p.skip[e] * xca[e]) * siluf_(xg[e]));  // xlstm.py:215-216
+  }
+}
+
+// The same, one warp per (row, head): the head's hs = 32*T columns sit T to a
+// lane, so GroupNorm's sums close with warp shuffles, with no shared memory,
+// barrier or per-element division of indices. Heads of up to 512 columns.
+constexpr int kPostWarps = 8;  // warps per CTA
+__global__ void __launch_bounds__(256) k_mlstm_post_w(const MlstmPostP p) {
+  pdl_wait();
+  pdl_launch();
+  const int w = blockIdx.x * kPostWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int r = w / p.nh, g = w - r * p.nh;
+  if (!row_live(p.rc, r)) return;
+  const int mi = p.mi, hs = mi / p.nh, T = hs >> 5;
+  const float* num = p.num + size_t(r) * mi;
+  const float* xca = p.xca + size_t(r) * mi;
+  const float* xg = p.proj + size_t(r) * 2 * mi + mi;
+  {
+    const float den = p.den[size_t(r) * p.nh + g];
+    const int e0 = g * hs + lane;
+    float o[16];
+    float s = 0.f;
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (t < T) {
+        o[t] = num[e0 + 32 * t] / den;  // xlstm.py:133
+        s += o[t];
+      }
+    const float mu = warp_sum(s) / float(hs);
+    float q = 0.f;
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (t < T) {
+        const float d = o[t] - mu;
+        q = fmaf(d, d, q);
+      }
+    const float rs = 1.0f / sqrtf(warp_sum(q) / float(hs) + 1e-5f);  // outnorm GroupNorm (xlstm.py:135)
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (t < T) {
+        const int e = e0 + 32 * t;
+        const float on = (o[t] - mu) * rs * p.gnw[e] + p.gnb[e];
+        store_as(p.at, p.A, size_t(r) * mi + e, (on + p.skip[e] * xca[e]) * siluf_(xg[e]));  // xlstm.py:215-216
+      }
   }
 }
 
@@ -1220,7 +1428,10 @@ class XLSTMLayer : public Layer {
     op.err = c.err;
     outer_rows(op, c.rows, c.s, c.ln_bulk);
     MlstmPostP pp{rc, b.num, b.den, b.xca, b.proj, mi_, nh_, ongw_, ongb_, skip_, b.A, lp_};
-    launch_k(c.ln, k_mlstm_post, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, pp);
+    if (hs_ % 32 == 0 && hs_ <= 512)
+      launch_k(c.ln, k_mlstm_post_w, dim3(ceil_div(c.rows * nh_, kPostWarps)), dim3(256), 0, c.s, pp);
+    else
+      launch_k(c.ln, k_mlstm_post, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, pp);
     if (post) {
       // proj_down + skip, final LayerNorm, Block residual and the Block's norm2,
       // all in the GEMM epilogue (xlstm.py:217-219, 365; inference_model.py:65-67)
