@@ -16,7 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libb2e.so"
 B2E_OK = 0
 DTYPES = {"fp32": 0, "bf16": 1, "fp16": 2}
 LAYER_KINDS = {"xlstm": 0, "mamba2": 1, "retnet": 2, "hawk": 3}
-FLAG_PDL = 1            # B2E_FLAG_PDL
+FLAG_NO_PDL = 1         # B2E_FLAG_NO_PDL
 FLAG_NO_PRIORITIES = 2  # B2E_FLAG_NO_PRIORITIES
 
 

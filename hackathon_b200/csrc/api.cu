@@ -79,7 +79,7 @@ EngineOptions to_opts(const b2e_engine_options* o) {
   if (o->lanes > 0) e.lanes = o->lanes;
   if (o->lane_min_rows > 0) e.lane_min_rows = o->lane_min_rows;
   if (o->lane_towers != 0) e.lane_towers = o->lane_towers;
-  e.pdl = (o->flags & B2E_FLAG_PDL) != 0;
+  e.pdl = !(o->flags & B2E_FLAG_NO_PDL);
   e.priorities = !(o->flags & B2E_FLAG_NO_PRIORITIES);
   return e;
 }

@@ -29,7 +29,6 @@ constexpr int U = 4;
 
 __global__ void __launch_bounds__(kThreads) outer_rows_kernel(const __grid_constant__ OuterRowsParams p, int HG) {
   pdl_wait();
-  pdl_launch();
   const int row = blockIdx.z;
   if (row >= live_rows(p.at.n_dev, p.at.n_host)) return;
   const int h0 = blockIdx.y * HG;
@@ -132,7 +131,6 @@ __global__ void __launch_bounds__(kThreads) outer_rows_kernel(const __grid_const
 // inside the CTA. Same two-batch prefetch as outer_rows.
 __global__ void __launch_bounds__(kThreads) ssm_cols_kernel(const __grid_constant__ SsmColsParams p, int PT, int HG) {
   pdl_wait();
-  pdl_launch();
   const int row = blockIdx.z;
   if (row >= live_rows(p.at.n_dev, p.at.n_host)) return;
   const int h0 = blockIdx.y * HG;
@@ -230,7 +228,6 @@ __global__ void __launch_bounds__(kThreads) ssm_cols_kernel(const __grid_constan
 template <int LC>
 __global__ void __launch_bounds__(kThreads, 4) ssm_cols_fast(const __grid_constant__ SsmColsParams p, int PT, int HG) {
   pdl_wait();
-  pdl_launch();
   const int row = blockIdx.z;
   if (row >= live_rows(p.at.n_dev, p.at.n_host)) return;
   constexpr int RP = kThreads / LC;  // state rows in flight per pass
@@ -318,7 +315,6 @@ __global__ void __launch_bounds__(kThreads, 4) ssm_cols_fast(const __grid_consta
 template <int L>
 __global__ void __launch_bounds__(kThreads, 4) outer_rows_fast(const __grid_constant__ OuterRowsParams p, int HG) {
   pdl_wait();
-  pdl_launch();
   const int row = blockIdx.z;
   if (row >= live_rows(p.at.n_dev, p.at.n_host)) return;
   constexpr int RH = kThreads / L, KW = 4 * L;

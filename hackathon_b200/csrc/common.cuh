@@ -139,16 +139,16 @@ inline int ceil_div(long a, long b) { return int((a + b - 1) / b); }
 
 // ------------------------------------------------------------ launches
 // The engine launches the kernels of a tower's chain with programmatic stream
-// serialization (PDL): a kernel may become resident while its predecessor in
-// the stream still runs, set up (barriers, tensor memory), and then waits in
-// pdl_wait() until the predecessor has completed and its writes are visible.
-// Every kernel calls pdl_wait() before its first global read other than weights,
-// and in every thread that reads or writes global memory, so a kernel's
-// completion also implies its predecessors' (the chain stays transitive);
-// pdl_launch() after the wait lets the successor start its own set-up. In a
-// kernel launched without the attribute both are no-ops.
+// serialization (PDL): a kernel's grid is launched as soon as every CTA of its
+// predecessor has exited, without the predecessor's completion and memory
+// flush in between, and then waits in pdl_wait() until those writes are
+// visible. No kernel triggers its successor earlier: successors resident ahead
+// of time would hold SM slots that the other towers' kernels need. Every kernel
+// calls pdl_wait() before its first global read other than weights, and in
+// every thread that reads or writes global memory, so a kernel's completion
+// also implies its predecessors' (the chain stays transitive). In a kernel
+// launched without the attribute it is a no-op.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // How a kernel is launched: plain (the C-ABI operators on a caller's stream), or
 // with PDL and a scheduling priority (the engine's chains: the HBM-streaming

@@ -17,7 +17,7 @@ struct EngineOptions {
   int lanes = 1;          // independent row shares per tower for batches of >= lane_min_rows
   int lane_min_rows = 256;
   int lane_towers = 0xF;  // bit t: tower t takes `lanes` lanes, else one chain over all rows
-  bool pdl = false;        // programmatic dependent launch inside each tower's chain
+  bool pdl = true;         // programmatic dependent launch inside each tower's chain
   bool priorities = true;   // the xLSTM tower's chain at high launch priority, the others low
 };
 

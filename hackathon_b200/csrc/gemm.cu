@@ -76,7 +76,6 @@ __device__ __forceinline__ float epilogue(const GemmParams& p, const GemmGroup& 
 template <int AT, int WT>
 __global__ void __launch_bounds__(TPB) gemm_tiled(const __grid_constant__ GemmParams p, bool vec_a, bool vec_w) {
   pdl_wait();
-  pdl_launch();
   const GemmGroup& g = p.g[blockIdx.z];
   const int M = live_rows(p.M_dev, p.M_max);
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
@@ -156,7 +155,6 @@ __global__ void __launch_bounds__(TPB) gemm_tiled(const __grid_constant__ GemmPa
 template <int AT, int WT, int MM>
 __global__ void __launch_bounds__(256) gemm_skinny(const __grid_constant__ GemmParams p, bool vec) {
   pdl_wait();
-  pdl_launch();
   const GemmGroup& g = p.g[blockIdx.y];
   const int M = min(live_rows(p.M_dev, p.M_max), MM);
   if (M <= 0) return;
@@ -245,7 +243,6 @@ constexpr int kNarrowRows = 2;
 template <int NN>
 __global__ void __launch_bounds__(256) gemm_narrow(const __grid_constant__ GemmParams p) {
   pdl_wait();
-  pdl_launch();
   const GemmGroup& g = p.g[0];
   const int M = live_rows(p.M_dev, p.M_max);
   const int lane = threadIdx.x & 31;
@@ -325,7 +322,6 @@ __global__ void __launch_bounds__(256) gemm_narrow_smem(const __grid_constant__ 
       if (i0 + j * blockDim.x < N * K4) reinterpret_cast<float4*>(ws)[i0 + j * blockDim.x] = t[j];
   }
   pdl_wait();
-  pdl_launch();
   const int M = live_rows(p.M_dev, p.M_max);
   __syncthreads();
   const int lane = threadIdx.x & 31;

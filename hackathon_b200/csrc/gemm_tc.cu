@@ -248,7 +248,6 @@ __global__ void __launch_bounds__(THREADS)
   const uint32_t tmem = *tmem_slot;
   // TMEM is held from here on; the successor may start only after this point.
   pdl_wait();
-  pdl_launch();
   const int M = live_rows(e.M_dev, e.M_max);
   const bool live = m0 < M;  // uniform over the CTA
   const int nkb = (e.K + BK - 1) / BK;

@@ -101,7 +101,6 @@ constexpr int kRowsPerCta = 8;
 
 __global__ void __launch_bounds__(256) k_rmsnorm(const RmsP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (!row_live(p.rc, r)) return;
@@ -135,7 +134,6 @@ struct OutP {
 };
 __global__ void __launch_bounds__(256) k_output_proj(const OutP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (!row_live(p.rc, r)) return;
@@ -166,7 +164,6 @@ struct Mamba2PreP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre(const Mamba2PreP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   const long long slot = row_slot(p.rc, r);
@@ -204,7 +201,6 @@ __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre(const Mamba2PreP p) 
 constexpr int kM2Rows = 4;
 __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre_rows(const Mamba2PreP p) {
   pdl_wait();
-  pdl_launch();
   constexpr int RM = kM2Rows;
   const int r0 = blockIdx.x * RM;
   const int nr = min(RM, live_rows(p.rc.n_dev, p.rc.rows) - r0);
@@ -284,7 +280,6 @@ struct Mamba2PostP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_mamba2_post(const Mamba2PostP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float g[];
@@ -309,7 +304,6 @@ __global__ void __launch_bounds__(kRowThreads) k_mamba2_post(const Mamba2PostP p
 constexpr int kM2PostRows = 8;
 __global__ void __launch_bounds__(256) k_mamba2_post_w(const Mamba2PostP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x * kM2PostRows + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (!row_live(p.rc, r)) return;
   const int n4 = p.mi >> 2;
@@ -458,7 +452,6 @@ struct RetPreP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_retnet_pre(const RetPreP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   const long long slot = row_slot(p.rc, r);
@@ -492,7 +485,6 @@ struct RetPostP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_retnet_post(const RetPostP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float inv[];  // per head
@@ -592,7 +584,6 @@ struct HawkConvP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_hawk_conv(const HawkConvP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   float* st = p.conv + row_slot(p.rc, r) * p.cs;
@@ -608,7 +599,6 @@ struct RglruP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_rglru(const RglruP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   float* h = p.h + row_slot(p.rc, r) * p.hs;
@@ -714,7 +704,6 @@ struct SlstmPreP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_slstm_pre(const SlstmPreP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float xn[];
@@ -749,7 +738,6 @@ struct SlstmPostP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float sm[];
@@ -818,7 +806,6 @@ struct SlstmFusedP {
 template <int RB, int HT>
 __global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
   pdl_wait();
-  pdl_launch();
   const int r0 = blockIdx.x * RB;
   const int nr = min(RB, live_rows(p.rc.n_dev, p.rc.rows) - r0);
   if (nr <= 0) return;
@@ -979,7 +966,6 @@ struct MlstmMidP {
 };
 __global__ void __launch_bounds__(kRowThreads, 3) k_mlstm_mid(const MlstmMidP p) {
   pdl_wait();
-  pdl_launch();
   const int r0 = blockIdx.x * p.rows_per_cta;
   const int nr = min(p.rows_per_cta, live_rows(p.rc.n_dev, p.rc.rows) - r0);
   if (nr <= 0) return;
@@ -1160,7 +1146,6 @@ struct MlstmPostP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_mlstm_post(const MlstmPostP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float o[];
@@ -1185,7 +1170,6 @@ __global__ void __launch_bounds__(kRowThreads) k_mlstm_post(const MlstmPostP p) 
 constexpr int kPostWarps = 8;  // warps per CTA
 __global__ void __launch_bounds__(256) k_mlstm_post_w(const MlstmPostP p) {
   pdl_wait();
-  pdl_launch();
   const int w = blockIdx.x * kPostWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int r = w / p.nh, g = w - r * p.nh;
   if (!row_live(p.rc, r)) return;
@@ -1229,7 +1213,6 @@ struct XFinalP {
 };
 __global__ void __launch_bounds__(kRowThreads) k_xlstm_final(const XFinalP p) {
   pdl_wait();
-  pdl_launch();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
   extern __shared__ float x[];

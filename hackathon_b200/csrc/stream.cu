@@ -169,7 +169,6 @@ template <int LC>
 __global__ void __launch_bounds__(kBulkThreads, 1) ssm_bulk_kernel(const __grid_constant__ SsmColsParams p) {
   const Ring r = ring_setup();
   pdl_wait();
-  pdl_launch();
   const int items = live_rows(p.at.n_dev, p.at.n_host) * p.nh;
   const int my = items_of_cta(items);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -288,7 +287,6 @@ template <int L>
 __global__ void __launch_bounds__(kBulkThreads, 1) outer_bulk_kernel(const __grid_constant__ OuterRowsParams p, int hg) {
   const Ring r = ring_setup();
   pdl_wait();
-  pdl_launch();
   const int groups = p.nh / hg;
   const int items = live_rows(p.at.n_dev, p.at.n_host) * groups;
   const int my = items_of_cta(items);

@@ -58,7 +58,7 @@ extern "C" {
 /* Storage type of the nn.Linear weights: LINEAR_DTYPE of example_model.py:151-157.
  * The four fp32-kept linears (example_model.py:106), BlockLinear, convs and norms
  * stay float32 in every mode. */
-#define B2E_FLAG_PDL 1           /* launch chain kernels with programmatic dependent launch */
+#define B2E_FLAG_NO_PDL 1        /* launch chain kernels without programmatic dependent launch */
 #define B2E_FLAG_NO_PRIORITIES 2 /* launch every chain at the same priority (default: the xLSTM tower's, the longest, first) */
 
 #define B2E_DTYPE_F32 0
@@ -91,7 +91,7 @@ typedef struct b2e_engine_options {
   int32_t use_graphs;   /* 1: replay each step from a CUDA graph per batch bucket */
   int32_t lanes;        /* independent row shares per tower for large batches; 0 = default (1) */
   int32_t lane_min_rows;/* batches from this many rows use `lanes`; 0 = default (256) */
-  int32_t flags;        /* 0 = defaults; B2E_FLAG_PDL turns PDL on, B2E_FLAG_NO_PRIORITIES turns priorities off */
+  int32_t flags;        /* 0 = defaults; B2E_FLAG_NO_PDL turns PDL off, B2E_FLAG_NO_PRIORITIES priorities */
   int32_t lane_towers;  /* bit t set: tower t (0 xLSTM, 1 Mamba2, 2 RetNet, 3 Hawk) splits into `lanes`; 0 = every tower */
 } b2e_engine_options;
 
