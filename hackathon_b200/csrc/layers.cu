@@ -162,42 +162,10 @@ struct Mamba2PreP {
   const float *wx, *bx, *wb, *bb, *wc, *bcv, *a;
   float *xs, *bs, *cs, *dt, *dc;
 };
-__global__ void __launch_bounds__(kRowThreads) k_mamba2_pre(const Mamba2PreP p) {
-  pdl_wait();
-  const int r = blockIdx.x;
-  if (!row_live(p.rc, r)) return;
-  const long long slot = row_slot(p.rc, r);
-  const float* pr = p.proj + size_t(r) * p.ldp;
-  float* sx = p.xconv + slot * p.xcs;
-  float* sb = p.bconv + slot * p.bcs;
-  float* sc = p.cconv + slot * p.ccs;
-  // convs + SiLU (mamba2.py:84-89)
-  for (int c = threadIdx.x; c < p.mi; c += blockDim.x)
-    p.xs[size_t(r) * p.mi + c] = siluf_(conv_step(p.wx, p.bx, sx, p.mi, c, pr[c]));
-  for (int c = threadIdx.x; c < p.bc; c += blockDim.x) {
-    p.bs[size_t(r) * p.bc + c] = siluf_(conv_step(p.wb, p.bb, sb, p.bc, c, pr[2 * p.mi + c]));
-    p.cs[size_t(r) * p.bc + c] = siluf_(conv_step(p.wc, p.bcv, sc, p.bc, c, pr[2 * p.mi + p.bc + c]));
-  }
-  // dt = softplus(dt_proj(t)); decay = exp(a * dt) (mamba2.py:81, 92-97): one
-  // warp per head, a dot product of length H over the row's input
-  const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const float* tr = p.tin + size_t(r) * p.H;
-  for (int h = threadIdx.x >> 5; h < p.nh; h += nw) {
-    const float* w = p.dtw + size_t(h) * p.H;
-    float acc = 0.f;
-    for (int k = lane; k < p.H; k += 32) acc = fmaf(tr[k], w[k], acc);
-    acc = warp_sum(acc);
-    if (lane == 0) {
-      const float d = softplusf_(acc + p.dtb[h]);
-      p.dt[size_t(r) * p.nh + h] = d;
-      p.dc[size_t(r) * p.nh + h] = expf(p.a[h] * d);
-    }
-  }
-}
-
-// The same for kM2Rows rows per CTA: every row's conv taps and inputs are
-// loaded before any is updated (one round trip to memory per phase instead of
-// one per channel and row), conv and dt weights are shared by the CTA's rows.
+// Mamba2 between in_proj and the state step, kM2Rows rows per CTA: the three
+// convs + SiLU and dt_proj with softplus and the decay. Every row's conv taps
+// and inputs are loaded before any is updated (one round trip to memory per
+// phase), conv and dt weights are shared by the CTA's rows.
 constexpr int kM2Rows = 4;
 __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre_rows(const Mamba2PreP p) {
   pdl_wait();
