@@ -178,29 +178,41 @@ class B200InferenceClient(_Base):
 
     def _run_round(self, locs: List[tuple], feats: np.ndarray) -> np.ndarray:
         """Step one round's rows (distinct symbols) on their engines; preds in row order."""
-        preds = np.empty((len(locs), self.num_outputs), np.float32)
-        by_engine: Dict[int, List[int]] = {}
-        for i, (e, _) in enumerate(locs):
-            by_engine.setdefault(e, []).append(i)
-        pending = []
-        for e, rows in by_engine.items():
-            rows_a = np.asarray(rows, np.int64)
-            for c0 in range(0, len(rows_a), self.max_batch):
-                chunk = rows_a[c0:c0 + self.max_batch]
-                slots = np.asarray([locs[i][1] for i in chunk], np.int32)
-                pending.append((e, chunk, slots))
-        # submit one chunk per engine at a time so devices overlap
-        while pending:
-            wave, rest, busy = [], [], set()
-            for item in pending:
-                (rest if item[0] in busy else wave).append(item)
-                busy.add(item[0])
-            for e, chunk, slots in wave:
-                self.engines[e].submit(slots, feats[chunk])
-            for e, chunk, _ in wave:
-                preds[chunk] = self.engines[e].wait()
-            pending = rest
-        return preds
+        return self._run_rounds([(locs, feats)])[0]
+
+    def _run_rounds(self, rounds: List[tuple]) -> List[np.ndarray]:
+        """Step rounds of (locs, feats) in order; preds per round in row order.
+        Each engine's steps are its chunks of each round, in round order, with
+        up to two in flight (b2e_engine_submit / b2e_engine_wait): a symbol's
+        next round runs after its previous one on the GPU (same engine, same
+        order), and the devices run side by side."""
+        out = [np.empty((len(locs), self.num_outputs), np.float32) for locs, _ in rounds]
+        queue: Dict[int, List[tuple]] = {}
+        for k, (locs, feats) in enumerate(rounds):
+            by_engine: Dict[int, List[int]] = {}
+            for i, (e, _) in enumerate(locs):
+                by_engine.setdefault(e, []).append(i)
+            for e, rows in by_engine.items():
+                rows_a = np.asarray(rows, np.int64)
+                for c0 in range(0, len(rows_a), self.max_batch):
+                    chunk = rows_a[c0:c0 + self.max_batch]
+                    slots = np.asarray([locs[i][1] for i in chunk], np.int32)
+                    queue.setdefault(e, []).append((k, chunk, slots, feats[chunk]))
+        depth = 2
+        inflight: Dict[int, List[tuple]] = {e: [] for e in queue}
+        pos = {e: 0 for e in queue}
+        while any(pos[e] < len(queue[e]) or inflight[e] for e in queue):
+            for e in queue:  # top every engine up, then drain the oldest of each
+                while pos[e] < len(queue[e]) and len(inflight[e]) < depth:
+                    k, chunk, slots, f = queue[e][pos[e]]
+                    self.engines[e].submit(slots, f)
+                    inflight[e].append((k, chunk))
+                    pos[e] += 1
+            for e in queue:
+                if inflight[e]:
+                    k, chunk = inflight[e].pop(0)
+                    out[k][chunk] = self.engines[e].wait()
+        return out
 
     def process_batch(self, requests_by_symbol: Dict[str, List["PendingRequest"]]) -> "InferenceResponse":
         """Answer every pending request, batching horizontally across symbols
@@ -219,6 +231,7 @@ class B200InferenceClient(_Base):
                 continue
             symbol_items.append((loc, reqs))
         if symbol_items:
+            rounds, reqs_of = [], []
             for k in range(max(len(reqs) for _, reqs in symbol_items)):
                 locs, feats, batch_requests = [], [], []
                 for loc, reqs in symbol_items:
@@ -227,7 +240,9 @@ class B200InferenceClient(_Base):
                         feats.append(reqs[k].features)
                         batch_requests.append(reqs[k])
                 rows = np.asarray(feats, dtype=np.float32).reshape(len(locs), self.num_features)
-                preds = self._run_round(locs, rows)
+                rounds.append((locs, rows))
+                reqs_of.append(batch_requests)
+            for batch_requests, preds in zip(reqs_of, self._run_rounds(rounds)):
                 for req, p in zip(batch_requests, preds):
                     all_unique_ids.append(req.unique_id)
                     all_predictions.append(p.astype(float).tolist())

@@ -249,15 +249,16 @@ class IngestClient(B200InferenceClient):
             uids_out.append(rows.unique_ids[idx])
             preds_out.append(np.zeros((len(idx), self.num_outputs), np.float32))
         start = 0
+        rounds = []
         for cnt in rows.round_rows.tolist():
             sel = np.arange(start, start + cnt)
             start += cnt
             sel = sel[live[sel]]
             if len(sel) == 0:
                 continue
-            locs = [loc_of[s] for s in rows.symbols[sel].tolist()]
-            preds_out.append(self._run_round(locs, rows.features[sel]))
+            rounds.append(([loc_of[s] for s in rows.symbols[sel].tolist()], rows.features[sel]))
             uids_out.append(rows.unique_ids[sel])
+        preds_out += self._run_rounds(rounds)
         return encode_response(np.concatenate(uids_out), np.concatenate(preds_out), self.clock())
 
     # ---- socket driving (client.py:125-200); the reference's connect() and

@@ -13,23 +13,26 @@ from tests.golden import streams
 
 
 class OracleEngine:
-    """Engine-shaped wrapper of the CPU oracle (test double)."""
+    """Engine-shaped wrapper of the CPU oracle (test double): steps run in
+    submit order, up to two in flight, wait() returns the oldest."""
 
     def __init__(self, cfg, sd, capacity):
         self.orc = O.Oracle(cfg, sd)
         self.state = O.init_state(cfg, capacity)
         self.calls = []
+        self._pending = []
 
     def submit(self, slots, feats):
+        assert len(self._pending) < 2, "more than two steps in flight"
         slots = list(np.asarray(slots).reshape(-1))
         assert len(set(slots)) == len(slots), "a symbol appears twice in one round"
         self.calls.append(slots)
         p, new = self.orc.step(np.asarray(feats, np.float32), O.gather_rows(self.state, slots))
         O.scatter_rows(self.state, slots, new)
-        self._p = p
+        self._pending.append(p)
 
     def wait(self):
-        return self._p
+        return self._pending.pop(0)
 
     def close(self):
         pass
