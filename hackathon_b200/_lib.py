@@ -87,6 +87,7 @@ _SIGS = {
     "b2e_layer_write_slot": (C.c_int, [_P, _I32, _P, _I64]),
     "b2e_ingest_create": (C.c_int, [_I32, _I32, C.POINTER(_P)]),
     "b2e_ingest_destroy": (None, [_P]),
+    "b2e_ingest_set_threads": (C.c_int, [_P, _I32]),
     "b2e_ingest_feed": (C.c_int, [_P, _P, _I64, _PI32, _PI32]),
     "b2e_ingest_next_other": (C.c_int, [_P, _P, _I64, _PI64]),
     "b2e_ingest_push": (C.c_int, [_P, _I64, _P, _I64, _P, _PI32]),

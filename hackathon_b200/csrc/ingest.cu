@@ -11,13 +11,18 @@
 // JSON, unusual field types) is handed back whole to the caller, whose decoder
 // is the reference's own, so no line is ever read differently from it.
 #include <algorithm>
+#include <atomic>
 #include <charconv>
+#include <condition_variable>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <deque>
 #include <functional>
+#include <memory>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -537,6 +542,65 @@ void py_float(std::string* out, double x) {
   }
 }
 
+// A fixed set of worker threads that run job(i) for i in [0, n) together with
+// the calling thread; run() returns when every job is done.
+class Pool {
+ public:
+  explicit Pool(int threads) {
+    for (int t = 0; t < threads; ++t) th_.emplace_back([this] { loop(); });
+  }
+  ~Pool() {
+    {
+      std::lock_guard<std::mutex> lk(m_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : th_) t.join();
+  }
+  int threads() const { return int(th_.size()) + 1; }
+  void run(int n, const std::function<void(int)>& job) {
+    {
+      std::lock_guard<std::mutex> lk(m_);
+      job_ = &job;
+      n_ = n;
+      next_.store(0);
+      pending_ = int(th_.size());
+      ++gen_;
+    }
+    cv_.notify_all();
+    work();
+    std::unique_lock<std::mutex> lk(m_);
+    done_.wait(lk, [&] { return pending_ == 0; });
+    job_ = nullptr;
+  }
+
+ private:
+  void work() {
+    for (int i; (i = next_.fetch_add(1)) < n_;) (*job_)(i);
+  }
+  void loop() {
+    uint64_t seen = 0;
+    for (;;) {
+      std::unique_lock<std::mutex> lk(m_);
+      cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+      if (stop_) return;
+      seen = gen_;
+      lk.unlock();
+      work();
+      lk.lock();
+      if (--pending_ == 0) done_.notify_all();
+    }
+  }
+  std::vector<std::thread> th_;
+  std::mutex m_;
+  std::condition_variable cv_, done_;
+  const std::function<void(int)>* job_ = nullptr;
+  int n_ = 0, pending_ = 0;
+  std::atomic<int> next_{0};
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
+
 }  // namespace
 
 struct b2e_ingest {
@@ -557,6 +621,15 @@ struct b2e_ingest {
   int64_t queued = 0;
   Request req;
   std::string mtype;
+  // lines parsed side by side, then queued in order
+  std::unique_ptr<Pool> pool;
+  struct Parsed {
+    Request req;
+    std::string mtype;
+    bool ok = false;
+  };
+  std::vector<Parsed> parsed;
+  std::vector<std::pair<size_t, size_t>> spans;  // (offset in buf, length) of complete lines
 
   int32_t id_of(const std::string& s) {
     auto it = ids.find(s);
@@ -579,17 +652,18 @@ struct b2e_ingest {
     ++queued;
     return true;
   }
-  // One complete line (no newline): queue its requests (true) or keep it whole.
-  bool line(const char* s, size_t n, int32_t* n_req, int32_t* n_other) {
+  // One complete line (no newline), parsed (`ok`: a request line in `q`):
+  // queue its requests (true) or keep it whole.
+  bool line(const char* s, size_t n, bool ok, const Request& q, int32_t* n_req, int32_t* n_other) {
     if (n == 0) return true;  // SocketReader skips empty lines
-    if (!parse_request(s, n, F, &req, &mtype)) {
+    if (!ok) {
       others.emplace_back(s, n);
       ++*n_other;
       return false;
     }
-    const size_t m = std::min({req.uids.size(), req.symbols.size(), req.rows});
+    const size_t m = std::min({q.uids.size(), q.symbols.size(), q.rows});
     for (size_t i = 0; i < m; ++i)
-      if (push(id_of(req.symbols[i]), req.uids[i], req.feats.data() + i * size_t(F))) ++*n_req;
+      if (push(id_of(q.symbols[i]), q.uids[i], q.feats.data() + i * size_t(F))) ++*n_req;
     return true;
   }
 };
@@ -623,11 +697,23 @@ int b2e_ingest_create(int32_t num_features, int32_t max_queue, b2e_ingest** out)
     auto* g = new b2e_ingest;
     g->F = num_features;
     g->max_queue = max_queue;
+    const unsigned hw = std::thread::hardware_concurrency();
+    const int threads = int(std::min(8u, hw > 0 ? hw : 1u));
+    if (threads > 1) g->pool = std::make_unique<Pool>(threads - 1);
     *out = g;
   });
 }
 
 void b2e_ingest_destroy(b2e_ingest* g) { delete g; }
+
+int b2e_ingest_set_threads(b2e_ingest* g, int32_t threads) {
+  return abi_call([&] {
+    b2e_ingest& s = G(g);
+    B2E_CHECK(threads >= 1 && threads <= 256, kErrInvalid, "threads must be in 1..256");
+    s.pool.reset();
+    if (threads > 1) s.pool = std::make_unique<Pool>(threads - 1);
+  });
+}
 
 int b2e_ingest_feed(b2e_ingest* g, const char* data, int64_t len, int32_t* n_requests, int32_t* n_other) {
   return abi_call([&] {
@@ -635,12 +721,40 @@ int b2e_ingest_feed(b2e_ingest* g, const char* data, int64_t len, int32_t* n_req
     B2E_CHECK(len >= 0 && (len == 0 || data != nullptr), kErrInvalid, "bad byte range");
     if (len > 0) s.buf.append(data, size_t(len));
     int32_t nr = 0, no = 0;
-    while (s.off < s.buf.size()) {
-      const char* p = s.buf.data() + s.off;
-      const char* nl = static_cast<const char*>(std::memchr(p, '\n', s.buf.size() - s.off));
+    // the complete lines from `off`
+    s.spans.clear();
+    size_t bytes = 0;
+    for (size_t o = s.off; o < s.buf.size();) {
+      const char* p = s.buf.data() + o;
+      const char* nl = static_cast<const char*>(std::memchr(p, '\n', s.buf.size() - o));
       if (!nl) break;
-      s.off += size_t(nl - p) + 1;
-      if (!s.line(p, size_t(nl - p), &nr, &no)) break;  // the caller reads this line first
+      s.spans.emplace_back(o, size_t(nl - p));
+      bytes += size_t(nl - p);
+      o += size_t(nl - p) + 1;
+    }
+    const int nl = int(s.spans.size());
+    if (s.pool && nl > 1 && bytes >= (size_t(64) << 10)) {
+      // parse side by side; the queue order below is the line order
+      if (s.parsed.size() < size_t(nl)) s.parsed.resize(size_t(nl));
+      const std::function<void(int)> job = [&](int i) {
+        b2e_ingest::Parsed& q = s.parsed[size_t(i)];
+        q.ok = s.spans[size_t(i)].second > 0 &&
+               parse_request(s.buf.data() + s.spans[size_t(i)].first, s.spans[size_t(i)].second, s.F, &q.req, &q.mtype);
+      };
+      s.pool->run(nl, job);
+      for (int i = 0; i < nl; ++i) {
+        const auto sp = s.spans[size_t(i)];
+        s.off = sp.first + sp.second + 1;
+        if (!s.line(s.buf.data() + sp.first, sp.second, s.parsed[size_t(i)].ok, s.parsed[size_t(i)].req, &nr, &no))
+          break;  // the caller reads this line first; the lines after it are parsed again next time
+      }
+    } else {
+      for (int i = 0; i < nl; ++i) {
+        const auto sp = s.spans[size_t(i)];
+        s.off = sp.first + sp.second + 1;
+        const bool ok = sp.second > 0 && parse_request(s.buf.data() + sp.first, sp.second, s.F, &s.req, &s.mtype);
+        if (!s.line(s.buf.data() + sp.first, sp.second, ok, s.req, &nr, &no)) break;
+      }
     }
     if (s.off == s.buf.size() || s.off > (size_t(1) << 20)) {
       s.buf.erase(0, s.off);

@@ -49,13 +49,15 @@ class IngestRows(NamedTuple):
 class RequestIngest:
     """Native queues of pending requests; see the module docstring."""
 
-    def __init__(self, num_features: int, max_queue_size: int = 100):
+    def __init__(self, num_features: int, max_queue_size: int = 100, threads: Optional[int] = None):
         self.num_features = int(num_features)
         self._L = _lib.lib()
         h = C.c_void_p()
         _lib.check(self._L.b2e_ingest_create(self.num_features, int(max_queue_size), C.byref(h)))
         self._h = h
         self._names: List[str] = []
+        if threads is not None:
+            _lib.check(self._L.b2e_ingest_set_threads(self._h, int(threads)))
 
     def close(self) -> None:
         if getattr(self, "_h", None):

@@ -222,6 +222,9 @@ B2E_API int b2e_layer_write_slot(b2e_layer* l, int32_t slot, const void* host, i
 typedef struct b2e_ingest b2e_ingest;
 B2E_API int b2e_ingest_create(int32_t num_features, int32_t max_queue, b2e_ingest** out);
 B2E_API void b2e_ingest_destroy(b2e_ingest* g);
+/* Threads that parse the lines of one feed side by side (default: up to 8, the
+ * host's hardware threads); requests are still queued in line order. */
+B2E_API int b2e_ingest_set_threads(b2e_ingest* g, int32_t threads);
 B2E_API int b2e_ingest_feed(b2e_ingest* g, const char* data, int64_t len, int32_t* n_requests, int32_t* n_other);
 /* The oldest kept line (without its newline); *len = -1 when there is none, or
  * the line's length when cap is too small (nothing is consumed then). */

@@ -263,3 +263,32 @@ def test_feed_rejects_bad_arguments():
     with pytest.raises(_lib.B2EError):
         RequestIngest(0)
     assert struct.calcsize("q") == 8
+
+
+def test_parallel_parsing_queues_exactly_what_one_thread_does():
+    rng = np.random.default_rng(3)
+    lines = []
+    for m in range(300):
+        n = int(rng.integers(1, 40))
+        syms = [f"S{int(x)}" for x in rng.integers(0, 50, n)]
+        f = rng.standard_normal((n, F)).astype(np.float32).astype(float).tolist()
+        lines.append(_request(list(range(m * 100, m * 100 + n)), syms, f))
+        if m % 37 == 5:
+            lines.append(b'{"timestamp": 1, "message_type": "heartbeat"}\n')
+    blob = b"".join(lines)
+    assert len(blob) > 256 << 10
+    out = []
+    for threads in (1, 8):
+        ing = RequestIngest(F, max_queue_size=0, threads=threads)
+        others = []
+        ing.feed(blob)
+        while (ln := ing.next_other()) is not None:
+            others.append(ln)
+            ing.feed(b"")
+        r = ing.take()
+        out.append((others, r.symbols.tolist(), r.unique_ids.tolist(), r.features.copy(), r.round_rows.tolist(),
+                    [ing.symbol_name(i) for i in range(int(r.symbols.max()) + 1)]))
+    a, b = out
+    assert a[0] == b[0] and len(a[0]) == sum(1 for m in range(300) if m % 37 == 5)
+    assert a[1] == b[1] and a[2] == b[2] and a[4] == b[4] and a[5] == b[5]
+    assert _same_f32(a[3], b[3])
