@@ -756,6 +756,20 @@ __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) 
 // row of the CTA; the weights are packed k-major ([2bs][4][H]) so a warp's 32
 // units read 128 contiguous bytes per gate and k, shared by the CTA's rows.
 constexpr int kSlRows = 16;
+// SLSTMCell.forward for one unit of one row (xlstm.py:247-262): gates i, f, z, o
+// in, (c, n, m) updated in place, h out. Out of line, so that the rows of a
+// k_slstm_fused CTA share one copy of the transcendental code.
+__device__ __noinline__ float slstm_cell(float i, float f, float z, float o, float& c, float& n, float& m) {
+  const float lfm = m + logsigmoidf_(f);
+  const float mn = fmaxf(i, lfm);
+  const float og = sigmoidf_(o);
+  const float ig = expf(i - mn);
+  const float fg = expf(lfm - mn);
+  c = fg * c + ig * tanhf(z);
+  n = fg * n + ig;
+  m = mn;
+  return og * c / (n + 1e-6f);
+}
 constexpr int kSlMaxGroups = 16;  // sLSTM heads (GroupNorm groups) per row
 constexpr size_t kSlSmemMax = 96 * 1024;
 struct SlstmFusedP {
@@ -875,16 +889,8 @@ __global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
 #pragma unroll
       for (int q = 0; q < RC; ++q) {
         const int r = rc + q;
-        // SLSTMCell.forward (xlstm.py:247-262)
-        const float i = acc[0][r] + bi, f = acc[1][r] + bf, z = acc[2][r] + bz, o = acc[3][r] + bo;
-        const float lfm = mo[q] + logsigmoidf_(f);
-        const float mn = fmaxf(i, lfm);
-        const float og = sigmoidf_(o);
-        const float ig = expf(i - mn);
-        const float fg = expf(lfm - mn);
-        const float cn = fg * co[q] + ig * tanhf(z);
-        const float nv = fg * no[q] + ig;
-        const float yv = og * cn / (nv + 1e-6f);
+        float cn = co[q], nv = no[q], mn = mo[q];
+        const float yv = slstm_cell(acc[0][r] + bi, acc[1][r] + bf, acc[2][r] + bz, acc[3][r] + bo, cn, nv, mn);
         xc[r * H + u] = yv;
         if (r < nr) {
           p.cs_[slot[r] * p.c_s + u] = cn;
