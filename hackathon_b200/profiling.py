@@ -2,6 +2,8 @@
 
     python -m hackathon_b200.profiling cell --kind mamba2 --rows 4096 --heads 8 --sh 64 --sk 128
         run one state-step kernel `--reps` times on a dense state (for ncu -k)
+    python -m hackathon_b200.profiling layer --kind xlstm --rows 4096 --reps 4
+        one layer at the bench's dims `--reps` steps (its kernels, for ncu -k)
     python -m hackathon_b200.profiling launches <launch list csv>
         per-kernel launches, total time and share of an ncu launch list
     python -m hackathon_b200.profiling metrics <raw csv from ncu -i ... --page raw --csv>
@@ -92,6 +94,31 @@ def cell(kind: str, rows: int, heads: int, sh: int, sk: int, reps: int) -> None:
     print(f"{kind} rows={rows} heads={heads} sh={sh} sk={sk}: {reps} launches, state {state.numel() * 4 / 1e9:.2f} GB")
 
 
+def layer(kind: str, rows: int, reps: int, dtype: str) -> None:
+    """One layer (xlstm / mamba2 / retnet / hawk) at the bench's dims (D2), `reps`
+    steps over `rows` rows with random slots: its kernels at their bench shapes,
+    with only that layer's state on the device."""
+    import numpy as np
+    import torch
+
+    from . import config as C
+    from . import weights as W
+    from .engine import LayerEngine
+
+    cfg = C.D2
+    dev = torch.device("cuda", 0)
+    eng = LayerEngine(kind, cfg, W.generate(W.layer_specs(kind, "", cfg), seed=0), linear_dtype=dtype,
+                      capacity=rows, max_batch=rows)
+    slots = torch.from_numpy(np.random.default_rng(0).permutation(rows).astype(np.int32)).to(dev)
+    x = torch.randn(rows, cfg.hidden_size, device=dev)
+    y = torch.empty_like(x)
+    for _ in range(reps):
+        eng.step_device(slots, x, y)
+    torch.cuda.synchronize()
+    print(f"{kind} layer at D2, rows={rows}: {reps} steps, state {eng.slot_bytes * rows / 1e9:.2f} GB")
+    eng.close()
+
+
 def linear(m: int, k: int, n: int, reps: int, dtype: str) -> None:
     import torch
 
@@ -127,6 +154,11 @@ def main(argv=None):
     li.add_argument("--n", type=int, default=256)
     li.add_argument("--reps", type=int, default=4)
     li.add_argument("--dtype", default="bf16")
+    la = sub.add_parser("layer")
+    la.add_argument("--kind", required=True)
+    la.add_argument("--rows", type=int, default=4096)
+    la.add_argument("--reps", type=int, default=4)
+    la.add_argument("--dtype", default="bf16")
     sub.add_parser("launches").add_argument("csv")
     sub.add_parser("metrics").add_argument("csv")
     a = ap.parse_args(argv)
@@ -134,6 +166,8 @@ def main(argv=None):
         cell(a.kind, a.rows, a.heads, a.sh, a.sk, a.reps)
     elif a.cmd == "linear":
         linear(a.m, a.k, a.n, a.reps, a.dtype)
+    elif a.cmd == "layer":
+        layer(a.kind, a.rows, a.reps, a.dtype)
     elif a.cmd == "launches":
         launches(a.csv)
     else:
