@@ -383,7 +383,9 @@ void Engine::launch(int n, int b, cudaStream_t s) {
 }
 
 void Engine::order_after_last_step(cudaStream_t s) {
-  if (last_stream_ && last_stream_ != s) B2E_CUDA(cudaStreamWaitEvent(s, last_step_, 0));
+  // always, even on the stream it was recorded on: a stream handle may have been
+  // destroyed and handed out again since
+  if (last_stream_) B2E_CUDA(cudaStreamWaitEvent(s, last_step_, 0));
 }
 
 void Engine::drain() { B2E_CUDA(cudaDeviceSynchronize()); }

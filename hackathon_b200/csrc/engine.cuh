@@ -136,7 +136,7 @@ class Engine {
   cudaStream_t s_d2h_ = nullptr;  // host steps' prediction copies
   cudaEvent_t fork_ = nullptr;
   cudaEvent_t last_step_ = nullptr;     // recorded after every step
-  cudaStream_t last_stream_ = nullptr;  // where it was recorded
+  cudaStream_t last_stream_ = nullptr;  // where it was recorded (null: no step yet)
   std::unordered_map<long long, cudaGraphExec_t> graphs_;  // (bucket, set)
   std::vector<uint8_t> seen_;  // duplicate-slot check
 };
