@@ -82,10 +82,13 @@ __device__ void produce(const Ring& r, int my, int* err, Issue&& issue) {
 // Consumers (kCT threads): wait for item k, `compute(k, stage)` in shared
 // memory (false: nothing to write back),
 // then one thread writes the stage back with `store(k, stage)` (a bulk store)
-// and releases the previous item's stage once its store has read it. Every
-// consumer thread takes the same path through the named barriers.
-template <class Compute, class Store>
-__device__ void consume(const Ring& r, int my, int* err, int ctid, Compute&& compute, Store&& store) {
+// and releases the previous item's stage once its store has read it, and every
+// consumer runs `after(k, stage, wrote)`: work that needs the whole CTA's
+// compute of item k (it sits between the barrier before the store and the next
+// item's first barrier, so it costs no barrier of its own). Every consumer
+// thread takes the same path through the named barriers.
+template <class Compute, class Store, class After>
+__device__ void consume(const Ring& r, int my, int* err, int ctid, Compute&& compute, Store&& store, After&& after) {
   for (int k = 0; k < my; ++k) {
     const int s = k % kStages;
     const uint32_t ph = (k / kStages) & 1;
@@ -110,6 +113,7 @@ __device__ void consume(const Ring& r, int my, int* err, int ctid, Compute&& com
       bulk_wait_read<1>();  // the previous item's store has read its stage
       if (k >= 1) mbar_arrive(&r.empty[(k - 1) % kStages]);
     }
+    after(k, st, wrote);
   }
   if (ctid == 0) bulk_wait_all();
 }
@@ -233,7 +237,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) ssm_bulk_kernel(const __grid_
         is.item(k, row, h);
         const long long slot = *reinterpret_cast<const long long*>(reinterpret_cast<const float*>(st + kScalarOff) + kSlot);
         bulk_store_hint(p.at.state + slot * p.at.row_stride + size_t(h) * p.sh * p.sc, st, sbytes, l2_evict_first());
-      });
+      },
+      [](int, uint8_t*, bool) {});
 }
 
 // ---- mLSTM / RetNet: item = (row, group of hg heads, hg | kCW); L = sk/4 lanes
@@ -344,15 +349,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) outer_bulk_kernel(const __gri
           acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
           acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
         }
+        // the warps' partial sums, added up in `after` once every warp wrote its own
         if (rsub == 0) r.part[cw * 32 + c4] = acc;
-        named_bar(1, kCT);
-        for (int kk = ctid; kk < hg * p.sk; kk += kCT) {  // column kk % sk of head kk / sk
-          const int h = kk / p.sk, col = kk - h * p.sk;
-          float sum = 0.f;
-          for (int w = 0; w < wph; ++w) sum += reinterpret_cast<const float*>(r.part + (h * wph + w) * 32)[col];
-          out[kk] = sum;
-        }
-        named_bar(1, kCT);  // the partials are rewritten by the next item
         return true;
       },
       [&](int k, uint8_t* st) {
@@ -360,6 +358,21 @@ __global__ void __launch_bounds__(kBulkThreads, 1) outer_bulk_kernel(const __gri
         is.item(k, row, h0);
         const long long slot = *reinterpret_cast<const long long*>(reinterpret_cast<const float*>(st + kScalarOff) + kSlot);
         bulk_store_hint(p.at.state + slot * p.at.row_stride + size_t(h0) * p.sh * p.sk, st, sbytes, l2_evict_first());
+      },
+      [&](int k, uint8_t*, bool wrote) {
+        // past the barrier before the store, so every warp's partials are written;
+        // the next item rewrites them only after its first barrier, which every
+        // consumer reaches only once done here
+        if (!wrote) return;
+        int row, h0;
+        is.item(k, row, h0);
+        float* out = p.out + size_t(row) * p.o_rs + size_t(h0) * p.sk;
+        for (int kk = ctid; kk < hg * p.sk; kk += kCT) {  // column kk % sk of head kk / sk
+          const int h = kk / p.sk, col = kk - h * p.sk;
+          float sum = 0.f;
+          for (int w = 0; w < wph; ++w) sum += reinterpret_cast<const float*>(r.part + (h * wph + w) * 32)[col];
+          out[kk] = sum;
+        }
       });
 }
 
