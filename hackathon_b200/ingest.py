@@ -196,6 +196,11 @@ class IngestClient(B200InferenceClient):
             self.queue_lock = threading.RLock()
         self.ingest = RequestIngest(self.num_features, max_queue_size)
         self.clock = clock
+        self._send_lock = threading.Lock()  # heartbeats and responses never interleave on the socket
+
+    def _send(self, data: bytes) -> None:
+        with self._send_lock:
+            self.socket.sendall(data)
 
     def _fields(self, msg):
         return msg if isinstance(msg, dict) else vars(msg)
@@ -278,8 +283,8 @@ class IngestClient(B200InferenceClient):
                 now = int(time.time())
                 if now % 5 == 0 and now - last_hb >= 5:
                     # Heartbeat(timestamp) as ProtocolHandler.encode writes it
-                    self.socket.sendall((json.dumps({"timestamp": time.time(), "message_type": "heartbeat"})
-                                         + "\n").encode("utf-8"))
+                    self._send((json.dumps({"timestamp": time.time(), "message_type": "heartbeat"})
+                                + "\n").encode("utf-8"))
                     last_hb = now
             except Exception as e:  # noqa: BLE001
                 if self.running:
@@ -293,7 +298,7 @@ class IngestClient(B200InferenceClient):
                 if out is None:
                     time.sleep(0.001)
                     continue
-                self.socket.sendall(out)
+                self._send(out)
             except Exception as e:  # noqa: BLE001
                 print(f"Process error: {e}")
                 time.sleep(0.1)
