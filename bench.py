@@ -208,6 +208,10 @@ def read_traffic_per_row(name: str):
 # ------------------------------------------------------------- reference arm
 
 
+def metric_name(wl) -> str:
+    return "requests/s (full 4-tower ensemble decode step, micro-batches <= %d)" % wl["max_batch"]
+
+
 def run_reference(a, wl):
     """The reference's CPU path (the oracle port: numpy float32, all host threads)
     on a bounded sample of the same workload; rank 0 only."""
@@ -236,11 +240,13 @@ def run_reference(a, wl):
     cores = os.cpu_count()
     cpu = {"value": value, "unit": "requests/s", "cores": cores, "kind": "port",
            "sample": f"{len(times)} steps of {sample_rows} symbols at {wl['preset']} (fp32 oracle, numpy)"}
-    line = {"impl": "reference", "metric": "requests/s (full ensemble step)", "value": value,
+    line = {"impl": "reference", "metric": metric_name(wl), "value": value,
             "unit": "requests/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": 1e3 * total / len(times), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": a.workload, "dims": wl["preset"], "rows_per_step": sample_rows},
+            "config": {"workload": a.workload, "dims": wl["preset"], "symbols": wl["symbols"],
+                       "max_batch": wl["max_batch"], "rows_per_step": sample_rows,
+                       "note": "a bounded sample: each step is one micro-batch of rows_per_step symbols"},
             "cpu_baseline": cpu,
             "e2e": {"value": value, "unit": "requests/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -364,7 +370,7 @@ def main():
     per_req = np.repeat(step_ms, [len(batches[Wm + k]) for k in range(len(step_ms))])
     if rank == 0:
         line = {
-            "metric": "requests/s (full 4-tower ensemble decode step, micro-batches <= %d)" % wl["max_batch"],
+            "metric": metric_name(wl),
             "value": value, "unit": "requests/s", "n_gpus": world, "steps": K, "warmup": Wm,
             "ms_per_step": t_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 state, %s weights" % wl["lp"], "data": "synthetic (seeded weights, N(0,1) features)",
