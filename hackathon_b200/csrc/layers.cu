@@ -106,6 +106,37 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const RmsP p) {
   if (!row_live(p.rc, r)) return;
   const float4* x = reinterpret_cast<const float4*>(p.x + size_t(r) * p.H);
   const int n4 = p.H >> 2;
+  constexpr int V = 16;  // rows of up to 32*V vectors (hidden 2048) stay in registers
+  if (n4 <= 32 * V) {
+    // every load of the row in flight at once, one pass over memory
+    float4 v[V];
+    float ss = 0.f;
+#pragma unroll
+    for (int t = 0; t < V; ++t) {
+      const int i = lane + 32 * t;
+      v[t] = i < n4 ? x[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int t = 0; t < V; ++t) ss = fmaf(v[t].x, v[t].x, fmaf(v[t].y, v[t].y, fmaf(v[t].z, v[t].z, fmaf(v[t].w, v[t].w, ss))));
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / float(p.H) + p.eps);
+#pragma unroll
+    for (int t = 0; t < V; ++t) {
+      const int i = lane + 32 * t;
+      if (i >= n4) break;
+      const float4 w = p.w ? reinterpret_cast<const float4*>(p.w)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+      const float4 o = make_float4(v[t].x * inv * w.x, v[t].y * inv * w.y, v[t].z * inv * w.z, v[t].w * inv * w.w);
+      if (p.out) reinterpret_cast<float4*>(p.out + size_t(r) * p.H)[i] = o;
+      if (p.out_lp) {
+        const size_t base = size_t(r) * p.H + size_t(i) * 4;
+        store_as(p.lp, p.out_lp, base + 0, o.x);
+        store_as(p.lp, p.out_lp, base + 1, o.y);
+        store_as(p.lp, p.out_lp, base + 2, o.z);
+        store_as(p.lp, p.out_lp, base + 3, o.w);
+      }
+    }
+    return;
+  }
   float ss = 0.f;
   for (int i = lane; i < n4; i += 32) {
     const float4 v = x[i];
