@@ -38,3 +38,15 @@ def test_harness_metrics_equal_the_oracle_predictions(tmp_path, batch_size):
     assert got["total_responses"] == req.n and got["response_rate"] == 1.0
     for t in range(4):
         np.testing.assert_allclose(got[f"tower_{t}"], want[f"tower_{t}"], rtol=1e-4, atol=1e-5)
+
+
+def test_command_line_reports_like_the_reference(tmp_path, capsys):
+    """`python -m hackathon_b200.evaluate` at the reference's default dims with
+    seeded weights: every request answered, the reference's report layout."""
+    path = tmp_path / "req.parquet"
+    write_requests(path, n=12, F=79, n_sym=3, seed=5)
+    EV.main(["--requests-parquet-file", str(path), "--batch-size", "4", "--seeded-weights"])
+    out = capsys.readouterr().out
+    assert "Total requests: 12" in out and "Total responses: 12" in out and "Response rate: 100.00%" in out
+    for name in EV.TOWER_NAMES:
+        assert f"{name}: max_error = " in out
