@@ -604,6 +604,9 @@ class Pool {
 }  // namespace
 
 struct b2e_ingest {
+  // Every entry point holds this while it touches the handle: a receive thread
+  // may feed (and so grow `syms`) while a process thread takes or names symbols.
+  mutable std::mutex mu;
   struct Sym {
     std::string name;
     std::vector<int64_t> uids;  // queued requests, oldest first
@@ -709,6 +712,7 @@ void b2e_ingest_destroy(b2e_ingest* g) { delete g; }
 int b2e_ingest_set_threads(b2e_ingest* g, int32_t threads) {
   return abi_call([&] {
     b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
     B2E_CHECK(threads >= 1 && threads <= 256, kErrInvalid, "threads must be in 1..256");
     s.pool.reset();
     if (threads > 1) s.pool = std::make_unique<Pool>(threads - 1);
@@ -718,6 +722,7 @@ int b2e_ingest_set_threads(b2e_ingest* g, int32_t threads) {
 int b2e_ingest_feed(b2e_ingest* g, const char* data, int64_t len, int32_t* n_requests, int32_t* n_other) {
   return abi_call([&] {
     b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
     B2E_CHECK(len >= 0 && (len == 0 || data != nullptr), kErrInvalid, "bad byte range");
     if (len > 0) s.buf.append(data, size_t(len));
     int32_t nr = 0, no = 0;
@@ -768,6 +773,7 @@ int b2e_ingest_feed(b2e_ingest* g, const char* data, int64_t len, int32_t* n_req
 int b2e_ingest_next_other(b2e_ingest* g, char* buf, int64_t cap, int64_t* len) {
   return abi_call([&] {
     b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
     B2E_CHECK(len != nullptr, kErrInvalid, "null length");
     if (s.others.empty()) {
       *len = -1;
@@ -783,6 +789,7 @@ int b2e_ingest_push(b2e_ingest* g, int64_t unique_id, const char* symbol, int64_
                     int32_t* queued) {
   return abi_call([&] {
     b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
     B2E_CHECK(symbol_len >= 0 && (symbol_len == 0 || symbol != nullptr), kErrInvalid, "bad symbol bytes");
     B2E_CHECK(features != nullptr, kErrInvalid, "null features");
     const bool ok = s.push(s.id_of(std::string(symbol ? symbol : "", size_t(symbol_len))), unique_id, features);
@@ -793,6 +800,7 @@ int b2e_ingest_push(b2e_ingest* g, int64_t unique_id, const char* symbol, int64_
 int b2e_ingest_next_drop(b2e_ingest* g, int32_t* symbol) {
   return abi_call([&] {
     b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
     B2E_CHECK(symbol != nullptr, kErrInvalid, "null output");
     if (s.drops.empty()) {
       *symbol = -1;
@@ -806,20 +814,25 @@ int b2e_ingest_next_drop(b2e_ingest* g, int32_t* symbol) {
 int b2e_ingest_pending(const b2e_ingest* g, int64_t* rows) {
   return abi_call([&] {
     B2E_CHECK(rows != nullptr, kErrInvalid, "null output");
-    *rows = G(g).queued;
+    const b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
+    *rows = s.queued;
   });
 }
 
 int b2e_ingest_symbol_count(const b2e_ingest* g, int32_t* n) {
   return abi_call([&] {
     B2E_CHECK(n != nullptr, kErrInvalid, "null output");
-    *n = int32_t(G(g).syms.size());
+    const b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
+    *n = int32_t(s.syms.size());
   });
 }
 
 int b2e_ingest_symbol_name(const b2e_ingest* g, int32_t symbol, char* buf, int64_t cap, int64_t* len) {
   return abi_call([&] {
     const b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
     B2E_CHECK(len != nullptr, kErrInvalid, "null length");
     B2E_CHECK(symbol >= 0 && size_t(symbol) < s.syms.size(), kErrInvalid, "unknown symbol id");
     bool taken = false;
@@ -831,6 +844,7 @@ int b2e_ingest_take(b2e_ingest* g, int64_t cap, int32_t* symbols, int64_t* uniqu
                     int32_t* round_rows, int32_t* n_rounds, int64_t* n_rows) {
   return abi_call([&] {
     b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
     B2E_CHECK(n_rounds && n_rows, kErrInvalid, "null output");
     B2E_CHECK(cap >= s.queued, kErrInvalid, "take: buffers hold fewer rows than are pending");
     B2E_CHECK(s.queued == 0 || (symbols && unique_ids && features && round_rows), kErrInvalid, "null output buffer");

@@ -56,6 +56,9 @@ class RequestIngest:
         _lib.check(self._L.b2e_ingest_create(self.num_features, int(max_queue_size), C.byref(h)))
         self._h = h
         self._names: List[str] = []
+        # guards the name cache: a receive thread (drops) and a process thread
+        # (take, then names) both grow it; the native handle has its own lock
+        self._names_lock = threading.Lock()
         if threads is not None:
             _lib.check(self._L.b2e_ingest_set_threads(self._h, int(threads)))
 
@@ -100,10 +103,11 @@ class RequestIngest:
         return bool(q.value)
 
     def symbol_name(self, sid: int) -> str:
-        while len(self._names) <= sid:
-            b = self._bytes(self._L.b2e_ingest_symbol_name, C.c_int32(len(self._names)))
-            self._names.append(b.decode("utf-8"))
-        return self._names[sid]
+        with self._names_lock:
+            while len(self._names) <= sid:
+                b = self._bytes(self._L.b2e_ingest_symbol_name, C.c_int32(len(self._names)))
+                self._names.append(b.decode("utf-8"))
+            return self._names[sid]
 
     def drops(self) -> List[str]:
         """Symbols of the requests dropped on a full queue since the last call, in order."""
@@ -238,13 +242,14 @@ class IngestClient(B200InferenceClient):
         order), then the rounds; returns the response line, or None when idle."""
         with self.queue_lock:
             rows = self.ingest.take()
+            sids = np.unique(rows.symbols)  # ascending ids = first-seen = dict order
+            names = {s: self.ingest.symbol_name(s) for s in sids.tolist()}
         n = len(rows.unique_ids)
         if n == 0:
             return None
-        sids = np.unique(rows.symbols)  # ascending ids = first-seen = dict order
         loc_of: Dict[int, Optional[tuple]] = {}
         for s in sids.tolist():
-            loc_of[s] = self._row_for(self.ingest.symbol_name(s))
+            loc_of[s] = self._row_for(names[s])
         over = np.asarray([s for s in sids.tolist() if loc_of[s] is None], np.int32)
         uids_out, preds_out = [], []
         live = np.ones(n, bool)

@@ -88,3 +88,85 @@ def test_socket_loops_answer_every_request_like_the_reference_path(monkeypatch):
     assert sorted(got) == sorted(want)
     assert_close(np.asarray([got[u] for u in sorted(got)], np.float32),
                  np.asarray([want[u] for u in sorted(got)], np.float32), 1e-4, 1e-5, "predictions")
+
+
+class SlotEchoEngine:
+    """Test double that answers each row with (its slot, its first feature, 0, 0),
+    so a response shows which state slot a request was stepped on."""
+
+    def __init__(self):
+        self._pending = []
+
+    def submit(self, slots, feats):
+        slots = np.asarray(slots, np.int32).reshape(-1)
+        feats = np.asarray(feats, np.float32)
+        out = np.zeros((len(slots), 4), np.float32)
+        out[:, 0] = slots
+        out[:, 1] = feats[:, 0]
+        self._pending.append(out)
+
+    def wait(self):
+        return self._pending.pop(0)
+
+    def close(self):
+        pass
+
+
+def test_new_symbols_arriving_while_the_process_loop_runs_keep_their_own_slots(monkeypatch):
+    """A receive thread keeps feeding lines that introduce new symbols while a
+    process thread drains and names them: every request is answered once, and
+    every symbol's requests land on one slot that no other symbol shares."""
+    cfg = streams.API_CFG
+    monkeypatch.setattr(CL.B200InferenceClient, "_make_engine",
+                        staticmethod(lambda config, weights, device, lp, cap, mb, graphs: SlotEchoEngine()))
+    n_sym, per_msg, n_msg = 3000, 16, 400
+    ing = IG.IngestClient(num_symbols=n_sym, config=cfg, weights={}, linear_dtype="fp32", max_queue_size=1000)
+    rng = np.random.default_rng(5)
+    sym_of, feat0 = {}, {}
+    msgs = []
+    uid = 0
+    for m in range(n_msg):
+        hi = min(n_sym, 8 * (m + 1))  # the symbol universe keeps growing
+        syms = [f"S{int(x)}" for x in rng.integers(0, hi, per_msg)]
+        feats = rng.standard_normal((per_msg, cfg.num_features), dtype=np.float32)
+        ids = list(range(uid, uid + per_msg))
+        uid += per_msg
+        for u, s, f in zip(ids, syms, feats):
+            sym_of[u], feat0[u] = s, float(f[0])
+        msgs.append((json.dumps({"unique_ids": ids, "symbols": syms, "features": feats.astype(float).tolist(),
+                                 "timestamp": 1.0, "message_type": "inference_request"}) + "\n").encode())
+    answers = []
+    done = threading.Event()
+
+    def receiver():
+        for b in msgs:
+            ing.receive(b)
+        done.set()
+
+    def processor():
+        while True:
+            finished = done.is_set()
+            out = ing.process_ingested()
+            if out is not None:
+                answers.append(out)
+            elif finished:
+                return
+
+    threads = [threading.Thread(target=receiver), threading.Thread(target=processor)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    got = {}
+    for line in answers:
+        d = json.loads(line)
+        for u, p in zip(d["unique_ids"], d["predictions"]):
+            assert u not in got, f"request {u} answered twice"
+            got[u] = p
+    assert sorted(got) == list(range(uid))
+    slot_of = {}
+    for u, p in got.items():
+        assert np.float32(p[1]) == np.float32(feat0[u]), "a request was answered with another's features"
+        assert slot_of.setdefault(sym_of[u], p[0]) == p[0], f"symbol {sym_of[u]} stepped on two slots"
+    assert len(set(slot_of.values())) == len(slot_of), "two symbols share a slot"
+    ing.close()
