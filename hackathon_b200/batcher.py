@@ -3,8 +3,9 @@
 * ``zipf_stream``: synthetic arrivals - symbol ids drawn from a Zipf(s) law over
   ``n_symbols`` ranks (rank r has weight r^-s), the ranks scattered over the ids
   by a seeded permutation so hot symbols do not cluster on one shard.
-* ``owner``: stable shard of a symbol id across GPUs (splitmix64 mod N). Each
-  GPU holds only its own symbols' state; no collective is needed on the path.
+* ``owner``: stable shard of a symbol key across GPUs (splitmix64 mod N; a
+  name's key is its crc32). Each GPU holds only its own symbols' state; no
+  collective is needed on the path.
 * ``micro_batches``: the reference's round rule (example_model.py:885-899) over a
   backlog - the k-th pending request of every symbol goes to round k, so a
   symbol appears at most once per batch and its requests stay in order - with
@@ -13,6 +14,7 @@
 
 from __future__ import annotations
 
+import zlib
 from typing import List, Tuple
 
 import numpy as np
@@ -28,11 +30,18 @@ def splitmix64(x: np.ndarray) -> np.ndarray:
 
 
 def owner(symbol_ids: np.ndarray, n_shards: int) -> np.ndarray:
-    """Shard of each symbol id: splitmix64(id) mod n_shards."""
+    """Shard of each symbol key: splitmix64(key) mod n_shards. The one sharding
+    rule of the package: the bench's keys are the dense symbol ids, the client's
+    the crc32 of the symbol name (``symbol_key``)."""
     if n_shards <= 1:
         return np.zeros(len(symbol_ids), np.int64)
     with np.errstate(over="ignore"):
         return (splitmix64(np.asarray(symbol_ids)) % np.uint64(n_shards)).astype(np.int64)
+
+
+def symbol_key(name: str) -> int:
+    """Integer key of a symbol name for ``owner``: crc32 of its UTF-8 bytes."""
+    return zlib.crc32(name.encode("utf-8"))
 
 
 def zipf_stream(n_symbols: int, n_requests: int, s: float = 1.1, seed: int = 0) -> np.ndarray:

@@ -18,7 +18,8 @@ InferenceResponse`` (client.py:88-92). Its semantics are the reference's:
 What changes is underneath: rows are stepped on the GPU by libb2e.so against a
 slot-indexed state table, so a round costs the live rows only (no masked pass
 over all rows, no state blend), and symbols can be spread over several GPUs by
-a stable hash of the symbol name, each GPU holding its own symbols' state.
+a stable hash of the symbol name, each GPU holding its own symbols' state (a
+symbol whose home GPU is full takes a slot on another one).
 """
 
 from __future__ import annotations
@@ -27,12 +28,12 @@ import importlib
 import math
 import os
 import time
-import zlib
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence
 
 import numpy as np
 
+from . import batcher as B
 from .config import D0, TOWER_KINDS, ModelConfig
 
 
@@ -95,8 +96,11 @@ DEFAULT_LINEAR_DTYPE = "fp16"            # example_model.py:157
 
 
 def owner_device(symbol: str, n_devices: int) -> int:
-    """Stable shard of a symbol name: crc32(name) mod the device count."""
-    return zlib.crc32(symbol.encode("utf-8")) % n_devices if n_devices > 1 else 0
+    """Home device of a symbol name: the bench's sharding rule (splitmix64 mod
+    the device count) over the name's crc32 key."""
+    if n_devices <= 1:
+        return 0
+    return int(B.owner(np.asarray([B.symbol_key(symbol)], np.int64), n_devices)[0])
 
 
 def load_reference_weights(token: Optional[str] = None) -> Dict[str, np.ndarray]:
@@ -137,6 +141,9 @@ class B200InferenceClient(_Base):
         nd = len(self.devices)
         if per_device_capacity is None:
             per_device_capacity = self.capacity if nd == 1 else int(math.ceil(self.capacity * 1.25 / nd)) + 4
+        if per_device_capacity * nd < self.capacity:
+            raise ValueError(f"{nd} devices x {per_device_capacity} slots hold fewer than num_symbols="
+                             f"{self.capacity} symbols")
         self.per_device_capacity = per_device_capacity
         if max_batch is None:
             max_batch = max(1, min(per_device_capacity, 4096))
@@ -159,11 +166,18 @@ class B200InferenceClient(_Base):
                               max_batch=max_batch, graphs=graphs)
 
     def _row_for(self, symbol: str):
-        """(engine, slot) that `symbol` owns, taking the next free slot on first sight."""
+        """(engine, slot) that `symbol` owns, taking the next free slot on first sight.
+
+        A new symbol goes to its home device (``owner_device``); when that device's
+        slots are all taken it goes to the device with the most free slots, so, as
+        in the reference (example_model.py:750-764), requests are answered with
+        zeros only once `num_symbols` distinct symbols hold every slot."""
         loc = self.symbol_to_idx.get(symbol)
         if loc is not None:
             return loc
         e = owner_device(symbol, len(self.engines))
+        if self._used[e] >= self.per_device_capacity:
+            e = min(range(len(self.engines)), key=lambda d: (self._used[d], d))
         if len(self.symbol_to_idx) >= self.capacity or self._used[e] >= self.per_device_capacity:
             if not B200InferenceClient._overflow_warned:
                 B200InferenceClient._overflow_warned = True
@@ -201,17 +215,29 @@ class B200InferenceClient(_Base):
         depth = 2
         inflight: Dict[int, List[tuple]] = {e: [] for e in queue}
         pos = {e: 0 for e in queue}
-        while any(pos[e] < len(queue[e]) or inflight[e] for e in queue):
-            for e in queue:  # top every engine up, then drain the oldest of each
-                while pos[e] < len(queue[e]) and len(inflight[e]) < depth:
-                    k, chunk, slots, f = queue[e][pos[e]]
-                    self.engines[e].submit(slots, f)
-                    inflight[e].append((k, chunk))
-                    pos[e] += 1
+        try:
+            while any(pos[e] < len(queue[e]) or inflight[e] for e in queue):
+                for e in queue:  # top every engine up, then drain the oldest of each
+                    while pos[e] < len(queue[e]) and len(inflight[e]) < depth:
+                        k, chunk, slots, f = queue[e][pos[e]]
+                        self.engines[e].submit(slots, f)
+                        inflight[e].append((k, chunk))
+                        pos[e] += 1
+                for e in queue:
+                    if inflight[e]:
+                        k, chunk = inflight[e].pop(0)
+                        out[k][chunk] = self.engines[e].wait()
+        except BaseException:
+            # an engine refused or reported a device error: collect every step
+            # still in flight, so each engine is idle again, then re-raise
             for e in queue:
-                if inflight[e]:
-                    k, chunk = inflight[e].pop(0)
-                    out[k][chunk] = self.engines[e].wait()
+                while inflight[e]:
+                    inflight[e].pop(0)
+                    try:
+                        self.engines[e].wait()
+                    except Exception:  # noqa: BLE001  (the first error is the one raised)
+                        pass
+            raise
         return out
 
     def process_batch(self, requests_by_symbol: Dict[str, List["PendingRequest"]]) -> "InferenceResponse":

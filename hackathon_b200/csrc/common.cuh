@@ -28,6 +28,7 @@ enum Status : int {
   kErrWeights = -3,   // a weight tensor is missing or has the wrong size
   kErrCapacity = -4,  // slot or batch outside the engine's capacity
   kErrInternal = -5,
+  kErrDevice = -6,    // a kernel recorded a code in the engine's device error word
 };
 
 #define B2E_CUDA(expr)                                                              \

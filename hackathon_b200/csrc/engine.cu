@@ -158,7 +158,8 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   slots_off_ = 256;  // n at 0, lane row counts from 16
   feats_off_ = (slots_off_ + 4 * R + 255) & ~size_t(255);
   preds_off_ = (feats_off_ + 4 * R * F + 255) & ~size_t(255);
-  const size_t io = preds_off_ + 16 * R + 128;
+  err_off_ = (preds_off_ + 16 * R + 15) & ~size_t(15);
+  const size_t io = err_off_ + 128;
   for (IoSet& st : io_) {
     B2E_CUDA(cudaMalloc(&st.d_io, io));
     B2E_CUDA(cudaMallocHost(&st.h_io, io));
@@ -462,6 +463,7 @@ void Engine::submit(const int* slots, const float* feats, int n) {
   // predictions out on their own stream: the next step's graph does not wait for them
   B2E_CUDA(cudaStreamWaitEvent(s_d2h_, io.stepped, 0));
   B2E_CUDA(cudaMemcpyAsync(io.h_io + preds_off_, io.d_preds, size_t(n) * 16, cudaMemcpyDeviceToHost, s_d2h_));
+  B2E_CUDA(cudaMemcpyAsync(io.h_io + err_off_, d_err_, 4, cudaMemcpyDeviceToHost, s_d2h_));
   B2E_CUDA(cudaEventRecord(io.done, s_d2h_));
   io.used = true;
   io.host_n = n;
@@ -478,6 +480,12 @@ void Engine::wait(float* preds) {
   B2E_CUDA(cudaSetDevice(opt_.device));
   B2E_CUDA(cudaEventSynchronize(io.done));
   if (preds) std::memcpy(preds, io.h_io + preds_off_, size_t(n) * 16);
+  int err = 0;
+  std::memcpy(&err, io.h_io + err_off_, 4);
+  if (err != 0)
+    throw Error(kErrDevice, "device error word " + std::to_string(err) +
+                                " after this step (101-103: a tensor-core wait timed out; 1: slots outside the "
+                                "table): its predictions and state are not valid; b2e_engine_device_error clears it");
 }
 
 void Engine::step_device(const int* d_slots, const float* d_feats, int n, float* d_preds, cudaStream_t s) {

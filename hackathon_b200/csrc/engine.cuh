@@ -41,6 +41,8 @@ class Engine {
   // raise the sticky flag read by device_error().
   void step_device(const int* d_slots, const float* d_feats, int n, float* d_preds, cudaStream_t stream);
   int device_error();  // synchronises; returns and clears the flag
+  // wait() throws kErrDevice while the flag is set (copied back with each host
+  // step's predictions), so a timed-out kernel never passes as an answer.
 
   void reset_slots(const int* slots, int n);
   void read_slot(int slot, void* host);
@@ -124,7 +126,7 @@ class Engine {
   const float *ow_ = nullptr, *ob_ = nullptr;
 
   IoSet io_[kSets];
-  size_t slots_off_ = 0, feats_off_ = 0, preds_off_ = 0;
+  size_t slots_off_ = 0, feats_off_ = 0, preds_off_ = 0, err_off_ = 0;  // err: the device error word after the step
   int next_set_ = 0;
   std::vector<int> host_fifo_;  // sets of the host steps in flight, oldest first
   int* d_err_ = nullptr;

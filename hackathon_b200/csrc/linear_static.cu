@@ -30,8 +30,9 @@ using namespace b2e;
 
 namespace {
 
-// Layout: [0, 256) the tensor-core kernel's error word (must read 0 before the
-// GEMM starts, so every call clears it); [256, 256 + kStageBytes) the input
+// Layout: [0, 256) three words - the tensor-core kernel's error word (must read
+// 0 before the GEMM starts), the code a call made without h_err left pending,
+// and the code a call with h_err reports; [256, 256 + kStageBytes) the input
 // rounded to the weight's type (fully rewritten by each call that uses it).
 constexpr size_t kHeadBytes = 256;
 constexpr size_t kStageBytes = size_t(16) << 20;  // 16 MiB
@@ -62,6 +63,22 @@ uint8_t* scratch_on_current_device() {
     g_dev_ptr[dev] = p;
   }
   return static_cast<uint8_t*>(g_dev_ptr[dev]);
+}
+
+// Start of a call: a code the last call left in the error word (that call had
+// no h_err to report it through) moves to the pending word; the error word
+// starts this call at 0.
+__global__ void k_err_begin(int* w) {
+  if (w[0] != 0) w[1] = w[0];
+  w[0] = 0;
+}
+
+// End of a call with h_err: report this call's code, or else the pending one,
+// and clear both.
+__global__ void k_err_report(int* w) {
+  w[2] = w[0] != 0 ? w[0] : w[1];
+  w[0] = 0;
+  w[1] = 0;
 }
 
 // x (f32, n elements) rounded to nearest-even in the weight's type: the
@@ -107,7 +124,8 @@ extern "C" int b2e_linear_static(const void* x, int32_t x_dtype, int32_t m, int3
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     uint8_t* scratch = scratch_on_current_device();
     int* d_err = reinterpret_cast<int*>(scratch);
-    B2E_CUDA(cudaMemsetAsync(d_err, 0, sizeof(int), s));
+    k_err_begin<<<1, 1, 0, s>>>(d_err);
+    B2E_CUDA(cudaGetLastError());
     const void* a = x;
     int a_type = x_dtype;
     if (stage) {
@@ -141,7 +159,9 @@ extern "C" int b2e_linear_static(const void* x, int32_t x_dtype, int32_t m, int3
     p.err = d_err;
     gemm(p, s);
     if (h_err) {
-      B2E_CUDA(cudaMemcpyAsync(h_err, d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+      k_err_report<<<1, 1, 0, s>>>(d_err);
+      B2E_CUDA(cudaGetLastError());
+      B2E_CUDA(cudaMemcpyAsync(h_err, d_err + 2, sizeof(int), cudaMemcpyDeviceToHost, s));
       B2E_CUDA(cudaStreamSynchronize(s));
     }
   });

@@ -124,10 +124,12 @@ class EnsembleEngine:
         return len(slots)
 
     def wait(self) -> np.ndarray:
-        n = self._pending[0] if self._pending else 0  # nothing in flight: the library refuses
+        """Predictions of the oldest submitted step. Raises B2EError with code
+        B2E_ERR_DEVICE when a kernel recorded an error in the engine's device error
+        word (the step is consumed either way; device_error() clears the word)."""
+        n = self._pending.pop(0) if self._pending else 0  # nothing in flight: the library refuses
         out = np.empty((max(n, 1), len(TOWER_KINDS)), np.float32)[:n]
         _lib.check(_lib.lib().b2e_engine_wait(self._h, out.ctypes.data))
-        self._pending.pop(0)
         return out
 
     def step_device(self, slots_t, feats_t, preds_t, n: int, stream=None):

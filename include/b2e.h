@@ -54,6 +54,11 @@ extern "C" {
 #define B2E_ERR_WEIGHTS (-3)  /* weight missing, unexpected, or wrong size */
 #define B2E_ERR_CAPACITY (-4) /* slot or batch outside the engine's capacity */
 #define B2E_ERR_INTERNAL (-5)
+#define B2E_ERR_DEVICE (-6)   /* a kernel recorded an error in the engine's device error word
+                                 (a bounded wait timed out, or a device step got slots outside
+                                 the table): that step's predictions and state are not valid.
+                                 The word stays set, and every later b2e_engine_wait fails,
+                                 until b2e_engine_device_error reads and clears it. */
 
 /* Storage type of the nn.Linear weights: LINEAR_DTYPE of example_model.py:151-157.
  * The four fp32-kept linears (example_model.py:106), BlockLinear, convs and norms
@@ -118,7 +123,9 @@ B2E_API int b2e_engine_step(b2e_engine* e, const int32_t* slots, const float* fe
 /* The same step split in two, so several devices run at once. Up to two submits
  * may be outstanding on one engine (wait returns the oldest step's
  * predictions): the second step's input copies and the first step's prediction
- * copies run beside the steps themselves. */
+ * copies run beside the steps themselves. The engine's device error word is
+ * copied back with the predictions: wait (and step) return B2E_ERR_DEVICE when
+ * it is set. */
 B2E_API int b2e_engine_submit(b2e_engine* e, const int32_t* slots, const float* features, int32_t n);
 B2E_API int b2e_engine_wait(b2e_engine* e, float* preds);
 /* Device-buffer step enqueued on `stream` (a cudaStream_t, NULL = default stream).
@@ -177,7 +184,9 @@ B2E_API int b2e_linear(const void* x, int32_t x_dtype, int32_t m, int32_t k, con
  *  - All calls share the array: calls that overlap on the GPU (other streams,
  *    other threads) race. Each call clears the error word it needs.
  *  - h_err: NULL, or a host int; when given, the call waits for the stream and
- *    stores the tensor-core kernel's error code there (0 = finished). */
+ *    stores there the tensor-core kernel's error code (0 = finished): this
+ *    call's, or, when this call finished, a code that earlier calls made with
+ *    h_err NULL left pending (kept in the array until a call reports it). */
 B2E_API int b2e_linear_static(const void* x, int32_t x_dtype, int32_t m, int32_t k, const void* w,
                               int32_t w_dtype, const void* bias, int32_t n, int32_t act, float* y,
                               int32_t* h_err, void* stream);

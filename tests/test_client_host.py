@@ -109,3 +109,64 @@ def test_sharded_client_routes_by_symbol_hash(monkeypatch):
     for sym, (e, _) in two.symbol_to_idx.items():
         assert e == CL.owner_device(sym, 2)
     assert made[0].calls and made[1].calls
+
+
+def test_full_home_device_spills_and_zeros_start_only_at_global_capacity(monkeypatch, capsys):
+    """Three devices of two slots each, six symbols allowed: a symbol whose home
+    device is full takes a slot elsewhere, and only the seventh distinct symbol
+    is answered with zeros (the reference's rule, example_model.py:750-764)."""
+    cfg = streams.API_CFG
+    sd = Wt.generate_model(cfg, seed=0)
+    made = []
+    monkeypatch.setattr(CL.B200InferenceClient, "_make_engine", staticmethod(
+        lambda config, weights, device, lp, cap, mb, graphs: made.append(OracleEngine(config, weights, cap)) or made[-1]))
+    monkeypatch.setattr(CL.B200InferenceClient, "_overflow_warned", False)
+    c = CL.B200InferenceClient(num_symbols=6, config=cfg, weights=sd, linear_dtype="fp32", devices=[0, 1, 2],
+                               per_device_capacity=2)
+    # pick names whose home device is 0, so devices 1 and 2 only fill by spilling
+    names = [n for n in (f"SYM_{i:03d}" for i in range(500)) if CL.owner_device(n, 3) == 0][:7]
+    rng = np.random.default_rng(1)
+    batch = {n: [CL.PendingRequest(i, n, rng.standard_normal(79).tolist(), 0.0)] for i, n in enumerate(names)}
+    r = c.process_batch(batch)
+    placed = [c.symbol_to_idx[n] for n in names[:6]]
+    assert sorted(placed) == [(0, 0), (0, 1), (1, 0), (1, 1), (2, 0), (2, 1)]
+    assert names[6] not in c.symbol_to_idx
+    zeros = [p for u, p in zip(r.unique_ids, r.predictions) if u == 6]
+    assert zeros == [[0.0] * 4]
+    assert all(any(v != 0.0 for v in p) for u, p in zip(r.unique_ids, r.predictions) if u != 6)
+    assert capsys.readouterr().out.count("WARNING: out of state rows") == 1
+
+
+def test_device_error_from_an_engine_raises_from_process_batch_and_drains_the_rest(monkeypatch):
+    """An engine whose wait() reports a device error (B2E_ERR_DEVICE) makes
+    process_batch raise; every other step in flight is collected first, so the
+    engines are idle and the next call runs."""
+    from hackathon_b200 import _lib
+
+    cfg = streams.API_CFG
+    sd = Wt.generate_model(cfg, seed=0)
+    client, made = make_client(monkeypatch, cfg, sd, 8, devices=[0, 1])
+    fail = {"on": True}
+    real_wait = OracleEngine.wait
+
+    def wait(self):
+        out = real_wait(self)
+        if self is made[1] and fail["on"]:
+            raise _lib.B2EError(-6, "device error word 101 after this step")
+        return out
+
+    monkeypatch.setattr(OracleEngine, "wait", wait)
+    rng = np.random.default_rng(2)
+    names = [f"SYM_{i:03d}" for i in range(6)]
+    assert {CL.owner_device(n, 2) for n in names} == {0, 1}
+    batch = {n: [CL.PendingRequest(10 * i + j, n, rng.standard_normal(79).tolist(), 0.0) for j in range(3)]
+             for i, n in enumerate(names)}
+    try:
+        client.process_batch(batch)
+        raise AssertionError("process_batch returned despite a device error")
+    except _lib.B2EError as e:
+        assert e.code == -6
+    assert not made[0]._pending and not made[1]._pending, "steps left in flight"
+    fail["on"] = False
+    r = client.process_batch(batch)
+    assert len(r.unique_ids) == 18

@@ -220,6 +220,39 @@ def test_error_paths_refuse_without_touching_state():
         assert np.array_equal(a, b)
 
 
+def test_device_error_word_fails_host_steps_until_cleared():
+    """A code in the engine's device error word (here the out-of-table slot flag
+    of a device step; a tensor-core timeout writes the same word) makes every
+    host step fail with B2E_ERR_DEVICE, through the engine and process_batch,
+    until device_error() reads and clears it; then steps answer again."""
+    cfg = C.SMALL
+    sd = Wt.generate_model(cfg, seed=0)
+    eng = EnsembleEngine(cfg, sd, capacity=4, max_batch=4)
+    f = np.random.default_rng(0).standard_normal((2, cfg.num_features), dtype=np.float32)
+    good = eng.step([0, 1], f)
+    eng.step_device(torch.tensor([0, 99], dtype=torch.int32, device=DEV), torch.zeros(2, cfg.num_features, device=DEV),
+                    torch.zeros(2, 4, device=DEV), 2)
+    for _ in range(2):
+        with pytest.raises(_lib.B2EError, match="device error word 1") as ei:
+            eng.step([2, 3], f)
+        assert ei.value.code == -6
+    assert eng.device_error() == 1
+    eng.reset_slots([0, 1])
+    assert np.array_equal(eng.step([0, 1], f), good), "after clearing, steps answer as before"
+    eng.close()
+
+    client = CL.B200InferenceClient(num_symbols=4, config=cfg, weights=sd, linear_dtype="fp32")
+    e = client.engines[0]
+    e.step_device(torch.tensor([99], dtype=torch.int32, device=DEV), torch.zeros(1, cfg.num_features, device=DEV),
+                  torch.zeros(1, 4, device=DEV), 1)
+    batch = {"SYM_001": [CL.PendingRequest(1, "SYM_001", f[0].tolist(), 0.0)]}
+    with pytest.raises(_lib.B2EError):
+        client.process_batch(batch)
+    assert e.device_error() == 1
+    assert len(client.process_batch(batch).predictions) == 1
+    client.close()
+
+
 def test_device_step_equals_host_step():
     cfg = C.SMALL
     sd = Wt.generate_model(cfg, seed=0)

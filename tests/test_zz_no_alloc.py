@@ -89,6 +89,42 @@ def test_static_scratch_matches_linear_on_two_calls_in_a_row(dt):
         assert torch.equal(linear_static(x3, w3, b3, relu=False), linear(x3, w3, b3, relu=False))
 
 
+def test_static_scratch_f32_input_within_one_rounding_of_float64():
+    """The f32-input result (x rounded into the static buffer) against a float64
+    restatement of CastLinear: x and the weight in the weight's type, exact
+    products and sums, bias added, ReLU, within the rounding bound above."""
+    for dt in (torch.bfloat16, torch.float16):
+        x, w, b = operands(512, 384, 320, dt, torch.float32, 21)
+        got = linear_static(x, w, b, relu=True)
+        want = torch.relu(x.to(dt).double() @ w.double().T + b.double())
+        excess = (got.double() - want).abs() - bound(x, w, dt)
+        assert float(excess.max()) <= 0.0, f"{dt}: worst excess {float(excess.max()):.3g}"
+
+
+def test_static_scratch_calls_allocate_no_device_memory():
+    """Repeated calls (after one warm-up round, which loads the kernels) leave
+    the device's free memory exactly where it was: no allocation on the path."""
+    dt = torch.bfloat16
+    ops = [operands(640, 512, 384, dt, torch.float32, 31), operands(300, 512, 256, dt, dt, 32)]
+    ys = [torch.empty(x.shape[0], w.shape[0], device=DEV) for x, w, _ in ops]
+    h_err = C.c_int32(-1)
+
+    def run(with_err):
+        for (x, w, b), y in zip(ops, ys):
+            _lib.check(_lib.lib().b2e_linear_static(_p(x), DT[x.dtype], x.shape[0], x.shape[1], _p(w), DT[w.dtype],
+                                                    _p(b), w.shape[0], 0, _p(y),
+                                                    C.byref(h_err) if with_err else None, _stream()))
+        torch.cuda.synchronize()
+
+    run(True)
+    run(False)
+    free0 = torch.cuda.mem_get_info(DEV)[0]
+    for i in range(5):
+        run(i % 2 == 0)
+    assert torch.cuda.mem_get_info(DEV)[0] == free0
+    assert h_err.value == 0
+
+
 def test_static_scratch_refuses_inputs_beyond_its_size():
     x = torch.zeros(4097, 2048, device=DEV)  # m * k = 8390656 > 8388608
     w = torch.zeros(16, 2048, dtype=torch.bfloat16, device=DEV)
