@@ -45,6 +45,22 @@ FP32_LINEAR_NAMES = ("dt_proj", "igate_proj", "fgate_proj", "output_proj")  # ex
 F32_EPS = float(np.finfo(np.float32).eps)  # nn.RMSNorm(eps=None) uses finfo(float32).eps
 
 
+def float64_twin():
+    """This restatement again, with every operation that runs in float32 here
+    carried out in float64 instead (the module's F32 rebound to float64): the
+    arbiter that measures how far an fp32 implementation - this one, the
+    reference's torch path, the CUDA engine - is from the exact answer of the
+    same arithmetic. Weights and inputs widen exactly; the reference's epsilon
+    constants keep their values. fp32 weights only (no CastLinear emulation)."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location(__name__ + "_float64", __file__)
+    twin = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(twin)
+    twin.F32 = np.float64
+    return twin
+
+
 # --------------------------------------------------------------- precision
 
 
@@ -393,6 +409,8 @@ class Oracle:
 
     def __init__(self, cfg: ModelConfig, sd: Dict[str, np.ndarray], lp: Optional[str] = None):
         cfg.validate()
+        if lp is not None and F32 is not np.float32:
+            raise ValueError("the float64 twin has no CastLinear emulation (lp must be None)")
         self.cfg, self.lp = cfg, lp
         self.sd = {k: np.ascontiguousarray(v, dtype=F32) for k, v in sd.items()}
 

@@ -22,6 +22,8 @@ Cases
              first-sight rows, capacity overflow answered with zeros
   d0stream   BASELINE config 1: default dims, 10,000 requests, SYM_001..SYM_016
              round-robin, one request per step (about 30 min on 8 cores)
+  d0arbiter  the first 320 requests of d0stream through the reference model in
+             float64 and in float32 (the arbiter of the fp32 D0 tolerance)
 """
 
 from __future__ import annotations
@@ -269,11 +271,52 @@ def case_d0stream(mods, n_requests):
           preds=preds, **summ)
 
 
+def case_d0arbiter(mods, n_requests):
+    """The first n_requests of BASELINE config 1 through the reference's model in
+    float64 (same seeded weights, module and state in double) and again in
+    float32: the float64 run is the arbiter that measures how far each fp32
+    implementation (the reference's torch CPU path, the CUDA engine) is from the
+    exact answer."""
+    cfg = C.D0
+    sd = Wt.generate_model(cfg, seed=0)
+    nsym = streams.D0_SYMBOLS
+    feats = streams.d0_features(n_requests)
+    out = {}
+    for tag, dt in (("f64", torch.float64), ("f32", torch.float32)):
+        m = _model(mods, cfg, sd).to(dt)
+        states = [m.init_state(1, torch.device("cpu")) for _ in range(nsym)]
+        states = [_cast_state(st, dt) for st in states]
+        preds = np.zeros((n_requests, 4), np.float64)
+        t0 = time.time()
+        with torch.inference_mode():
+            for i in range(n_requests):
+                k = i % nsym
+                p, states[k] = m(torch.from_numpy(feats[i:i + 1]).to(dt), states[k])
+                preds[i] = p.double().numpy()[0]
+                if i % 50 == 0:
+                    print(f"d0arbiter {tag} {i}/{n_requests} {time.time() - t0:.0f} s", flush=True)
+        out[f"{tag}_preds"] = preds
+        for k in range(nsym):
+            for li, leaf in enumerate(_leaves(states[k])):
+                a = leaf.double().numpy().reshape(-1) if leaf.is_floating_point() else leaf.numpy().reshape(-1)
+                out[f"{tag}_sym{k}_leaf{li}"] = streams.leaf_summary(a)
+        del m, states
+    _save("d0arbiter", {"n_requests": n_requests, "symbols": nsym, "weight_seed": 0,
+                        "input_sum": float(np.sum(feats, dtype=np.float64))}, **out)
+
+
+def _cast_state(state, dt):
+    if isinstance(state, (list, tuple)):
+        return type(state)(_cast_state(s, dt) for s in state)
+    return state.to(dt) if state.is_floating_point() else state
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
     ap.add_argument("cases", nargs="+")
     ap.add_argument("--d0-requests", type=int, default=10_000)
+    ap.add_argument("--arbiter-requests", type=int, default=320)
     a = ap.parse_args()
     mods = _import_reference(a.ref)
     for c in a.cases:
@@ -290,6 +333,8 @@ def main():
             case_api(mods, a.ref)
         elif c == "d0stream":
             case_d0stream(mods, a.d0_requests)
+        elif c == "d0arbiter":
+            case_d0arbiter(mods, a.arbiter_requests)
         else:
             raise SystemExit(f"unknown case {c}")
         print(f"{c}: {time.time() - t:.0f} s")
