@@ -18,6 +18,7 @@ DTYPES = {"fp32": 0, "bf16": 1, "fp16": 2}
 LAYER_KINDS = {"xlstm": 0, "mamba2": 1, "retnet": 2, "hawk": 3}
 FLAG_NO_PDL = 1         # B2E_FLAG_NO_PDL
 FLAG_NO_PRIORITIES = 2  # B2E_FLAG_NO_PRIORITIES
+FLAG_NO_LATENCY_PATH = 4  # B2E_FLAG_NO_LATENCY_PATH
 
 
 class B2ELibraryError(RuntimeError):
@@ -71,6 +72,7 @@ _SIGS = {
     "b2e_engine_read_slot": (C.c_int, [_P, _I32, _P, _I64]),
     "b2e_engine_write_slot": (C.c_int, [_P, _I32, _P, _I64]),
     "b2e_engine_launches": (C.c_int, [_P, _I32, _PI32]),
+    "b2e_engine_latency_rows": (C.c_int, [_P, _PI32, _PI32]),
     "b2e_engine_memory": (C.c_int, [_P, _PI64, _PI64]),
     "b2e_mlstm_step": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P]),
     "b2e_retnet_step": (C.c_int, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P]),

@@ -81,6 +81,7 @@ EngineOptions to_opts(const b2e_engine_options* o) {
   if (o->lane_towers != 0) e.lane_towers = o->lane_towers;
   e.pdl = !(o->flags & B2E_FLAG_NO_PDL);
   e.priorities = !(o->flags & B2E_FLAG_NO_PRIORITIES);
+  e.latency = !(o->flags & B2E_FLAG_NO_LATENCY_PATH);
   return e;
 }
 
@@ -208,6 +209,14 @@ int b2e_engine_launches(b2e_engine* e, int32_t n, int32_t* kernels) {
     B2E_CHECK(kernels != nullptr, kErrInvalid, "null output");
     B2E_CHECK(n >= 1 && n <= E(e).max_batch(), kErrCapacity, "batch outside 1..max_batch");
     *kernels = E(e).launches_per_step(n);
+  });
+}
+
+int b2e_engine_latency_rows(b2e_engine* e, int32_t* rows, int32_t* cluster) {
+  return guard([&] {
+    B2E_CHECK(rows != nullptr, kErrInvalid, "null output");
+    *rows = E(e).latency_rows();
+    if (cluster) *cluster = E(e).latency_cluster();
   });
 }
 

@@ -191,6 +191,29 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
 
   arena_.reset_all(s0_);
   B2E_CUDA(cudaDeviceSynchronize());
+
+  if (o.latency) {
+    // the same packed weights and state leaves, described for the latency kernel
+    LatTower lt[4];
+    std::vector<std::vector<LatBlock>> lb(4);
+    for (int t = 0; t < 4; ++t) {
+      const Tower& tw = towers_[t];
+      lt[t].kind = tw.kind;
+      lt[t].upw = static_cast<const uint8_t*>(upw_) + size_t(t) * P * fpad_ * dtype_size(lp);
+      lt[t].upb = static_cast<const uint8_t*>(upb_) + size_t(t) * P * dtype_size(lp);
+      lt[t].dnw = tw.dnw;
+      lt[t].dnb = tw.dnb;
+      for (const Block& bl : tw.blocks) {
+        LatBlock b;
+        bl.layer->latency_desc(b.L);
+        b.n1 = bl.n1; b.n2 = bl.n2;
+        b.f1w = bl.f1w; b.f1b = bl.f1b; b.f2w = bl.f2w; b.f2b = bl.f2b;
+        lb[t].push_back(b);
+      }
+    }
+    lat_ = std::make_unique<LatencyPath>(d_, lp, lt, lb, ow_, ob_, d_err_);
+    B2E_CUDA(cudaDeviceSynchronize());
+  }
 }
 
 Engine::~Engine() {
@@ -392,6 +415,7 @@ void Engine::order_after_last_step(cudaStream_t s) {
 void Engine::drain() { B2E_CUDA(cudaDeviceSynchronize()); }
 
 int Engine::launches_per_step(int n) {
+  if (n <= latency_rows()) return 1;
   B2E_CUDA(cudaSetDevice(opt_.device));
   cudaGraph_t g = nullptr;
   B2E_CUDA(cudaStreamBeginCapture(s0_, cudaStreamCaptureModeThreadLocal));
@@ -446,6 +470,26 @@ void Engine::submit(const int* slots, const float* feats, int n) {
   IoSet& io = io_[b];
   if (io.used) B2E_CUDA(cudaEventSynchronize(io.done));  // its pinned buffers are free
   const int F = d_.F;
+  if (n <= latency_rows()) {
+    // one kernel: the rows travel as launch parameters, the predictions and
+    // the error word land straight in the set's pinned buffer
+    LatIO li{};
+    li.n = n;
+    std::memcpy(li.slots, slots, size_t(n) * 4);
+    std::memcpy(li.feats, feats, size_t(n) * F * 4);
+    li.preds = reinterpret_cast<float*>(io.h_io + preds_off_);
+    li.err_out = reinterpret_cast<int*>(io.h_io + err_off_);
+    order_after_last_step(s0_);
+    lat_->launch(li, s0_);
+    B2E_CUDA(cudaEventRecord(io.stepped, s0_));
+    B2E_CUDA(cudaEventRecord(last_step_, s0_));
+    last_stream_ = s0_;
+    B2E_CUDA(cudaEventRecord(io.done, s0_));
+    io.used = true;
+    io.host_n = n;
+    host_fifo_.push_back(b);
+    return;
+  }
   std::memcpy(io.h_io, &n, 4);
   std::memcpy(io.h_io + slots_off_, slots, size_t(n) * 4);
   std::memcpy(io.h_io + feats_off_, feats, size_t(n) * F * 4);

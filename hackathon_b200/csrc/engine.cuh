@@ -4,6 +4,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "latency.cuh"
 #include "layers.cuh"
 
 namespace b2e {
@@ -19,6 +20,7 @@ struct EngineOptions {
   int lane_towers = 0xF;  // bit t: tower t takes `lanes` lanes, else one chain over all rows
   bool pdl = true;         // programmatic dependent launch inside each tower's chain
   bool priorities = true;   // the xLSTM tower's chain at high launch priority, the others low
+  bool latency = true;      // host steps of a few rows run as one kernel (latency.cuh)
 };
 
 class Engine {
@@ -54,6 +56,8 @@ class Engine {
   int max_batch() const { return opt_.max_batch; }
   int device() const { return opt_.device; }
   int launches_per_step(int n);  // kernels one step of n rows enqueues
+  int latency_rows() const { return lat_ && lat_->ok() ? lat_->max_rows() : 0; }
+  int latency_cluster() const { return lat_ && lat_->ok() ? lat_->cluster() : 0; }
   cudaStream_t stream() const { return s0_; }
   static constexpr int kSets = 2;  // step I/O buffer sets
 
@@ -141,6 +145,7 @@ class Engine {
   cudaStream_t last_stream_ = nullptr;  // where it was recorded (null: no step yet)
   std::unordered_map<long long, cudaGraphExec_t> graphs_;  // (bucket, set)
   std::vector<uint8_t> seen_;  // duplicate-slot check
+  std::unique_ptr<LatencyPath> lat_;  // one-kernel steps of a few rows
 };
 
 }  // namespace b2e

@@ -13,6 +13,7 @@
 #include "cells.cuh"
 #include "gemm.cuh"
 #include "layers.cuh"
+#include "latency.cuh"
 
 namespace b2e {
 
@@ -427,6 +428,14 @@ class Mamba2Layer : public Layer {
     B2E_CUDA(cudaGetLastError());
   }
 
+  void latency_desc(LatLayer& L) const override {
+    const void* w[] = {w1_, dtw_, dtb_, wx_, bx_, wb_, bb_, wc_, bcv_, a_, dd_, nw_, out_};
+    for (size_t i = 0; i < sizeof(w) / sizeof(w[0]); ++i) L.w[i] = w[i];
+    float* st[] = {xc_, bcs_, ccs_, ssm_};
+    const long long ss[] = {sxc_, sbc_, scc_, sssm_};
+    for (int i = 0; i < 4; ++i) { L.st[i] = st[i]; L.ss[i] = ss[i]; }
+  }
+
  private:
   Dims d_;
   int lp_, mi_, nh_, hs_, bc_, H_, n1_;
@@ -560,6 +569,13 @@ class RetNetLayer : public Layer {
     B2E_CUDA(cudaGetLastError());
   }
 
+  void latency_desc(LatLayer& L) const override {
+    L.w[0] = w1_; L.w[1] = out_; L.w[2] = decay_; L.w[3] = angle_;
+    L.st[0] = reinterpret_cast<float*>(pos_); L.ss[0] = spos_;
+    L.st[1] = sc_; L.ss[1] = ssc_;
+    L.st[2] = S_; L.ss[2] = sS_;
+  }
+
  private:
   Dims d_;
   int lp_, H_, nh_, hs_;
@@ -676,6 +692,12 @@ class HawkLayer : public Layer {
     launch_k(c.ln, k_rglru, dim3(c.rows), dim3(kRowThreads), 0, c.s, rp);
     linear(c, b.A, lp_, H_, out_, lp_, nullptr, H_, H_, out, H_, kActNone, residual, H_, nullptr, 0, post);  // out_proj (hawk.py:84)
     B2E_CUDA(cudaGetLastError());
+  }
+
+  void latency_desc(LatLayer& L) const override {
+    L.w[0] = w1_; L.w[1] = cw_; L.w[2] = cb_; L.w[3] = a_; L.w[4] = gw_; L.w[5] = out_;
+    L.st[0] = conv_; L.ss[0] = sconv_;
+    L.st[1] = h_; L.ss[1] = sh_;
   }
 
  private:
@@ -1435,6 +1457,15 @@ class XLSTMLayer : public Layer {
       launch_k(c.ln, k_xlstm_final, dim3(c.rows), dim3(kRowThreads), H_ * sizeof(float), c.s, fp);
     }
     B2E_CUDA(cudaGetLastError());
+  }
+
+  void latency_desc(LatLayer& L) const override {
+    const void* w[] = {slnw_, scw_, scb_, swcat_, sbias_, sgnw_, sgnb_, skip_, mlnw_, mw1_, wq_,
+                       wk_, wv_, mcw_, mcb_, gw_, gb_, ongw_, ongb_, down_, fnw_};
+    for (size_t k = 0; k < sizeof(w) / sizeof(w[0]); ++k) L.w[k] = w[k];
+    float* st[] = {sconv_, sh_, sc_, sn_, sm_, mconv_, C_, n_, m_};
+    const long long ss[] = {ssconv_, ssh_, ssc_, ssn_, ssm_, smconv_, sC_, sn2_, sm2_};
+    for (int k = 0; k < 9; ++k) { L.st[k] = st[k]; L.ss[k] = ss[k]; }
   }
 
  private:

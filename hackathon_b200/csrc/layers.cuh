@@ -26,6 +26,7 @@ struct Dims {
 };
 
 enum LayerKind : int { kXLSTM = 0, kMamba2 = 1, kRetNet = 2, kHawk = 3 };
+struct LatLayer;  // latency.cuh
 const char* layer_name(int kind);
 
 // Everything one enqueue of a step needs besides the layer's own buffers.
@@ -57,6 +58,10 @@ class Layer {
   // (fused_rows(c, H) must hold): the engine passes the Block's norm2 there.
   virtual void forward(const StepCtx& c, const float* in, const void* in_lp, float* out, const float* residual,
                        uint8_t* scratch, const RowEpi* post = nullptr) = 0;
+
+  // The layer's packed weights and state leaves for the latency path (latency.cu
+  // names each index per layer kind).
+  virtual void latency_desc(LatLayer& L) const = 0;
 
   static std::unique_ptr<Layer> make(int kind, const Dims& d, int lp);
 };

@@ -165,6 +165,14 @@ class EnsembleEngine:
         _lib.check(_lib.lib().b2e_engine_launches(self._h, int(n), C.byref(k)))
         return k.value
 
+    def latency_rows(self) -> Tuple[int, int]:
+        """(rows, cluster): host steps of at most `rows` rows run as one kernel,
+        one cluster of `cluster` CTAs per tower; (0, 0) when every step runs on
+        the batch graphs."""
+        r, c = C.c_int32(), C.c_int32()
+        _lib.check(_lib.lib().b2e_engine_latency_rows(self._h, C.byref(r), C.byref(c)))
+        return r.value, c.value
+
     def memory(self) -> Tuple[int, int]:
         w, s = C.c_int64(), C.c_int64()
         _lib.check(_lib.lib().b2e_engine_memory(self._h, C.byref(w), C.byref(s)))

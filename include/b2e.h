@@ -65,6 +65,7 @@ extern "C" {
  * stay float32 in every mode. */
 #define B2E_FLAG_NO_PDL 1        /* launch chain kernels without programmatic dependent launch */
 #define B2E_FLAG_NO_PRIORITIES 2 /* launch every chain at the same priority (default: the xLSTM tower's, the longest, first) */
+#define B2E_FLAG_NO_LATENCY_PATH 4 /* run every host step through the batch graphs, never the one-kernel latency path */
 
 #define B2E_DTYPE_F32 0
 #define B2E_DTYPE_BF16 1
@@ -139,8 +140,15 @@ B2E_API int b2e_engine_reset_slots(b2e_engine* e, const int32_t* slots, int32_t 
 B2E_API int b2e_engine_slot_bytes(const b2e_engine* e, int64_t* bytes);
 B2E_API int b2e_engine_read_slot(b2e_engine* e, int32_t slot, void* host, int64_t bytes);
 B2E_API int b2e_engine_write_slot(b2e_engine* e, int32_t slot, const void* host, int64_t bytes);
-/* Kernels one step of n rows launches (counted from its captured graph). */
+/* Kernels one step of n rows launches (counted from its captured graph; 1 when
+ * the step runs on the latency path). */
 B2E_API int b2e_engine_launches(b2e_engine* e, int32_t n, int32_t* kernels);
+/* Host steps of at most *rows rows run as one kernel (one thread-block cluster
+ * of *cluster CTAs per tower) instead of the batch graph; *rows = 0 when these
+ * dims or this GPU keep every step on the graphs. The latency path behind
+ * b2e_engine_step / submit; no counterpart in the reference (a property of this
+ * engine, reported for tests and measurement). */
+B2E_API int b2e_engine_latency_rows(b2e_engine* e, int32_t* rows, int32_t* cluster);
 B2E_API int b2e_engine_memory(const b2e_engine* e, int64_t* weight_bytes, int64_t* state_bytes);
 
 /* ---- fused state steps: the model/kernels.py operator API ----

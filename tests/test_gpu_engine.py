@@ -271,9 +271,11 @@ def test_device_step_equals_host_step():
 
 def test_launch_count_is_reported():
     cfg = C.SMALL
-    eng = EnsembleEngine(cfg, Wt.generate_model(cfg, 0), capacity=4, max_batch=4)
+    eng = EnsembleEngine(cfg, Wt.generate_model(cfg, 0), capacity=4, max_batch=4, flags=_lib.FLAG_NO_LATENCY_PATH)
     k = eng.launches_per_step(4)
     assert 50 < k < 400, k
+    lat = EnsembleEngine(cfg, Wt.generate_model(cfg, 0), capacity=4, max_batch=4)
+    assert lat.launches_per_step(4) == 1  # the latency path: one kernel
 
 
 def test_process_batch_on_gpu_matches_reference(capsys):
