@@ -244,3 +244,53 @@ def weight_bytes(cfg: ModelConfig, linear_dtype: str) -> int:
         lin = s.linear and s.name.split(".")[-2] not in FP32_LINEAR_NAMES
         total += n * (low if lin else 4)
     return total
+
+
+def layer_weight_bytes(kind: str, cfg: ModelConfig, linear_dtype: str) -> int:
+    """Bytes of one layer's weights as the engine stores them (see weight_bytes)."""
+    low = {"fp32": 4, "bf16": 2, "fp16": 2}[linear_dtype]
+    total = 0
+    for s in layer_specs(kind, "", cfg):
+        n = int(np.prod(s.shape))
+        lin = s.linear and s.name.split(".")[-2] not in FP32_LINEAR_NAMES
+        total += n * (low if lin else 4)
+    return total
+
+
+# ---------------------------------------------------------------------------
+# BASELINE configs 2 and 3: single-layer micro-benchmarks with stated fills.
+#
+# config 2: Mamba2(256, head_size=64, bc_head_size=64) - d_inner 512, 8 heads,
+#           d_state 64 - with a = -exp(U(0, ln 16)) and the dt bias set so that
+#           softplus(dt) lies in [1e-3, 0.1] (bias = softplus^-1(U(1e-3, 0.1)),
+#           dt_proj weights U(-1e-4, 1e-4), so W.x moves dt by ~1e-3 at most).
+# config 3: RetNet(256, num_heads=4) - heads of 64 - with decay
+#           gamma_h = 1 - 2^(-5-h) and angle theta_j = 10000^(-2 floor(j/2) / 64);
+#           and the mLSTM cell with 4 heads of 64 (a 64 x 64 matrix memory per
+#           head), which is the cell of XLSTM(128, mlstm_num_heads=4): its inner
+#           width 2 x 128 = 256 splits into 4 heads of 64.
+MICRO_CONFIGS = {
+    "mamba2": ModelConfig(hidden_size=256, proj_size=512, tower_depth=1, num_heads=8, num_features=79,
+                          mamba_head_size=64, mamba_bc_size=64),
+    "retnet": ModelConfig(hidden_size=256, proj_size=512, tower_depth=1, num_heads=4, num_features=79),
+    "xlstm": ModelConfig(hidden_size=128, proj_size=256, tower_depth=1, num_heads=4, num_features=79),
+}
+
+
+def micro_layer(kind: str, seed: int = 0) -> Tuple[ModelConfig, Dict[str, np.ndarray]]:
+    """(config, layer state_dict) of BASELINE config 2 ("mamba2") or 3
+    ("retnet", "xlstm"): the seeded layer weights with the fills stated above."""
+    cfg = MICRO_CONFIGS[kind]
+    sd = generate(layer_specs(kind, "", cfg), seed=seed)
+    rng = np.random.default_rng([seed, zlib.crc32(f"micro.{kind}".encode())])
+    if kind == "mamba2":
+        nh = 2 * cfg.hidden_size // cfg.mamba_head_size
+        sd["a"] = (-np.exp(rng.uniform(0.0, math.log(16.0), nh))).astype(np.float32)
+        target = rng.uniform(1e-3, 0.1, nh)
+        sd["dt_proj.bias"] = np.log(np.expm1(target)).astype(np.float32)  # softplus^-1
+        sd["dt_proj.weight"] = rng.uniform(-1e-4, 1e-4, sd["dt_proj.weight"].shape).astype(np.float32)
+    elif kind == "retnet":
+        nh, hs = cfg.num_heads, cfg.hidden_size // cfg.num_heads
+        sd["decay"] = (1.0 - 2.0 ** (-5.0 - np.arange(nh))).astype(np.float32)
+        sd["angle"] = (10000.0 ** (-2.0 * (np.arange(hs) // 2) / hs)).astype(np.float32)
+    return cfg, sd

@@ -22,6 +22,8 @@ Cases
              first-sight rows, capacity overflow answered with zeros
   d0stream   BASELINE config 1: default dims, 10,000 requests, SYM_001..SYM_016
              round-robin, one request per step (about 30 min on 8 cores)
+  micro      BASELINE configs 2 and 3: the Mamba2, RetNet and xLSTM layers at
+             their stated dims and fills, float32 and float64
   d0arbiter  the first 320 requests of d0stream through the reference model in
              float64 and in float32 (the arbiter of the fp32 D0 tolerance)
 """
@@ -305,6 +307,41 @@ def case_d0arbiter(mods, n_requests):
                         "input_sum": float(np.sum(feats, dtype=np.float64))}, **out)
 
 
+def case_micro(mods):
+    """BASELINE configs 2 and 3: Mamba2(256, head 64, d_state 64) with its stated
+    a / dt fills, RetNet(256, 4 heads of 64) with gamma_h = 1 - 2^(-5-h), and
+    XLSTM(128, 4 mLSTM heads of 64), each over MICRO_STEPS steps of MICRO_BATCH
+    rows (all active), in float32 and in float64 (the arbiter)."""
+    out, meta = {}, {"cases": []}
+    for kind in ("mamba2", "retnet", "xlstm"):
+        cfg, sd = Wt.micro_layer(kind, seed=0)
+        xs = streams.micro_inputs(kind)
+        for tag, dt in (("f32", torch.float32), ("f64", torch.float64)):
+            if kind == "mamba2":
+                mod = mods["model.mamba2"].Mamba2(cfg.hidden_size, head_size=cfg.mamba_head_size,
+                                                  bc_head_size=cfg.mamba_bc_size)
+            elif kind == "retnet":
+                mod = mods["model.retnet"].RetNet(cfg.hidden_size, num_heads=cfg.num_heads)
+            else:
+                mod = mods["model.xlstm"].XLSTM(cfg.hidden_size, mlstm_num_heads=cfg.num_heads,
+                                                slstm_num_heads=cfg.num_heads // 2)
+            mod = _load(mod, sd).to(dt)
+            state = _cast_state(mod.init_state(xs.shape[1], torch.device("cpu")), dt)
+            ys = []
+            with torch.inference_mode():
+                for s in range(xs.shape[0]):
+                    y, state = mod(torch.from_numpy(xs[s]).to(dt), state)
+                    ys.append(y.float().numpy())
+            # float64 results are stored rounded to float32: 6e-8 relative, far
+            # below the fp32 rounding noise (1e-6 and up) they arbitrate
+            out[f"{kind}_{tag}_y"] = np.stack(ys)
+            for i, leaf in enumerate(_leaves(state)):
+                out[f"{kind}_{tag}_state{i}"] = leaf.float().numpy() if leaf.is_floating_point() else leaf.numpy()
+        meta["cases"].append({"kind": kind, "steps": int(xs.shape[0]), "batch": int(xs.shape[1]),
+                              "input_sum": float(np.sum(xs, dtype=np.float64))})
+    _save("micro", meta, **out)
+
+
 def _cast_state(state, dt):
     if isinstance(state, (list, tuple)):
         return type(state)(_cast_state(s, dt) for s in state)
@@ -333,6 +370,8 @@ def main():
             case_api(mods, a.ref)
         elif c == "d0stream":
             case_d0stream(mods, a.d0_requests)
+        elif c == "micro":
+            case_micro(mods)
         elif c == "d0arbiter":
             case_d0arbiter(mods, a.arbiter_requests)
         else:

@@ -142,3 +142,15 @@ def leaf_summary(a: np.ndarray) -> np.ndarray:
     fin = np.isfinite(a)
     s = np.array([np.sum(a[fin], dtype=np.float64), np.sum(np.square(a[fin], dtype=np.float64))])
     return np.concatenate([s, a[sample_index(a.size)].astype(np.float64)])
+
+
+# BASELINE configs 2 and 3 (single-layer micro-benchmarks, hackathon_b200.weights.micro_layer):
+# all rows active, layer inputs N(0,1)
+MICRO_STEPS, MICRO_BATCH, MICRO_SEED = 24, 4, 31
+
+
+def micro_inputs(kind: str, steps: int = MICRO_STEPS, batch: int = MICRO_BATCH, seed: int = MICRO_SEED) -> np.ndarray:
+    from hackathon_b200.weights import MICRO_CONFIGS
+
+    h = MICRO_CONFIGS[kind].hidden_size
+    return _rng(seed).standard_normal((steps, batch, h), dtype=F32)

@@ -127,3 +127,43 @@ def test_d0_stream_first_requests_match_reference():
         # 12 blocks of K=2048/4096 float32 dot products: numpy's and torch's BLAS
         # sum in different orders, which moves the predictions by ~3e-4 relative.
         assert_close(p[0], g["preds"][i], 1e-3, 1e-3, f"request {i}")
+
+
+@pytest.mark.parametrize("kind", ["mamba2", "retnet", "xlstm"])
+def test_micro_layers_within_fp32_noise_of_the_reference_in_float64(kind):
+    """BASELINE configs 2 and 3 (tests/golden/micro.npz, the reference's layers
+    in float32 and float64): the oracle, another fp32 evaluation, is within twice
+    the reference fp32's distance from float64 (never required below 1e-4), on
+    every step's output rows and on every final state leaf."""
+    from tests import arbiter as A
+
+    g, meta = load_golden("micro")
+    (c,) = [m for m in meta["cases"] if m["kind"] == kind]
+    cfg, sd = Wt.micro_layer(kind, seed=0)
+    xs = streams.micro_inputs(kind)
+    assert np.isclose(float(np.sum(xs, dtype=np.float64)), c["input_sum"]), "input stream drifted"
+    W = O.Weights(sd)
+    state = O.init_block_state(kind, cfg, xs.shape[1])
+    ys = []
+    for s in range(xs.shape[0]):
+        y, state = O.layer_step(kind, W, xs[s], state, cfg)
+        ys.append(y)
+    A.check_fp32_rows(f"{kind} outputs", np.stack(ys), g[f"{kind}_f32_y"], g[f"{kind}_f64_y"])
+    nl = len(state)
+    A.check_fp32_leaves(kind, state, [g[f"{kind}_f32_state{i}"] for i in range(nl)],
+                        [g[f"{kind}_f64_state{i}"] for i in range(nl)])
+
+
+def test_micro_fills_are_the_stated_ones():
+    """Config 2: a = -exp(U(0, ln 16)) in [-16, -1], softplus(dt bias) in
+    [1e-3, 0.1]; config 3: gamma_h = 1 - 2^(-5-h), 64-wide heads."""
+    cfg, sd = Wt.micro_layer("mamba2")
+    assert cfg.mamba_bc_size == 64 and 2 * cfg.hidden_size // cfg.mamba_head_size == 8
+    assert np.all((sd["a"] <= -1.0) & (sd["a"] >= -16.0))
+    sp = np.log1p(np.exp(sd["dt_proj.bias"].astype(np.float64)))
+    assert np.all((sp >= 1e-3 - 1e-9) & (sp <= 0.1 + 1e-9))
+    cfg, sd = Wt.micro_layer("retnet")
+    assert cfg.hidden_size // cfg.num_heads == 64
+    np.testing.assert_allclose(sd["decay"], 1.0 - 2.0 ** (-5.0 - np.arange(4)), rtol=0, atol=1e-7)
+    cfg, _ = Wt.micro_layer("xlstm")
+    assert 2 * cfg.hidden_size // cfg.num_heads == 64
