@@ -27,6 +27,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -59,6 +60,7 @@ def parse():
     ap.add_argument("--linear-dtype", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--no-targets", action="store_true", help="skip the D1 / config 2-3 target runs")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed steps only (no e2e, latency, roofline or CPU legs): for profiling")
     return ap.parse_args()
@@ -297,9 +299,8 @@ def main():
     torch.cuda.synchronize()
     barrier(world)
     clocks = Clocks(dev)
-    out_dir = REPO / "gpurun_out"
-    out_dir.mkdir(exist_ok=True)
-    clocks.start(out_dir / f"clocks_rank{rank}.csv")
+    clock_dir = tempfile.mkdtemp(prefix="b2e_clocks_")
+    clocks.start(Path(clock_dir) / f"clocks_rank{rank}.csv")
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
     torch.cuda.synchronize()
     barrier(world)
@@ -362,12 +363,18 @@ def main():
         roof = dominant_kernel_roofline(cfg, wl, dev, K)
     launches = eng.launches_per_step(wl["max_batch"])
     nb = step_bytes(cfg, wl["lp"], int(np.mean([len(batches[Wm + k]) for k in range(K)])))
+    lat_rows, lat_cl = eng.latency_rows()
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline(cfg, wl)
 
     per_req = np.repeat(step_ms, [len(batches[Wm + k]) for k in range(len(step_ms))])
+    tg = None
+    if rank == 0 and world == 1 and not a.no_targets:
+        eng.close()  # the scale-out state table (119 GB) makes room for the target runs
+        peak = roof["peak"] if roof else 6650.0
+        tg = targets(dev, peak, K)
     if rank == 0:
         line = {
             "metric": metric_name(wl),
@@ -385,7 +392,9 @@ def main():
             "latency_us": {"batch_p50": float(np.percentile(per_req, 50) * 1e3),
                            "batch_p99": float(np.percentile(per_req, 99) * 1e3),
                            "single_request_p50": float(np.percentile(lat, 50)),
-                           "single_request_p99": float(np.percentile(lat, 99))},
+                           "single_request_p99": float(np.percentile(lat, 99)),
+                           "single_request_path": (f"one kernel, {lat_cl}-CTA cluster per tower" if lat_rows
+                                                   else "batch graph")},
             "hbm_gbs_step": nb / (t_max / K / 1e3) / 1e9,
             "e2e": {"value": e2e_val, "unit": "requests/s", "h2d_bytes_per_step": h2d // K,
                     "d2h_bytes_per_step": d2h // K},
@@ -393,6 +402,7 @@ def main():
             "roofline": roof,
             "cpu_baseline": cpu,
             "clocks": clk,
+            "targets": tg,
         }
         print(json.dumps(line), flush=True)
     eng.close()
@@ -443,6 +453,90 @@ def dominant_kernel_roofline(cfg, wl, dev, K):
             "unit": "GB/s", "frac": achieved / peak, "traffic": None if tr is None else tr * rows,
             "bytes_per_launch": rows * per_row, "launch_us": t * 1e6,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs" if pk.exists() else "fallback 6650 GB/s"}
+
+
+def _lat(eng, slots, F, n=220, skip=20):
+    """Single-request latency through the host API (b2e_engine_step), microseconds:
+    (p50, p99) over n - skip calls, rows at the given slots in turn."""
+    one = np.zeros((1, F), np.float32)
+    lat = []
+    for i in range(n):
+        s = slots[i % len(slots)]
+        t1 = time.perf_counter()
+        eng.step(np.asarray([s], np.int32), one)
+        lat.append((time.perf_counter() - t1) * 1e6)
+    lat = np.asarray(lat[skip:])
+    return float(np.percentile(lat, 50)), float(np.percentile(lat, 99))
+
+
+def _device_steps(step, K, W, stream):
+    """Mean ms of one step over K device-timed steps after W warm-up ones."""
+    import torch
+
+    for _ in range(W):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(K):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / K
+
+
+def targets(dev, peak, K):
+    """The north_star's target row and BASELINE configs 2 and 3, beside the headline:
+    * d1_4096: the full ensemble at D1 (depth 12), 4096 symbols per step, bf16
+      weights, fp32 state: requests/s and the whole step's HBM fraction;
+    * single-request latency (host API, one row) at D1 and D2;
+    * config2 / config3: the Mamba2 layer (d_state 64, stated a / dt fills), the
+      RetNet layer (4 heads of 64, gamma_h = 1 - 2^(-5-h)) and the xLSTM layer
+      whose mLSTM cell has 4 heads of 64, each 4096 symbols x 1,000 steps, bf16
+      weights: ms per step and HBM fraction of weights + state read and written."""
+    import torch
+
+    from hackathon_b200 import config as C
+    from hackathon_b200 import weights as Wt
+    from hackathon_b200.engine import EnsembleEngine, LayerEngine, leaf_layout
+
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    cfg = C.D1
+    sd = Wt.generate_model(cfg, seed=0)
+    rows = 4096
+    eng = EnsembleEngine(cfg, sd, device=dev.index, linear_dtype="bf16", capacity=rows, max_batch=rows)
+    rng = np.random.default_rng(3)
+    slots = torch.from_numpy(rng.permutation(rows).astype(np.int32)).to(dev)
+    feats = torch.from_numpy(rng.standard_normal((rows, cfg.num_features), dtype=np.float32)).to(dev)
+    preds = torch.empty(rows, 4, device=dev)
+    ms = _device_steps(lambda: eng.step_device(slots, feats, preds, rows), max(K, 10), 3, stream)
+    assert eng.device_error() == 0
+    nb = step_bytes(cfg, "bf16", rows)
+    out["d1_4096"] = {"requests_per_s": rows / (ms / 1e3), "ms_per_step": ms, "bytes_per_step": nb,
+                      "hbm_gbs": nb / (ms / 1e3) / 1e9, "hbm_frac": nb / (ms / 1e3) / 1e9 / peak,
+                      "launches_per_step": eng.launches_per_step(rows)}
+    lr, cl = eng.latency_rows()
+    p50, p99 = _lat(eng, list(range(64)), cfg.num_features)
+    out["d1_single_request_us"] = {"p50": p50, "p99": p99, "path": f"one kernel, {cl}-CTA cluster per tower"
+                                   if lr else "batch graph"}
+    eng.close()
+    del sd
+    for name, kinds in (("config2", ["mamba2"]), ("config3", ["retnet", "xlstm"])):
+        res = {}
+        for kind in kinds:
+            mc, msd = Wt.micro_layer(kind, seed=0)
+            le = LayerEngine(kind, mc, msd, device=dev.index, linear_dtype="bf16", capacity=rows, max_batch=rows)
+            x = torch.from_numpy(rng.standard_normal((rows, mc.hidden_size), dtype=np.float32)).to(dev)
+            y = torch.empty(rows, mc.hidden_size, device=dev)
+            ms = _device_steps(lambda: le.step_device(slots, x, y), 1000, 5, stream)
+            srow = sum(int(np.prod(sh)) * dt.itemsize for sh, dt in leaf_layout(kind, mc))
+            nbk = Wt.layer_weight_bytes(kind, mc, "bf16") + rows * (2 * srow + 2 * mc.hidden_size * 4)
+            res[kind] = {"ms_per_step": ms, "steps": 1000, "symbols": rows, "bytes_per_step": nbk,
+                         "hbm_frac": nbk / (ms / 1e3) / 1e9 / peak}
+            le.close()
+        out[name] = res
+    return out
 
 
 def cpu_baseline(cfg, wl):
