@@ -98,6 +98,7 @@ _SIGS = {
     "b2e_ingest_symbol_count": (C.c_int, [_P, _PI32]),
     "b2e_ingest_symbol_name": (C.c_int, [_P, _I32, _P, _I64, _PI64]),
     "b2e_ingest_take": (C.c_int, [_P, _I64, _P, _P, _P, _P, _PI32, _PI64]),
+    "b2e_ingest_take_batch": (C.c_int, [_P, _I32, _P, _P, _P, _PI32]),
     "b2e_encode_response": (C.c_int, [_P, _P, _I64, _I32, C.c_double, _P, _I64, _PI64]),
 }
 

@@ -609,8 +609,17 @@ struct b2e_ingest {
   mutable std::mutex mu;
   struct Sym {
     std::string name;
-    std::vector<int64_t> uids;  // queued requests, oldest first
+    std::vector<int64_t> uids;  // queued requests, oldest first, from `head`
     std::vector<float> feats;
+    std::vector<uint64_t> seqs;  // arrival order of each queued request
+    size_t head = 0;             // requests before it were taken by take_batch
+    size_t len() const { return uids.size() - head; }
+    void clear() {
+      uids.clear();
+      feats.clear();
+      seqs.clear();
+      head = 0;
+    }
   };
   int F = 0;
   int max_queue = 0;  // <= 0: unbounded, like queue.Queue(maxsize=0)
@@ -619,6 +628,7 @@ struct b2e_ingest {
   std::vector<Sym> syms;
   std::unordered_map<std::string, int32_t> ids;
   std::vector<int32_t> active;  // symbols with queued requests
+  uint64_t seq = 0;             // arrivals so far
   std::deque<std::string> others;
   std::deque<int32_t> drops;
   int64_t queued = 0;
@@ -638,20 +648,21 @@ struct b2e_ingest {
     auto it = ids.find(s);
     if (it != ids.end()) return it->second;
     const int32_t id = int32_t(syms.size());
-    syms.push_back(Sym{s, {}, {}});
+    syms.push_back(Sym{s, {}, {}, {}, 0});
     ids.emplace(s, id);
     return id;
   }
   // _handle_request for one request (client.py:162-173).
   bool push(int32_t id, int64_t uid, const float* f) {
     Sym& y = syms[size_t(id)];
-    if (max_queue > 0 && y.uids.size() >= size_t(max_queue)) {
+    if (max_queue > 0 && y.len() >= size_t(max_queue)) {
       drops.push_back(id);
       return false;
     }
-    if (y.uids.empty()) active.push_back(id);
+    if (y.len() == 0) active.push_back(id);
     y.uids.push_back(uid);
     y.feats.insert(y.feats.end(), f, f + F);
+    y.seqs.push_back(seq++);
     ++queued;
     return true;
   }
@@ -850,7 +861,7 @@ int b2e_ingest_take(b2e_ingest* g, int64_t cap, int32_t* symbols, int64_t* uniqu
     B2E_CHECK(s.queued == 0 || (symbols && unique_ids && features && round_rows), kErrInvalid, "null output buffer");
     std::sort(s.active.begin(), s.active.end());  // ids are first-sight order: the dict order
     size_t depth = 0;
-    for (int32_t id : s.active) depth = std::max(depth, s.syms[size_t(id)].uids.size());
+    for (int32_t id : s.active) depth = std::max(depth, s.syms[size_t(id)].len());
     const size_t F = size_t(s.F);
     int64_t row = 0;
     int32_t rounds = 0;
@@ -860,25 +871,67 @@ int b2e_ingest_take(b2e_ingest* g, int64_t cap, int32_t* symbols, int64_t* uniqu
       size_t w = 0;
       for (int32_t id : live) {
         const b2e_ingest::Sym& y = s.syms[size_t(id)];
-        if (y.uids.size() <= k) continue;
+        if (y.len() <= k) continue;
         live[w++] = id;
         symbols[row] = id;
-        unique_ids[row] = y.uids[k];
-        std::memcpy(features + size_t(row) * F, y.feats.data() + k * F, F * sizeof(float));
+        unique_ids[row] = y.uids[y.head + k];
+        std::memcpy(features + size_t(row) * F, y.feats.data() + (y.head + k) * F, F * sizeof(float));
         ++row;
         ++in_round;
       }
       live.resize(w);
       round_rows[rounds++] = in_round;
     }
-    for (int32_t id : s.active) {
-      s.syms[size_t(id)].uids.clear();
-      s.syms[size_t(id)].feats.clear();
-    }
+    for (int32_t id : s.active) s.syms[size_t(id)].clear();
     s.active.clear();
     s.queued = 0;
     *n_rounds = rounds;
     *n_rows = row;
+  });
+}
+
+int b2e_ingest_take_batch(b2e_ingest* g, int32_t max_rows, int32_t* symbols, int64_t* unique_ids, float* features,
+                          int32_t* n_rows) {
+  return abi_call([&] {
+    b2e_ingest& s = G(g);
+    std::lock_guard<std::mutex> lk(s.mu);
+    B2E_CHECK(n_rows != nullptr && max_rows >= 0, kErrInvalid, "bad output");
+    const size_t n = std::min(size_t(max_rows), s.active.size());
+    B2E_CHECK(n == 0 || (symbols && unique_ids && features), kErrInvalid, "null output buffer");
+    // the n symbols whose oldest queued request arrived first, in that order
+    std::vector<std::pair<uint64_t, int32_t>> heads;
+    heads.reserve(s.active.size());
+    for (int32_t id : s.active) {
+      const b2e_ingest::Sym& y = s.syms[size_t(id)];
+      heads.emplace_back(y.seqs[y.head], id);
+    }
+    std::partial_sort(heads.begin(), heads.begin() + std::ptrdiff_t(n), heads.end());
+    const size_t F = size_t(s.F);
+    bool emptied = false;
+    for (size_t r = 0; r < n; ++r) {
+      b2e_ingest::Sym& y = s.syms[size_t(heads[r].second)];
+      symbols[r] = heads[r].second;
+      unique_ids[r] = y.uids[y.head];
+      std::memcpy(features + r * F, y.feats.data() + y.head * F, F * sizeof(float));
+      ++y.head;
+      if (y.len() == 0) {
+        y.clear();
+        emptied = true;
+      } else if (y.head >= 64 && 2 * y.head >= y.uids.size()) {  // keep a long-lived queue compact
+        y.uids.erase(y.uids.begin(), y.uids.begin() + std::ptrdiff_t(y.head));
+        y.seqs.erase(y.seqs.begin(), y.seqs.begin() + std::ptrdiff_t(y.head));
+        y.feats.erase(y.feats.begin(), y.feats.begin() + std::ptrdiff_t(y.head * F));
+        y.head = 0;
+      }
+    }
+    if (emptied) {
+      size_t w = 0;
+      for (int32_t id : s.active)
+        if (s.syms[size_t(id)].len() > 0) s.active[w++] = id;
+      s.active.resize(w);
+    }
+    s.queued -= int64_t(n);
+    *n_rows = int32_t(n);
   });
 }
 

@@ -15,7 +15,9 @@ comes back whole, in order, to be decoded by the reference's own
 ``ProtocolHandler`` (``IngestClient.receive``), so no line is read differently.
 ``take()`` returns the drained requests as flat arrays in round order.
 ``encode_response`` writes the bytes ``ProtocolHandler.encode`` would.
-``IngestClient`` is ``B200InferenceClient`` wired to both.
+``IngestClient`` is ``B200InferenceClient`` wired to both; its process loop
+either answers micro-batches as they form (continuous batching, the default)
+or drains every queue into the reference's rounds.
 """
 
 from __future__ import annotations
@@ -137,6 +139,21 @@ class RequestIngest:
         return IngestRows(sym, uid, feats, rr[:nr.value].copy())
 
 
+    def take_batch(self, max_rows: int) -> IngestRows:
+        """One micro-batch (continuous batching): the oldest queued request of up
+        to `max_rows` distinct symbols, in the arrival order of those requests;
+        later requests of those symbols stay queued (b2e_ingest_take_batch)."""
+        m = max(0, int(max_rows))
+        sym = np.empty(m, np.int32)
+        uid = np.empty(m, np.int64)
+        feats = np.empty((m, self.num_features), np.float32)
+        n = C.c_int32()
+        _lib.check(self._L.b2e_ingest_take_batch(self._h, m, sym.ctypes.data, uid.ctypes.data, feats.ctypes.data,
+                                                 C.byref(n)))
+        k = n.value
+        return IngestRows(sym[:k], uid[:k], feats[:k], np.asarray([k], np.int32) if k else np.zeros(0, np.int32))
+
+
 def encode_response(unique_ids, predictions, client_timestamp: float) -> bytes:
     """ProtocolHandler.encode(InferenceResponse(unique_ids, predictions,
     client_timestamp)) for float32 predictions [n, n_out]."""
@@ -193,8 +210,11 @@ class IngestClient(B200InferenceClient):
     written natively. ``receive(bytes)`` and ``process_ingested()`` are the two
     halves; ``run()`` drives them from the socket like the reference's threads."""
 
-    def __init__(self, *args, max_queue_size: int = 100, clock=time.time, **kw):
+    def __init__(self, *args, max_queue_size: int = 100, clock=time.time, batching: str = "continuous", **kw):
         super().__init__(*args, **kw)
+        if batching not in ("continuous", "rounds"):
+            raise ValueError(f"batching must be 'continuous' or 'rounds', got {batching!r}")
+        self.batching = batching
         self.max_queue_size = max_queue_size
         if not hasattr(self, "queue_lock"):
             self.queue_lock = threading.RLock()
@@ -273,6 +293,29 @@ class IngestClient(B200InferenceClient):
         preds_out += self._run_rounds(rounds)
         return encode_response(np.concatenate(uids_out), np.concatenate(preds_out), self.clock())
 
+    def process_continuous(self) -> Optional[bytes]:
+        """Continuous batching: answer one micro-batch formed from whatever is
+        queued now - the oldest request of up to max_batch distinct symbols, in
+        arrival order (RequestIngest.take_batch) - and return its response line,
+        or None when idle. A symbol's requests still reach the model one per
+        step and in order; a micro-batch does not wait for a whole drain, so a
+        request's answer never waits behind a deep backlog's later rounds.
+        Symbols without a state slot are answered with zeros (example_model.py:
+        750-764)."""
+        with self.queue_lock:
+            rows = self.ingest.take_batch(self.max_batch)
+            names = {s: self.ingest.symbol_name(s) for s in np.unique(rows.symbols).tolist()}
+        n = len(rows.unique_ids)
+        if n == 0:
+            return None
+        locs = [self._row_for(names[s]) for s in rows.symbols.tolist()]
+        live = np.asarray([loc is not None for loc in locs], bool)
+        preds = np.zeros((n, self.num_outputs), np.float32)
+        if live.any():
+            idx = np.nonzero(live)[0]
+            preds[idx] = self._run_rounds([([locs[i] for i in idx.tolist()], rows.features[idx])])[0]
+        return encode_response(rows.unique_ids, preds, self.clock())
+
     # ---- socket driving (client.py:125-200); the reference's connect() and
     # run() start these two threads
     def _receive_loop(self):
@@ -297,9 +340,10 @@ class IngestClient(B200InferenceClient):
                     break
 
     def _process_loop(self):
+        step = self.process_continuous if self.batching == "continuous" else self.process_ingested
         while self.running:
             try:
-                out = self.process_ingested()
+                out = step()
                 if out is None:
                     time.sleep(0.001)
                     continue

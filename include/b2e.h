@@ -259,6 +259,16 @@ B2E_API int b2e_ingest_symbol_name(const b2e_ingest* g, int32_t symbol, char* bu
 B2E_API int b2e_ingest_take(b2e_ingest* g, int64_t cap, int32_t* symbols, int64_t* unique_ids, float* features,
                             int32_t* round_rows, int32_t* n_rounds, int64_t* n_rows);
 
+/* One micro-batch for continuous batching: the oldest queued request of each of
+ * up to max_rows distinct symbols, taken in the arrival order of those requests;
+ * a symbol's later requests stay queued for later calls, so its requests are
+ * still taken in order and at most once per batch. The request loop's
+ * counterpart of b2e_ingest_take (client.py:202-220's drain and
+ * example_model.py:885-899's rounds) for a caller that steps batches as they
+ * form instead of waiting for a whole drain. */
+B2E_API int b2e_ingest_take_batch(b2e_ingest* g, int32_t max_rows, int32_t* symbols, int64_t* unique_ids,
+                                  float* features, int32_t* n_rows);
+
 /* The bytes ProtocolHandler.encode(InferenceResponse(unique_ids, predictions,
  * client_timestamp)) produces: json.dumps' layout and float repr (predictions
  * widened float32 -> double as p.astype(float).tolist() does), newline

@@ -292,3 +292,52 @@ def test_parallel_parsing_queues_exactly_what_one_thread_does():
     assert a[0] == b[0] and len(a[0]) == sum(1 for m in range(300) if m % 37 == 5)
     assert a[1] == b[1] and a[2] == b[2] and a[4] == b[4] and a[5] == b[5]
     assert _same_f32(a[3], b[3])
+
+
+def test_take_batch_is_the_continuous_batching_rule():
+    """b2e_ingest_take_batch picks, batch after batch, exactly the requests
+    hackathon_b200.batcher.continuous_batches picks from the same arrivals (the
+    oldest head request of up to k distinct symbols, oldest first), also when
+    new arrivals land between batches, and every request comes out once with
+    its own features."""
+    from hackathon_b200 import batcher as B
+    from hackathon_b200 import ingest as IG
+
+    rng = np.random.default_rng(4)
+    stream = B.zipf_stream(40, 600, 1.1, seed=2)
+    feats = rng.standard_normal((len(stream), 5), dtype=np.float32)
+    ing = IG.RequestIngest(5, max_queue_size=0)
+    for i, sym in enumerate(stream):
+        assert ing.push(i, f"S{int(sym)}", feats[i])
+    got = []
+    while True:
+        rows = ing.take_batch(7)
+        if len(rows.unique_ids) == 0:
+            break
+        assert len(set(rows.symbols.tolist())) == len(rows.symbols), "a symbol twice in one batch"
+        assert np.array_equal(rows.features, feats[rows.unique_ids])
+        got.append(rows.unique_ids.tolist())
+    want = [b.tolist() for b in B.continuous_batches(stream, 7)]
+    assert got == want
+    assert ing.pending() == 0
+
+    # arrivals between batches: a second stream after the first batch
+    ing2 = IG.RequestIngest(5, max_queue_size=0)
+    for i in range(100):
+        ing2.push(i, f"S{int(stream[i])}", feats[i])
+    first = ing2.take_batch(7).unique_ids.tolist()
+    for i in range(100, 200):
+        ing2.push(i, f"S{int(stream[i])}", feats[i])
+    rest = []
+    while True:
+        rows = ing2.take_batch(7)
+        if len(rows.unique_ids) == 0:
+            break
+        rest.append(rows.unique_ids.tolist())
+    order = {}
+    for u in first + [u for b in rest for u in b]:
+        order.setdefault(int(stream[u]), []).append(u)
+    assert all(v == sorted(v) for v in order.values()), "a symbol's requests out of order"
+    assert sorted(first + [u for b in rest for u in b]) == list(range(200))
+    ing.close()
+    ing2.close()

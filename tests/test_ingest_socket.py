@@ -12,6 +12,7 @@ import threading
 import time
 
 import numpy as np
+import pytest
 
 from hackathon_b200 import client as CL
 from hackathon_b200 import ingest as IG
@@ -27,7 +28,8 @@ def _client(monkeypatch, cls, cfg, sd, **kw):
     return cls(num_symbols=6, config=cfg, weights=sd, linear_dtype="fp32", **kw)
 
 
-def test_socket_loops_answer_every_request_like_the_reference_path(monkeypatch):
+@pytest.mark.parametrize("batching", ["continuous", "rounds"])
+def test_socket_loops_answer_every_request_like_the_reference_path(monkeypatch, batching):
     cfg = streams.API_CFG
     sd = Wt.generate_model(cfg, seed=0)
     rng = np.random.default_rng(12)
@@ -52,7 +54,7 @@ def test_socket_loops_answer_every_request_like_the_reference_path(monkeypatch):
     r = ref.process_batch(by_sym)
     want = dict(zip(r.unique_ids, r.predictions))
 
-    ing = _client(monkeypatch, IG.IngestClient, cfg, sd, max_queue_size=100)
+    ing = _client(monkeypatch, IG.IngestClient, cfg, sd, max_queue_size=100, batching=batching)
     a, b = socket.socketpair()
     ing.socket = a
     ing.running = True
