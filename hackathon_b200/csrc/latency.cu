@@ -38,6 +38,7 @@
 #include <cstring>
 
 #include "latency.cuh"
+#include "mbarrier.cuh"
 
 namespace b2e {
 namespace {
@@ -66,7 +67,7 @@ __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.w
 
 // rows x row_bytes from src (src_stride bytes apart) into shared memory
 // (dst_stride bytes apart), spread over the CTA's threads; asynchronous.
-__device__ __noinline__ void pf2d(void* dst, const void* src, int rows, int row_bytes, long long src_stride,
+__device__ __forceinline__ void pf2d(void* dst, const void* src, int rows, int row_bytes, long long src_stride,
                                   int dst_stride) {
   if (rows <= 0 || row_bytes <= 0) return;
   const bool v16 = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0 &&
@@ -84,7 +85,17 @@ __device__ __noinline__ void pf2d(void* dst, const void* src, int rows, int row_
       cp4(d, s);
   }
 }
-__device__ __forceinline__ void pf1d(void* dst, const void* src, int bytes) { pf2d(dst, src, 1, bytes, 0, 0); }
+// One contiguous segment: no per-chunk row arithmetic.
+__device__ __forceinline__ void pf1d(void* dst, const void* src, int bytes) {
+  if (bytes <= 0) return;
+  char* d = static_cast<char*>(dst);
+  const char* sp = static_cast<const char*>(src);
+  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | uintptr_t(bytes)) & 15) == 0) {
+    for (int i = threadIdx.x * 16; i < bytes; i += kThreads * 16) cp16(d + i, sp + i);
+  } else {
+    for (int i = threadIdx.x * 4; i < bytes; i += kThreads * 4) cp4(d + i, sp + i);
+  }
+}
 
 // A 16-byte aligned bump allocator over one stage buffer; prefetch and compute
 // of a stage carve the same sequence, so they agree on every offset.
@@ -149,7 +160,7 @@ struct WVec<__half> {
 // W and X in shared memory, W rows 16-byte aligned (ldw elements apart); eight
 // lanes per row, four rows per warp at a time.
 template <class WT>
-__device__ __noinline__ void gemv(const WT* W, int ldw, int K, int nrows, const float* X, int ldx, int R, float* out,
+__device__ __forceinline__ void gemv(const WT* W, int ldw, int K, int nrows, const float* X, int ldx, int R, float* out,
                                   int ldo) {
   constexpr int V = WVec<WT>::N;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane & 7, grp = lane >> 3;
@@ -194,7 +205,7 @@ __device__ __noinline__ void gemv(const WT* W, int ldw, int K, int nrows, const 
 
 // out[r*2 + j] = sum_k W[j*ldw + k] * X[r*ldx + k] for j < 2 rows of a long K,
 // with every thread of the CTA (f32 weights). `red` holds kWarps*8 floats.
-__device__ __noinline__ void dot2_wide(const float* W, int ldw, int K, const float* X, int ldx, int R, float* out,
+__device__ __forceinline__ void dot2_wide(const float* W, int ldw, int K, const float* X, int ldx, int R, float* out,
                                        float* red) {
   float a[2][kLatMaxRows] = {};
   const int K4 = K / 4;
@@ -237,35 +248,26 @@ __device__ __noinline__ void dot2_wide(const float* W, int ldw, int K, const flo
   __syncthreads();
 }
 
-// Per row r < R: the sum of f(x[r*ld + i]) over i < n, every thread gets it.
-// `red` holds kWarps*kLatMaxRows floats.
+// Per row r < R: the sum of f(x[r*ld + i]) over i < n, computed by every warp
+// on its own (lanes stride the row, then a shuffle reduction), so no block
+// barrier is needed before the result is used. `red` is unused.
 template <class F>
-__device__ void row_sums(const float* x, int ld, int n, int R, F f, float* red, float* out) {
-  float a[kLatMaxRows] = {0.f, 0.f, 0.f, 0.f};
-  for (int i = threadIdx.x; i < n; i += kThreads)
-#pragma unroll
-    for (int r = 0; r < kLatMaxRows; ++r)
-      if (r < R) a[r] += f(x[r * ld + i], r);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+__device__ __forceinline__ void row_sums(const float* x, int ld, int n, int R, F f, float* red, float* out) {
+  (void)red;
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int r = 0; r < kLatMaxRows; ++r) {
-    const float s = warp_sum(a[r]);
-    if (lane == 0) red[warp * kLatMaxRows + r] = s;
+    float a = 0.f;
+    if (r < R)
+      for (int i = lane; i < n; i += 32) a += f(x[r * ld + i], r);
+    out[r] = warp_sum(a);
   }
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < kLatMaxRows; ++r) {
-    float s = 0.f;
-    for (int w = 0; w < kWarps; ++w) s += red[w * kLatMaxRows + r];
-    out[r] = s;
-  }
-  __syncthreads();
 }
 
 // RMSNorm rows: y = x / sqrt(mean(x^2) + eps) * w (w may be null), over n
 // values; y in f32 (yf, may be null) and rounded to the CastLinear type (yl).
 template <class WT>
-__device__ __noinline__ void rmsnorm(const float* x, int ld, int n, int R, const float* w, float eps, float* yf, int ldf, float* yl,
+__device__ __forceinline__ void rmsnorm(const float* x, int ld, int n, int R, const float* w, float eps, float* yf, int ldf, float* yl,
                         int ldl, float* red) {
   float ss[kLatMaxRows];
   row_sums(x, ld, n, R, [](float v, int) { return v * v; }, red, ss);
@@ -286,7 +288,7 @@ __device__ __noinline__ void rmsnorm(const float* x, int ld, int n, int R, const
 }
 
 // LayerNorm rows (no bias): y = (x - mean) / sqrt(var + eps) * w.
-__device__ __noinline__ void layernorm(const float* x, int ld, int n, int R, const float* w, float eps, float* y, int ldy,
+__device__ __forceinline__ void layernorm(const float* x, int ld, int n, int R, const float* w, float eps, float* y, int ldy,
                           float* red) {
   float s[kLatMaxRows];
   row_sums(x, ld, n, R, [](float v, int) { return v; }, red, s);
@@ -307,7 +309,7 @@ __device__ __noinline__ void layernorm(const float* x, int ld, int n, int R, con
 
 // Mean and 1/sqrt(var + eps) of G groups of gs values per row, one warp per
 // (row, group): gm[r*G + g], gr[r*G + g]. Ends with a barrier.
-__device__ __noinline__ void group_stats(const float* x, int ld, int G, int gs, int R, float eps, float* gm, float* gr) {
+__device__ __forceinline__ void group_stats(const float* x, int ld, int G, int gs, int R, float eps, float* gm, float* gr) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int p = warp; p < R * G; p += kWarps) {
     const int r = p / G, g = p - r * G;
@@ -331,7 +333,7 @@ __device__ __noinline__ void group_stats(const float* x, int ld, int G, int gs, 
 
 // Write src[r*sld + i] (local shared memory, i < cnt) to dst[r*ld + off + i]
 // in every CTA of the cluster (dst: this CTA's address of the vector).
-__device__ __noinline__ void bcast(const float* src, int sld, int cnt, int R, float* dst, int ld, int off, int CL) {
+__device__ __forceinline__ void bcast(const float* src, int sld, int cnt, int R, float* dst, int ld, int off, int CL) {
   if (cnt <= 0) return;
   cg::cluster_group cluster = cg::this_cluster();
   const bool v4 = (cnt & 3) == 0 && (off & 3) == 0 && (ld & 3) == 0 && (sld & 3) == 0;
@@ -395,7 +397,9 @@ struct Act {
   int ldH, ldP, ldT, ld1, ld2;
 };
 
-template <class WT>
+// KIND: the tower's layer kind (its index too); RT: 1 when the step has exactly
+// one row (every row loop folds away), 0 for up to kLatMaxRows rows.
+template <class WT, int KIND, int RT>
 struct Tower {
   const LatModel& M;
   const LatTower* T;       // this tower's descriptor (a shared-memory copy in the step kernel)
@@ -403,11 +407,11 @@ struct Tower {
   long long* slot;         // the step's state slots (shared memory)
   const LatIO& io;
   int fpad, F, depth;
-  int kind, rank, CL, R, RM, H, P, mi, nh_m, hs_m, bc, nh, hs_r, nbl, bs, hs_x, nh_x;  // RM: rows the carve holds
+  static constexpr int kind = KIND;
+  int rank, CL, R, RM, H, P, mi, nh_m, hs_m, bc, nh, hs_r, nbl, bs, hs_x, nh_x;  // RM: rows the carve holds
   Act a;
   bool dry = false;  // carve only (the planning pass sizes the buffers this way)
   uint32_t act_used = 0;
-
   __device__ void P2(void* dst, const void* src, int rows, int row_bytes, long long src_stride, int dst_stride) {
     if (!dry) pf2d(dst, src, rows, row_bytes, src_stride, dst_stride);
   }
@@ -420,7 +424,7 @@ struct Tower {
   // T and blocks at the shared-memory copies.
   __device__ Tower(const LatModel& m, const LatTower& t, const LatIO& i, int rk, int cl, uint8_t* act_base)
       : M(m), T(&t), blocks(t.blocks), io(i) {
-    kind = t.kind; rank = rk; CL = cl; R = i.n; RM = m.rmax;
+    rank = rk; CL = cl; R = RT ? RT : i.n; RM = m.rmax;
     fpad = m.fpad; F = m.F; depth = m.depth;
     H = m.H; P = m.P;
     mi = 2 * H; nh_m = mi / m.m_hs; hs_m = m.m_hs; bc = m.m_bc;
@@ -1168,17 +1172,8 @@ struct Tower {
       __syncthreads();
       if (n > 0) {
         bcast(xcv, n, n, R, a.V1, a.ld1, lo, CL);  // xc
-        for (int t = 0; t < 3; ++t) {
-          cg::cluster_group cluster = cg::this_cluster();
-          // q, k, v rows are strided by 3n in qkv: copy each row separately
-          for (int r = 0; r < R; ++r) {
-            const float* src = qkv + (r * 3 + t) * n;
-            for (int i = threadIdx.x; i < CL * n; i += kThreads) {
-              const int peer = i / n, k = i - peer * n;
-              *cluster.map_shared_rank(a.V1 + r * a.ld1 + (2 + t) * mi + lo + k, peer) = src[k];
-            }
-          }
-        }
+        for (int t = 0; t < 3; ++t)  // q, k, v: row r of each at qkv + (3r + t) n
+          bcast(qkv + t * n, 3 * n, n, R, a.V1, a.ld1, (2 + t) * mi + lo, CL);
       }
       const int glo = max(sl.lo, mi), ghi = max(sl.hi, mi);
       if (ghi > glo) {  // gate rows -> xg at [mi, 2mi)
@@ -1382,21 +1377,18 @@ struct Tower {
   }
 };
 
-template <class WT>
-__global__ void __launch_bounds__(kThreads, 1) k_latency_step(const LatModel* __restrict__ model, const LatIO io) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  cg::cluster_group cluster = cg::this_cluster();
-  const int CL = int(cluster.num_blocks());
-  const int rank = int(cluster.block_rank());
-  const int tower = blockIdx.x / CL;
-  const LatModel& M = *model;
-  Tower<WT> tw(M, M.t[tower], io, rank, CL, smem);
+// One tower's whole step on its cluster: prefetch of stage s+1 (every thread's
+// share of 16- and 4-byte cp.async copies) while stage s runs, the stages
+// separated by cluster barriers, then output_proj of the tower's column.
+template <class WT, int KIND, int RT>
+__device__ __noinline__ void tower_main(const LatModel& M, const LatIO& io, uint8_t* smem, int rank, int CL) {
+  Tower<WT, KIND, RT> tw(M, M.t[KIND], io, rank, CL, smem);
   tw.load_desc();
-  const uint32_t act_bytes = M.act_bytes[tower], buf_bytes = M.buf_bytes[tower];  // this tower's carve
+  const uint32_t act_bytes = M.act_bytes[KIND], buf_bytes = M.buf_bytes[KIND];  // this tower's carve
   uint8_t* buf[2] = {smem + act_bytes, smem + act_bytes + buf_bytes};
   const int ns = tw.nstages();
-  if (tower == 0 && rank == 0 && threadIdx.x == 0 && io.err_out) *io.err_out = *M.err;
-  if (rank == 0) pf1d(tw.a.OW, M.ow, M.H * 4);
+  if (KIND == 0 && rank == 0 && threadIdx.x == 0 && io.err_out) *io.err_out = *M.err;
+  if (rank == 0) pf1d(tw.a.OW, M.ow, tw.H * 4);
   tw.prefetch(0, buf[0]);
   cp_commit();
   cluster_arrive();
@@ -1417,34 +1409,54 @@ __global__ void __launch_bounds__(kThreads, 1) k_latency_step(const LatModel* __
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int r = warp; r < tw.R; r += kWarps) {
       float acc = 0.f;
-      for (int k = lane; k < M.H; k += 32) acc = fmaf(tw.a.OW[k], tw.a.X[r * tw.a.ldH + k], acc);
+      for (int k = lane; k < tw.H; k += 32) acc = fmaf(tw.a.OW[k], tw.a.X[r * tw.a.ldH + k], acc);
       acc = warp_sum(acc);
-      if (lane == 0) io.preds[r * 4 + tower] = acc + M.ob[0];
+      if (lane == 0) io.preds[r * 4 + KIND] = acc + M.ob[0];
     }
+  }
+}
+
+template <class WT, int RT>
+__global__ void __launch_bounds__(kThreads, 1) k_latency_step(const LatModel* __restrict__ model,
+                                                               const __grid_constant__ LatIO io) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int CL = int(cluster.num_blocks());
+  const int rank = int(cluster.block_rank());
+  switch (blockIdx.x / CL) {  // cluster t runs tower t (xLSTM, Mamba2, RetNet, Hawk)
+    case 0: tower_main<WT, kXLSTM, RT>(*model, io, smem, rank, CL); break;
+    case 1: tower_main<WT, kMamba2, RT>(*model, io, smem, rank, CL); break;
+    case 2: tower_main<WT, kRetNet, RT>(*model, io, smem, rank, CL); break;
+    default: tower_main<WT, kHawk, RT>(*model, io, smem, rank, CL); break;
   }
 }
 
 // Planning pass: the shared memory the kernel carves (activations; the largest
 // stage buffer over every stage, rank and tower) for the worst-case row count,
 // measured by running the kernel's own carving code with no copies issued.
-template <class WT>
-__global__ void k_latency_plan(const LatModel* __restrict__ model, int CL, uint32_t* out) {
-  const LatModel& M = *model;
+template <class WT, int KIND>
+__device__ void plan_tower(const LatModel& M, int CL, uint32_t* out) {
   LatIO io{};
   io.n = M.rmax;
-  for (int t = 0; t < 4; ++t) {
-    uint32_t act = 0, buf = 0;
-    for (int rank = 0; rank < CL; ++rank) {
-      Tower<WT> tw(M, M.t[t], io, rank, CL, nullptr);
-      long long zero_slots[kLatMaxRows] = {};
-      tw.slot = zero_slots;  // addresses are formed, nothing is read through them
-      tw.dry = true;
-      act = max(act, tw.act_used);
-      for (int s = 0; s < tw.nstages(); ++s) buf = max(buf, tw.prefetch(s, nullptr));
-    }
-    out[2 * t] = act;
-    out[2 * t + 1] = (buf + 127u) & ~127u;
+  uint32_t act = 0, buf = 0;
+  for (int rank = 0; rank < CL; ++rank) {
+    Tower<WT, KIND, 0> tw(M, M.t[KIND], io, rank, CL, nullptr);
+    long long zero_slots[kLatMaxRows] = {};
+    tw.slot = zero_slots;  // addresses are formed, nothing is read through them
+    tw.dry = true;
+    act = max(act, tw.act_used);
+    for (int s = 0; s < tw.nstages(); ++s) buf = max(buf, tw.prefetch(s, nullptr));
   }
+  out[2 * KIND] = act;
+  out[2 * KIND + 1] = (buf + 127u) & ~127u;
+}
+
+template <class WT>
+__global__ void k_latency_plan(const LatModel* __restrict__ model, int CL, uint32_t* out) {
+  plan_tower<WT, kXLSTM>(*model, CL, out);
+  plan_tower<WT, kMamba2>(*model, CL, out);
+  plan_tower<WT, kRetNet>(*model, CL, out);
+  plan_tower<WT, kHawk>(*model, CL, out);
 }
 
 }  // namespace
@@ -1454,12 +1466,12 @@ __global__ void k_latency_plan(const LatModel* __restrict__ model, int CL, uint3
 namespace {
 
 template <class WT>
-void* kernel_of() {
-  return reinterpret_cast<void*>(k_latency_step<WT>);
+void* kernel_of(int rt) {
+  return rt ? reinterpret_cast<void*>(k_latency_step<WT, 1>) : reinterpret_cast<void*>(k_latency_step<WT, 0>);
 }
 
-void* step_kernel(int lp) {
-  return lp == kBF16 ? kernel_of<__nv_bfloat16>() : lp == kF16 ? kernel_of<__half>() : kernel_of<float>();
+void* step_kernel(int lp, int rt) {
+  return lp == kBF16 ? kernel_of<__nv_bfloat16>(rt) : lp == kF16 ? kernel_of<__half>(rt) : kernel_of<float>(rt);
 }
 
 }  // namespace
@@ -1535,9 +1547,15 @@ LatencyPath::LatencyPath(const Dims& d, int lp, const LatTower (&towers)[4],
       why_ = "stage slices need " + std::to_string(smem) + " bytes of shared memory";
       continue;
     }
-    void* kern = step_kernel(lp);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
-        (CL > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)) {
+    void* kern = step_kernel(lp, 0);
+    bool refused = false;
+    for (int rt = 0; rt < 2; ++rt) {
+      void* k = step_kernel(lp, rt);
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
+          (CL > 8 && cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess))
+        refused = true;
+    }
+    if (refused) {
       cudaGetLastError();
       why_ = "cluster of " + std::to_string(CL) + " refused";
       continue;
@@ -1591,12 +1609,16 @@ void LatencyPath::launch(const LatIO& io, cudaStream_t s) const {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const LatModel* m = d_model_;
+  const bool one = io.n == 1;  // the single-request kernel: every row loop folded to one row
   if (lp_ == kBF16)
-    B2E_CUDA(cudaLaunchKernelEx(&cfg, k_latency_step<__nv_bfloat16>, m, io));
+    B2E_CUDA(one ? cudaLaunchKernelEx(&cfg, k_latency_step<__nv_bfloat16, 1>, m, io)
+                 : cudaLaunchKernelEx(&cfg, k_latency_step<__nv_bfloat16, 0>, m, io));
   else if (lp_ == kF16)
-    B2E_CUDA(cudaLaunchKernelEx(&cfg, k_latency_step<__half>, m, io));
+    B2E_CUDA(one ? cudaLaunchKernelEx(&cfg, k_latency_step<__half, 1>, m, io)
+                 : cudaLaunchKernelEx(&cfg, k_latency_step<__half, 0>, m, io));
   else
-    B2E_CUDA(cudaLaunchKernelEx(&cfg, k_latency_step<float>, m, io));
+    B2E_CUDA(one ? cudaLaunchKernelEx(&cfg, k_latency_step<float, 1>, m, io)
+                 : cudaLaunchKernelEx(&cfg, k_latency_step<float, 0>, m, io));
 }
 
 }  // namespace b2e
