@@ -14,8 +14,10 @@
 //              (M=128 features, N=BR rows, K=16 per instruction) per 128-feature
 //              half and commits each stage back to the producer and the finished
 //              accumulator to the epilogue;
-//   warps 2-5  epilogue, in two phases. Phase 1: each warp reads its 32-lane
-//              TMEM quadrant (one thread per feature, 32 rows per tcgen05.ld),
+//   warps 2-9  epilogue (kEpiWarps = 8), in two phases. Phase 1: each warp
+//              reads its 32-lane TMEM quadrant (warps w and w+4 share one quadrant
+//              and split its 32-row chunks; one thread per feature, 32 rows per
+//              tcgen05.ld),
 //              applies bias, CastLinear rounding and activation, and stages the
 //              tile row-major in the now idle operand ring. Phase 2: each warp
 //              takes whole rows (lane = 16-byte column unit) and writes them with

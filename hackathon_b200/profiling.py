@@ -4,6 +4,10 @@
         run one state-step kernel `--reps` times on a dense state (for ncu -k)
     python -m hackathon_b200.profiling layer --kind xlstm --rows 4096 --reps 4
         one layer at the bench's dims `--reps` steps (its kernels, for ncu -k)
+    python -m hackathon_b200.profiling step --preset D2 --rows 2048 --reps 4
+        the whole ensemble step on device buffers (its GEMMs, for ncu -k)
+    python -m hackathon_b200.profiling latency --preset D2 --reps 8
+        single-request steps on the one-kernel latency path (for ncu -k)
     python -m hackathon_b200.profiling launches <launch list csv>
         per-kernel launches, total time and share of an ncu launch list
     python -m hackathon_b200.profiling metrics <raw csv from ncu -i ... --page raw --csv>
@@ -138,6 +142,48 @@ def linear(m: int, k: int, n: int, reps: int, dtype: str) -> None:
     print(f"linear {dtype} m={m} k={k} n={n}: {reps} launches")
 
 
+def step(preset: str, rows: int, reps: int, dtype: str) -> None:
+    """The whole ensemble step on device buffers, `reps` times (its GEMMs and
+    state kernels, for ncu -k)."""
+    import numpy as np
+    import torch
+
+    from . import config as C
+    from . import weights as W
+    from .engine import EnsembleEngine
+
+    cfg = C.PRESETS[preset]
+    eng = EnsembleEngine(cfg, W.generate_model(cfg, 0), linear_dtype=dtype, capacity=rows, max_batch=rows)
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    slots = torch.from_numpy(rng.permutation(rows).astype(np.int32)).to(dev)
+    feats = torch.from_numpy(rng.standard_normal((rows, cfg.num_features), dtype=np.float32)).to(dev)
+    preds = torch.empty(rows, 4, device=dev)
+    for _ in range(reps):
+        eng.step_device(slots, feats, preds, rows)
+    torch.cuda.synchronize()
+    assert eng.device_error() == 0
+    print(f"step {preset} {dtype} rows={rows}: {reps} steps, {eng.launches_per_step(rows)} kernels each")
+    eng.close()
+
+
+def latency(preset: str, reps: int, dtype: str) -> None:
+    """`reps` single-request host steps (the one-kernel latency path, for ncu -k)."""
+    import numpy as np
+
+    from . import config as C
+    from . import weights as W
+    from .engine import EnsembleEngine
+
+    cfg = C.PRESETS[preset]
+    eng = EnsembleEngine(cfg, W.generate_model(cfg, 0), linear_dtype=dtype, capacity=16, max_batch=16)
+    one = np.zeros((1, cfg.num_features), np.float32)
+    for i in range(reps):
+        eng.step(np.asarray([i % 16], np.int32), one)
+    print(f"latency {preset} {dtype}: {reps} single-request steps, latency rows/cluster {eng.latency_rows()}")
+    eng.close()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -159,6 +205,15 @@ def main(argv=None):
     la.add_argument("--rows", type=int, default=4096)
     la.add_argument("--reps", type=int, default=4)
     la.add_argument("--dtype", default="bf16")
+    st = sub.add_parser("step")
+    st.add_argument("--preset", default="D2")
+    st.add_argument("--rows", type=int, default=2048)
+    st.add_argument("--reps", type=int, default=4)
+    st.add_argument("--dtype", default="bf16")
+    lt = sub.add_parser("latency")
+    lt.add_argument("--preset", default="D2")
+    lt.add_argument("--reps", type=int, default=8)
+    lt.add_argument("--dtype", default="bf16")
     sub.add_parser("launches").add_argument("csv")
     sub.add_parser("metrics").add_argument("csv")
     a = ap.parse_args(argv)
@@ -168,6 +223,10 @@ def main(argv=None):
         linear(a.m, a.k, a.n, a.reps, a.dtype)
     elif a.cmd == "layer":
         layer(a.kind, a.rows, a.reps, a.dtype)
+    elif a.cmd == "step":
+        step(a.preset, a.rows, a.reps, a.dtype)
+    elif a.cmd == "latency":
+        latency(a.preset, a.reps, a.dtype)
     elif a.cmd == "launches":
         launches(a.csv)
     else:
