@@ -11,9 +11,12 @@ seeded (hackathon_b200.weights, seed 0); data is synthetic.
 
 A step = one micro-batch through the whole ensemble on each GPU. `value` is the
 requests all ranks stepped in the K timed steps divided by the max-over-ranks
-device time (CUDA events, inputs already in HBM). `e2e` is the same metric
-through the C-ABI with HOST buffers (b2e_engine_step: H2D of slots and features,
-the step, D2H of predictions, all inside the timed region).
+device time (CUDA events around K b2e_engine_submit_device calls and their join,
+inputs already in HBM; consecutive steps overlap tower by tower). `e2e` is the
+same metric through the C-ABI with HOST buffers (b2e_engine_submit / wait, two
+steps in flight: H2D of slots and features, the step, D2H of predictions, all
+inside the timed region). `latency_us.batch_*` is a step's submit-to-wait time
+on that host path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload scaleout|d1-4096|d0-256]
     python bench.py --impl reference ...   # the reference's CPU path (oracle port), same metric
@@ -339,32 +342,34 @@ def main():
     feats = [rng.standard_normal((len(b), F), dtype=np.float32) for b in batches]
     d_slots = [torch.from_numpy(b).to(dev) for b in batches]
     d_feats = [torch.from_numpy(f).to(dev) for f in feats]
-    preds = torch.empty(wl["max_batch"], 4, device=dev)
+    preds = [torch.empty(wl["max_batch"], 4, device=dev) for _ in range(max(K, Wm))]
     stream = torch.cuda.current_stream(dev)
 
-    # ---- device-resident timing (value)
+    # ---- device-resident timing (value): b2e_engine_submit_device per micro-batch
+    # (consecutive steps overlap tower by tower), one join at the end
     for i in range(Wm):
-        eng.step_device(d_slots[i], d_feats[i], preds, len(batches[i]))
+        eng.submit_device(d_slots[i], d_feats[i], preds[i], len(batches[i]), stream=stream)
+    eng.join_device(stream=stream)
     torch.cuda.synchronize()
     barrier(world)
     clocks = Clocks(dev)
     clock_dir = tempfile.mkdtemp(prefix="b2e_clocks_")
     clocks.start(Path(clock_dir) / f"clocks_rank{rank}.csv")
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     torch.cuda.synchronize()
     barrier(world)
     ev[0].record(stream)
     rows = 0
     for k in range(K):
         i = Wm + k
-        eng.step_device(d_slots[i], d_feats[i], preds, len(batches[i]))
-        ev[k + 1].record(stream)
+        eng.submit_device(d_slots[i], d_feats[i], preds[k], len(batches[i]), stream=stream)
         rows += len(batches[i])
+    eng.join_device(stream=stream)
+    ev[1].record(stream)
     torch.cuda.synchronize()
     barrier(world)
     clk = clocks.stop()
-    step_ms = [ev[k].elapsed_time(ev[k + 1]) for k in range(K)]
-    t_ms = ev[0].elapsed_time(ev[K])
+    t_ms = ev[0].elapsed_time(ev[1])
     assert eng.device_error() == 0
     t_max = allreduce(t_ms, "max", world, dev)
     rows_all = allreduce(float(rows), "sum", world, dev)
@@ -380,19 +385,25 @@ def main():
 
     # ---- end to end through the C-ABI with host buffers (e2e): b2e_engine_submit
     # / b2e_engine_wait with two steps in flight, so a step's host->device copy
-    # and start overlap the previous step's end
+    # and towers overlap the previous step's; each step's latency is the time
+    # from its submit to the return of its wait
     barrier(world)
     t0 = time.perf_counter()
     h2d = d2h = 0
+    t_sub, t_done = [], []
     for k in range(K):
         i = Wm + K + k
+        t_sub.append(time.perf_counter())
         eng.submit(batches[i], feats[i])
         if k:
             eng.wait()
+            t_done.append(time.perf_counter())
         h2d += 4 + 4 * len(batches[i]) + 4 * F * len(batches[i])
         d2h += 16 * len(batches[i])
     eng.wait()
+    t_done.append(time.perf_counter())
     e2e_s = time.perf_counter() - t0
+    step_ms = [(d - u) * 1e3 for u, d in zip(t_sub, t_done)]
     e2e_rows = float(sum(len(batches[Wm + K + k]) for k in range(K)))
     e2e_max = allreduce(e2e_s, "max", world, dev)
     e2e_val = allreduce(e2e_rows, "sum", world, dev) / e2e_max
@@ -418,7 +429,7 @@ def main():
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline(cfg, wl)
 
-    per_req = np.repeat(step_ms, [len(batches[Wm + k]) for k in range(len(step_ms))])
+    per_req = np.repeat(step_ms, [len(batches[Wm + K + k]) for k in range(len(step_ms))])
     tg = None
     if rank == 0 and world == 1 and not a.no_targets:
         eng.close()  # the scale-out state table (119 GB) makes room for the target runs
@@ -534,6 +545,26 @@ def _device_steps(step, K, W, stream):
     return e0.elapsed_time(e1) / K
 
 
+def _device_submits(eng, slots, feats, rows, K, W, stream):
+    """Mean ms of one step over K device-timed b2e_engine_submit_device steps and
+    their join, after W warm-up ones."""
+    import torch
+
+    preds = [torch.empty(rows, 4, device=slots.device) for _ in range(max(K, W))]
+    for i in range(W):
+        eng.submit_device(slots, feats, preds[i], rows, stream=stream)
+    eng.join_device(stream=stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(K):
+        eng.submit_device(slots, feats, preds[i], rows, stream=stream)
+    eng.join_device(stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / K
+
+
 def targets(dev, peak, K):
     """The north_star's target row and BASELINE configs 2 and 3, beside the headline:
     * d1_4096: the full ensemble at D1 (depth 12), 4096 symbols per step, bf16
@@ -558,8 +589,7 @@ def targets(dev, peak, K):
     rng = np.random.default_rng(3)
     slots = torch.from_numpy(rng.permutation(rows).astype(np.int32)).to(dev)
     feats = torch.from_numpy(rng.standard_normal((rows, cfg.num_features), dtype=np.float32)).to(dev)
-    preds = torch.empty(rows, 4, device=dev)
-    ms = _device_steps(lambda: eng.step_device(slots, feats, preds, rows), max(K, 10), 3, stream)
+    ms = _device_submits(eng, slots, feats, rows, max(K, 10), 3, stream)
     assert eng.device_error() == 0
     nb = step_bytes(cfg, "bf16", rows)
     out["d1_4096"] = {"requests_per_s": rows / (ms / 1e3), "ms_per_step": ms, "bytes_per_step": nb,

@@ -19,6 +19,7 @@ LAYER_KINDS = {"xlstm": 0, "mamba2": 1, "retnet": 2, "hawk": 3}
 FLAG_NO_PDL = 1         # B2E_FLAG_NO_PDL
 FLAG_NO_PRIORITIES = 2  # B2E_FLAG_NO_PRIORITIES
 FLAG_NO_LATENCY_PATH = 4  # B2E_FLAG_NO_LATENCY_PATH
+FLAG_NO_PIPELINE = 8  # B2E_FLAG_NO_PIPELINE
 
 
 class B2ELibraryError(RuntimeError):
@@ -66,6 +67,8 @@ _SIGS = {
     "b2e_engine_submit": (C.c_int, [_P, _P, _P, _I32]),
     "b2e_engine_wait": (C.c_int, [_P, _P]),
     "b2e_engine_step_device": (C.c_int, [_P, _P, _P, _I32, _P, _P]),
+    "b2e_engine_submit_device": (C.c_int, [_P, _P, _P, _I32, _P, _P]),
+    "b2e_engine_join_device": (C.c_int, [_P, _P]),
     "b2e_engine_device_error": (C.c_int, [_P, _PI32]),
     "b2e_engine_reset_slots": (C.c_int, [_P, _P, _I32]),
     "b2e_engine_slot_bytes": (C.c_int, [_P, _PI64]),

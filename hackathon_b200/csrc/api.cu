@@ -82,6 +82,7 @@ EngineOptions to_opts(const b2e_engine_options* o) {
   e.pdl = !(o->flags & B2E_FLAG_NO_PDL);
   e.priorities = !(o->flags & B2E_FLAG_NO_PRIORITIES);
   e.latency = !(o->flags & B2E_FLAG_NO_LATENCY_PATH);
+  e.pipeline = !(o->flags & B2E_FLAG_NO_PIPELINE);
   return e;
 }
 
@@ -167,6 +168,15 @@ int b2e_engine_wait(b2e_engine* e, float* preds) {
 int b2e_engine_step_device(b2e_engine* e, const int32_t* d_slots, const float* d_features, int32_t n,
                            float* d_preds, void* stream) {
   return guard([&] { E(e).step_device(d_slots, d_features, n, d_preds, static_cast<cudaStream_t>(stream)); });
+}
+
+int b2e_engine_submit_device(b2e_engine* e, const int32_t* d_slots, const float* d_features, int32_t n,
+                             float* d_preds, void* stream) {
+  return guard([&] { E(e).submit_device(d_slots, d_features, n, d_preds, static_cast<cudaStream_t>(stream)); });
+}
+
+int b2e_engine_join_device(b2e_engine* e, void* stream) {
+  return guard([&] { E(e).join_device(static_cast<cudaStream_t>(stream)); });
 }
 
 int b2e_engine_device_error(b2e_engine* e, int32_t* flag) {

@@ -149,8 +149,6 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   ow_ = pack_.ptr<float>(o_ow_);
   upw_ = pack_.ptr(o_upw_);
   upb_ = pack_.ptr(o_upb_);
-  B2E_CUDA(cudaMalloc(&d_up_, size_t(o.max_batch) * 4 * P * dtype_size(lp)));
-  if (lp != kF32) B2E_CUDA(cudaMalloc(&d_feats_lp_, size_t(o.max_batch) * fpad_ * dtype_size(lp)));
   ob_ = pack_.ptr<float>(o_ob_);
 
   // ---- step I/O: kSets sets, so a host step's copies overlap the step before
@@ -172,6 +170,11 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
     B2E_CUDA(cudaEventCreateWithFlags(&st.in_ready, cudaEventDisableTiming));
     B2E_CUDA(cudaEventCreateWithFlags(&st.stepped, cudaEventDisableTiming));
     B2E_CUDA(cudaEventCreateWithFlags(&st.done, cudaEventDisableTiming));
+    B2E_CUDA(cudaEventCreateWithFlags(&st.head, cudaEventDisableTiming));
+    for (auto& ev : st.tower) B2E_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    // per set: a pipelined step's input projection runs while the step before still reads its own
+    B2E_CUDA(cudaMalloc(&st.d_up, size_t(o.max_batch) * 4 * P * dtype_size(lp)));
+    if (lp != kF32) B2E_CUDA(cudaMalloc(&st.d_feats_lp, size_t(o.max_batch) * fpad_ * dtype_size(lp)));
   }
   B2E_CUDA(cudaMalloc(&d_err_, 256));
   B2E_CUDA(cudaMemset(d_err_, 0, 256));
@@ -180,6 +183,7 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   B2E_CUDA(cudaStreamCreateWithFlags(&s0_, cudaStreamNonBlocking));
   B2E_CUDA(cudaStreamCreateWithFlags(&s_h2d_, cudaStreamNonBlocking));
   B2E_CUDA(cudaStreamCreateWithFlags(&s_d2h_, cudaStreamNonBlocking));
+  B2E_CUDA(cudaStreamCreateWithFlags(&s_head_, cudaStreamNonBlocking));
   B2E_CUDA(cudaEventCreateWithFlags(&fork_, cudaEventDisableTiming));
   B2E_CUDA(cudaEventCreateWithFlags(&last_step_, cudaEventDisableTiming));
   int prio_low = 0, prio_high = 0;
@@ -231,17 +235,21 @@ Engine::~Engine() {
     if (st.in_ready) cudaEventDestroy(st.in_ready);
     if (st.stepped) cudaEventDestroy(st.stepped);
     if (st.done) cudaEventDestroy(st.done);
+    if (st.head) cudaEventDestroy(st.head);
+    for (auto ev : st.tower)
+      if (ev) cudaEventDestroy(ev);
+    if (st.d_up) cudaFree(st.d_up);
+    if (st.d_feats_lp) cudaFree(st.d_feats_lp);
   }
   if (fork_) cudaEventDestroy(fork_);
   if (last_step_) cudaEventDestroy(last_step_);
   if (s0_) cudaStreamDestroy(s0_);
   if (s_h2d_) cudaStreamDestroy(s_h2d_);
   if (s_d2h_) cudaStreamDestroy(s_d2h_);
+  if (s_head_) cudaStreamDestroy(s_head_);
   if (d_err_) cudaFree(d_err_);
   if (d_rs_) cudaFree(d_rs_);
   if (h_rs_) cudaFreeHost(h_rs_);
-  if (d_up_) cudaFree(d_up_);
-  if (d_feats_lp_) cudaFree(d_feats_lp_);
 }
 
 int Engine::bucket(int n) const {
@@ -317,7 +325,7 @@ void Engine::tower_forward(const Tower& tw, Chain& ch, int idx, const StepCtx& c
   if (!fuse) output_proj_rows(c, ch.x, ow_, ob_, H, preds, 4, idx);  // shared output_proj (model/inference_model.py:142)
 }
 
-void Engine::enqueue(int rows, int b, cudaStream_t s) {
+void Engine::enqueue_head(int rows, int b, cudaStream_t s) {
   const IoSet& io = io_[b];
   const int L = lanes_for(rows);
   const int per = (rows + L - 1) / L;
@@ -336,14 +344,41 @@ void Engine::enqueue(int rows, int b, cudaStream_t s) {
   if (lp != kF32) {
     const int blocks = std::max(1, std::min(ceil_div(long(rows) * fpad_, 256 * 4), 148 * 4));
     if (lp == kBF16)
-      k_feats_lp<kBF16><<<blocks, 256, 0, s>>>(io.d_feats, F, d_feats_lp_, fpad_, io.d_n);
+      k_feats_lp<kBF16><<<blocks, 256, 0, s>>>(io.d_feats, F, io.d_feats_lp, fpad_, io.d_n);
     else
-      k_feats_lp<kF16><<<blocks, 256, 0, s>>>(io.d_feats, F, d_feats_lp_, fpad_, io.d_n);
+      k_feats_lp<kF16><<<blocks, 256, 0, s>>>(io.d_feats, F, io.d_feats_lp, fpad_, io.d_n);
     B2E_CUDA(cudaGetLastError());
-    linear(c0, d_feats_lp_, lp, fpad_, upw_, lp, upb_, 4 * P, fpad_, nullptr, 0, kActRelu, nullptr, 0, d_up_, 4 * P);
+    linear(c0, io.d_feats_lp, lp, fpad_, upw_, lp, upb_, 4 * P, fpad_, nullptr, 0, kActRelu, nullptr, 0, io.d_up, 4 * P);
   } else {
-    linear(c0, io.d_feats, kF32, F, upw_, kF32, upb_, 4 * P, F, static_cast<float*>(d_up_), 4 * P, kActRelu);
+    linear(c0, io.d_feats, kF32, F, upw_, kF32, upb_, 4 * P, F, static_cast<float*>(io.d_up), 4 * P, kActRelu);
   }
+}
+
+StepCtx Engine::chain_ctx(int t, cudaStream_t s, int rows, const int* n_dev, const int* slots) const {
+  StepCtx c;
+  c.s = s;
+  c.rows = rows;
+  c.n_dev = n_dev;
+  c.slots = slots;
+  c.lp = opt_.lp;
+  c.err = d_err_;
+  c.ln = ln_;
+  c.ln_bulk = ln_bulk_;
+  if (opt_.priorities && prio_hi_ != prio_lo_) {
+    // the xLSTM and Mamba2 towers' chains are the longest: their kernels
+    // take SM slots first
+    c.ln.set_prio = c.ln_bulk.set_prio = true;
+    c.ln.prio = c.ln_bulk.prio = t <= 1 ? prio_hi_ : prio_lo_;
+  }
+  return c;
+}
+
+void Engine::enqueue(int rows, int b, cudaStream_t s) {
+  const IoSet& io = io_[b];
+  const int L = lanes_for(rows);
+  const int per = (rows + L - 1) / L;
+  const int P = d_.P, lp = opt_.lp;
+  enqueue_head(rows, b, s);
   B2E_CUDA(cudaEventRecord(fork_, s));
   for (int l = 0; l < L; ++l) {
     for (int t = 0; t < 4; ++t) {
@@ -352,22 +387,8 @@ void Engine::enqueue(int rows, int b, cudaStream_t s) {
       if (!split && l > 0) continue;
       Chain& ch = chains_[size_t(l) * 4 + t];
       B2E_CUDA(cudaStreamWaitEvent(ch.s, fork_, 0));
-      StepCtx c;
-      c.s = ch.s;
-      c.rows = split ? per : rows;
-      c.n_dev = split ? io.d_nl + l : io.d_n;
-      c.slots = io.d_slots + size_t(l) * per;
-      c.lp = opt_.lp;
-      c.err = d_err_;
-      c.ln = ln_;
-      c.ln_bulk = ln_bulk_;
-      if (opt_.priorities && prio_hi_ != prio_lo_) {
-        // the xLSTM and Mamba2 towers' chains are the longest: their kernels
-        // take SM slots first
-        c.ln.set_prio = c.ln_bulk.set_prio = true;
-        c.ln.prio = c.ln_bulk.prio = t <= 1 ? prio_hi_ : prio_lo_;
-      }
-      const void* up = static_cast<const uint8_t*>(d_up_) + (size_t(l) * per * 4 * P + size_t(t) * P) * dtype_size(lp);
+      const StepCtx c = chain_ctx(t, ch.s, split ? per : rows, split ? io.d_nl + l : io.d_n, io.d_slots + size_t(l) * per);
+      const void* up = static_cast<const uint8_t*>(io.d_up) + (size_t(l) * per * 4 * P + size_t(t) * P) * dtype_size(lp);
       tower_forward(towers_[t], ch, t, c, up, 4 * P, io.d_preds + size_t(l) * per * 4);
       B2E_CUDA(cudaEventRecord(ch.done, ch.s));
     }
@@ -377,20 +398,19 @@ void Engine::enqueue(int rows, int b, cudaStream_t s) {
       if (l == 0 || ((opt_.lane_towers >> t) & 1)) B2E_CUDA(cudaStreamWaitEvent(s, chains_[size_t(l) * 4 + t].done, 0));
 }
 
-void Engine::launch(int n, int b, cudaStream_t s) {
-  const int rows = bucket(n);
+template <class F>
+void Engine::replay(long long key, cudaStream_t s, F&& enqueue_fn) {
   if (!opt_.graphs) {
-    enqueue(rows, b, s);
+    enqueue_fn(s);
     return;
   }
-  const long long key = (long long)rows * kSets + b;
   auto it = graphs_.find(key);
   if (it == graphs_.end()) {
     // Capture on a private stream so the caller's stream is never in capture mode.
     cudaGraph_t g = nullptr;
     B2E_CUDA(cudaStreamBeginCapture(s0_, cudaStreamCaptureModeThreadLocal));
     try {
-      enqueue(rows, b, s0_);
+      enqueue_fn(s0_);
     } catch (...) {
       cudaStreamEndCapture(s0_, &g);
       if (g) cudaGraphDestroy(g);
@@ -404,6 +424,38 @@ void Engine::launch(int n, int b, cudaStream_t s) {
     it = graphs_.emplace(key, ex).first;
   }
   B2E_CUDA(cudaGraphLaunch(it->second, s));
+}
+
+// Graph keys: (bucket, set, segment); segment 0 the whole step, 1 the input
+// projection of a pipelined step, 2-5 its towers.
+static long long graph_key(int rows, int b, int seg) { return ((long long)rows * 8 + b) * 8 + seg; }
+
+bool Engine::pipelined(int n) const { return opt_.pipeline && lanes_for(bucket(n)) == 1; }
+
+void Engine::launch_pipelined(int n, int b) {
+  const int rows = bucket(n);
+  IoSet& io = io_[b];
+  const int P = d_.P, lp = opt_.lp;
+  replay(graph_key(rows, b, 1), s_head_, [&](cudaStream_t s) { enqueue_head(rows, b, s); });
+  B2E_CUDA(cudaEventRecord(io.head, s_head_));
+  for (int t = 0; t < 4; ++t) {
+    Chain& ch = chains_[t];
+    // the chain's stream already holds this tower's previous step: the state
+    // rows it wrote are final before this step's kernels read them
+    B2E_CUDA(cudaStreamWaitEvent(ch.s, io.head, 0));
+    replay(graph_key(rows, b, 2 + t), ch.s, [&](cudaStream_t s) {
+      const StepCtx c = chain_ctx(t, s, rows, io.d_n, io.d_slots);
+      const void* up = static_cast<const uint8_t*>(io.d_up) + size_t(t) * P * dtype_size(lp);
+      tower_forward(towers_[t], ch, t, c, up, 4 * P, io.d_preds);
+    });
+    B2E_CUDA(cudaEventRecord(io.tower[t], ch.s));
+  }
+  for (int t = 0; t < 4; ++t) B2E_CUDA(cudaStreamWaitEvent(s0_, io.tower[t], 0));
+}
+
+void Engine::launch(int n, int b, cudaStream_t s) {
+  const int rows = bucket(n);
+  replay(graph_key(rows, b, 0), s, [&](cudaStream_t cs) { enqueue(rows, b, cs); });
 }
 
 void Engine::order_after_last_step(cudaStream_t s) {
@@ -484,6 +536,7 @@ void Engine::submit(const int* slots, const float* feats, int n) {
     B2E_CUDA(cudaEventRecord(io.stepped, s0_));
     B2E_CUDA(cudaEventRecord(last_step_, s0_));
     last_stream_ = s0_;
+    last_pipelined_ = false;
     B2E_CUDA(cudaEventRecord(io.done, s0_));
     io.used = true;
     io.host_n = n;
@@ -498,12 +551,20 @@ void Engine::submit(const int* slots, const float* feats, int n) {
   B2E_CUDA(cudaMemcpyAsync(io.d_slots, io.h_io + slots_off_, size_t(n) * 4, cudaMemcpyHostToDevice, s_h2d_));
   B2E_CUDA(cudaMemcpyAsync(io.d_feats, io.h_io + feats_off_, size_t(n) * F * 4, cudaMemcpyHostToDevice, s_h2d_));
   B2E_CUDA(cudaEventRecord(io.in_ready, s_h2d_));
-  order_after_last_step(s0_);
-  B2E_CUDA(cudaStreamWaitEvent(s0_, io.in_ready, 0));
-  launch(n, b, s0_);
+  if (pipelined(n)) {
+    // the set's previous step finished before this submit (io.done above)
+    B2E_CUDA(cudaStreamWaitEvent(s_head_, io.in_ready, 0));
+    if (!last_pipelined_) order_after_last_step(s_head_);
+    launch_pipelined(n, b);
+  } else {
+    order_after_last_step(s0_);
+    B2E_CUDA(cudaStreamWaitEvent(s0_, io.in_ready, 0));
+    launch(n, b, s0_);
+  }
   B2E_CUDA(cudaEventRecord(io.stepped, s0_));
   B2E_CUDA(cudaEventRecord(last_step_, s0_));
   last_stream_ = s0_;
+  last_pipelined_ = pipelined(n);
   // predictions out on their own stream: the next step's graph does not wait for them
   B2E_CUDA(cudaStreamWaitEvent(s_d2h_, io.stepped, 0));
   B2E_CUDA(cudaMemcpyAsync(io.h_io + preds_off_, io.d_preds, size_t(n) * 16, cudaMemcpyDeviceToHost, s_d2h_));
@@ -549,7 +610,48 @@ void Engine::step_device(const int* d_slots, const float* d_feats, int n, float*
   B2E_CUDA(cudaEventRecord(io.done, s));
   B2E_CUDA(cudaEventRecord(last_step_, s));
   last_stream_ = s;
+  last_pipelined_ = false;
   io.used = true;
+}
+
+void Engine::submit_device(const int* d_slots, const float* d_feats, int n, float* d_preds, cudaStream_t s) {
+  B2E_CHECK(host_fifo_.empty(), kErrInvalid, "a host step is in flight on this engine");
+  B2E_CHECK(n >= 1 && n <= opt_.max_batch, kErrCapacity, "batch outside 1..max_batch");
+  B2E_CHECK(d_slots && d_feats && d_preds, kErrInvalid, "null device buffer");
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  const int b = next_set_;
+  next_set_ = (next_set_ + 1) % kSets;
+  IoSet& io = io_[b];
+  const bool pipe = pipelined(n);
+  // inputs: after the caller's work on `s`; the set: after its previous step's
+  // predictions were copied out
+  B2E_CUDA(cudaEventRecord(io.in_ready, s));
+  B2E_CUDA(cudaStreamWaitEvent(s_head_, io.in_ready, 0));
+  if (io.used) B2E_CUDA(cudaStreamWaitEvent(s_head_, io.done, 0));
+  if (!pipe || !last_pipelined_) order_after_last_step(s_head_);
+  B2E_CUDA(cudaMemcpyAsync(io.d_slots, d_slots, size_t(n) * 4, cudaMemcpyDeviceToDevice, s_head_));
+  B2E_CUDA(cudaMemcpyAsync(io.d_feats, d_feats, size_t(n) * d_.F * 4, cudaMemcpyDeviceToDevice, s_head_));
+  k_validate<<<1, 256, 0, s_head_>>>(io.d_slots, n, opt_.capacity, io.d_n, d_err_);
+  B2E_CUDA(cudaGetLastError());
+  if (pipe) {
+    launch_pipelined(n, b);
+  } else {
+    B2E_CUDA(cudaEventRecord(io.head, s_head_));
+    B2E_CUDA(cudaStreamWaitEvent(s0_, io.head, 0));
+    launch(n, b, s0_);
+  }
+  B2E_CUDA(cudaMemcpyAsync(d_preds, io.d_preds, size_t(n) * 16, cudaMemcpyDeviceToDevice, s0_));
+  B2E_CUDA(cudaEventRecord(io.stepped, s0_));
+  B2E_CUDA(cudaEventRecord(io.done, s0_));
+  B2E_CUDA(cudaEventRecord(last_step_, s0_));
+  last_stream_ = s0_;
+  last_pipelined_ = pipe;
+  io.used = true;
+}
+
+void Engine::join_device(cudaStream_t s) {
+  B2E_CUDA(cudaSetDevice(opt_.device));
+  order_after_last_step(s);
 }
 
 int Engine::device_error() {

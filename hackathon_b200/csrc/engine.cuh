@@ -21,6 +21,11 @@ struct EngineOptions {
   bool pdl = true;         // programmatic dependent launch inside each tower's chain
   bool priorities = true;   // the xLSTM tower's chain at high launch priority, the others low
   bool latency = true;      // host steps of a few rows run as one kernel (latency.cuh)
+  // Steps submitted while earlier ones run (submit, submit_device) replay as five
+  // graphs - the shared input projection, then one per tower on the tower's own
+  // stream - so a tower's chain waits only for the same tower's previous step:
+  // the towers of consecutive steps overlap instead of meeting at every step's end.
+  bool pipeline = true;
 };
 
 class Engine {
@@ -42,6 +47,13 @@ class Engine {
   // Invalid slots zero the live-row count on the device (no row is stepped) and
   // raise the sticky flag read by device_error().
   void step_device(const int* d_slots, const float* d_feats, int n, float* d_preds, cudaStream_t stream);
+  // Device-buffer step that does not order its end onto `stream`: the step reads
+  // d_slots/d_feats after the work enqueued on `stream` so far and writes
+  // d_preds at its end; join_device(stream) makes `stream` wait for every step
+  // submitted before it. Between the two, the caller leaves the three buffers
+  // alone. Consecutive submits overlap (options.pipeline).
+  void submit_device(const int* d_slots, const float* d_feats, int n, float* d_preds, cudaStream_t stream);
+  void join_device(cudaStream_t stream);
   int device_error();  // synchronises; returns and clears the flag
   // wait() throws kErrDevice while the flag is set (copied back with each host
   // step's predictions), so a timed-out kernel never passes as an answer.
@@ -96,6 +108,10 @@ class Engine {
     cudaEvent_t in_ready = nullptr;  // inputs copied in
     cudaEvent_t stepped = nullptr;   // the step's graph finished
     cudaEvent_t done = nullptr;      // predictions copied out: the set is free
+    cudaEvent_t head = nullptr;      // the step's input projection finished
+    cudaEvent_t tower[4] = {};       // each tower's chain finished (pipelined steps)
+    void* d_up = nullptr;            // input_up output of the step [rows][4P], CastLinear type
+    void* d_feats_lp = nullptr;      // the features in the CastLinear type [rows][fpad]
     bool used = false;
     int host_n = -1;                 // rows of the host step in flight on this set
   };
@@ -103,6 +119,14 @@ class Engine {
   int bucket(int n) const;
   void launch(int n, int b, cudaStream_t s);   // graph replay or eager enqueue, I/O set b
   void enqueue(int rows, int b, cudaStream_t s);
+  // pipelined step over set b (inputs in place, ordered on s_head_): the input
+  // projection on s_head_, each tower on its chain's stream, joined on s0_
+  bool pipelined(int n) const;
+  void launch_pipelined(int n, int b);
+  void enqueue_head(int rows, int b, cudaStream_t s);
+  StepCtx chain_ctx(int t, cudaStream_t s, int rows, const int* n_dev, const int* slots) const;
+  template <class F>
+  void replay(long long key, cudaStream_t s, F&& enqueue_fn);  // capture once per key, then launch
   void order_after_last_step(cudaStream_t s);  // `s` waits for the last step, wherever it ran
   void drain();
   void tower_forward(const Tower& t, Chain& ch, int idx, const StepCtx& c, const void* up, int ld_up, float* preds);
@@ -122,8 +146,6 @@ class Engine {
   int fpad_ = 0;
   size_t o_upw_ = 0, o_upb_ = 0;
   const void *upw_ = nullptr, *upb_ = nullptr;
-  void* d_feats_lp_ = nullptr;
-  void* d_up_ = nullptr;
   LaunchCfg ln_, ln_bulk_;     // chain kernels / state-streaming kernels
   int prio_hi_ = 0, prio_lo_ = 0;
   size_t o_ow_ = 0, o_ob_ = 0;
@@ -140,10 +162,12 @@ class Engine {
   cudaStream_t s0_ = nullptr;     // host steps
   cudaStream_t s_h2d_ = nullptr;  // host steps' input copies
   cudaStream_t s_d2h_ = nullptr;  // host steps' prediction copies
+  cudaStream_t s_head_ = nullptr; // pipelined steps' input checks and input projection
+  bool last_pipelined_ = false;   // the last step ran pipelined (its towers are ordered by their streams)
   cudaEvent_t fork_ = nullptr;
   cudaEvent_t last_step_ = nullptr;     // recorded after every step
   cudaStream_t last_stream_ = nullptr;  // where it was recorded (null: no step yet)
-  std::unordered_map<long long, cudaGraphExec_t> graphs_;  // (bucket, set)
+  std::unordered_map<long long, cudaGraphExec_t> graphs_;  // (bucket, set, segment)
   std::vector<uint8_t> seen_;  // duplicate-slot check
   std::unique_ptr<LatencyPath> lat_;  // one-kernel steps of a few rows
 };

@@ -3,7 +3,10 @@
 // Two kernels:
 //  * gemm_tiled: 64x64 output tile per CTA, 16-deep K slices through shared
 //    memory with a register prefetch of the next slice, 4x4 outputs per thread.
-//    Exact f32 FMA arithmetic, which is what the fp32 path must match.
+//    f32 FMA arithmetic; each 16-deep slice is summed into a fresh partial that
+//    joins the running sum through Kahan's compensated addition, so the error of
+//    a long dot product (K = 2048 at the default dims) grows like that of 16
+//    terms rather than of K.
 //  * gemm_skinny: M <= 16 rows. Weight-bound: each warp streams whole W rows with
 //    128-bit loads and keeps one accumulator per live row; this is the path a
 //    single request takes, where the step is a chain of GEMVs over the weights.
@@ -89,11 +92,11 @@ __global__ void __launch_bounds__(TPB) gemm_tiled(const __grid_constant__ GemmPa
   const int tx = tid & 15, ty = tid >> 4;       // compute: cols 4tx.., rows ty+16i
   const bool round_a = (AT == kF32 && WT != kF32);
 
-  float acc[4][4];
+  float acc[4][4], cmp[4][4];  // running sums and their Kahan compensations
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = cmp[i][j] = 0.f;
 
   auto fetch = [&](int k0, float4& a, float4& w) {
     a = load_row4<AT>(g.A, p.lda, m0 + lr, M, k0 + lk, p.K, vec_a);
@@ -115,6 +118,11 @@ __global__ void __launch_bounds__(TPB) gemm_tiled(const __grid_constant__ GemmPa
   for (int k0 = 0; k0 < p.K; k0 += BK) {
     const bool more = k0 + BK < p.K;
     if (more) fetch(k0 + BK, ra, rw);
+    float part[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) part[i][j] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
       float a[4];
@@ -123,12 +131,21 @@ __global__ void __launch_bounds__(TPB) gemm_tiled(const __grid_constant__ GemmPa
       const float4 w = *reinterpret_cast<const float4*>(&Ws[buf][kk][tx * 4]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        acc[i][0] = fmaf(a[i], w.x, acc[i][0]);
-        acc[i][1] = fmaf(a[i], w.y, acc[i][1]);
-        acc[i][2] = fmaf(a[i], w.z, acc[i][2]);
-        acc[i][3] = fmaf(a[i], w.w, acc[i][3]);
+        part[i][0] = fmaf(a[i], w.x, part[i][0]);
+        part[i][1] = fmaf(a[i], w.y, part[i][1]);
+        part[i][2] = fmaf(a[i], w.z, part[i][2]);
+        part[i][3] = fmaf(a[i], w.w, part[i][3]);
       }
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {  // Kahan: acc + part, the lost low part kept in cmp
+        const float y = part[i][j] - cmp[i][j];
+        const float t = acc[i][j] + y;
+        cmp[i][j] = (t - acc[i][j]) - y;
+        acc[i][j] = t;
+      }
     if (more) {
       stash(buf ^ 1, ra, rw);
       __syncthreads();

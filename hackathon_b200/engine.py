@@ -141,6 +141,24 @@ class EnsembleEngine:
                                                      C.c_void_p(feats_t.data_ptr()), int(n),
                                                      C.c_void_p(preds_t.data_ptr()), C.c_void_p(s.cuda_stream)))
 
+    def submit_device(self, slots_t, feats_t, preds_t, n: int, stream=None):
+        """Device-buffer step that overlaps the steps around it: it reads its inputs
+        after the work on `stream` so far and fills preds_t when it ends, which only
+        join_device(stream) waits for. Keep the three tensors unchanged until then."""
+        import torch
+
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        _lib.check(_lib.lib().b2e_engine_submit_device(self._h, C.c_void_p(slots_t.data_ptr()),
+                                                       C.c_void_p(feats_t.data_ptr()), int(n),
+                                                       C.c_void_p(preds_t.data_ptr()), C.c_void_p(s.cuda_stream)))
+
+    def join_device(self, stream=None):
+        """`stream` waits for every step submit_device started."""
+        import torch
+
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        _lib.check(_lib.lib().b2e_engine_join_device(self._h, C.c_void_p(s.cuda_stream)))
+
     def device_error(self) -> int:
         f = C.c_int32()
         _lib.check(_lib.lib().b2e_engine_device_error(self._h, C.byref(f)))

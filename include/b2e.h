@@ -66,6 +66,8 @@ extern "C" {
 #define B2E_FLAG_NO_PDL 1        /* launch chain kernels without programmatic dependent launch */
 #define B2E_FLAG_NO_PRIORITIES 2 /* launch every chain at the same priority (default: the xLSTM tower's, the longest, first) */
 #define B2E_FLAG_NO_LATENCY_PATH 4 /* run every host step through the batch graphs, never the one-kernel latency path */
+#define B2E_FLAG_NO_PIPELINE 8 /* run each step as one graph whose four towers all finish before the next step starts
+                                  (default: a tower's chain waits only for the same tower's previous step) */
 
 #define B2E_DTYPE_F32 0
 #define B2E_DTYPE_BF16 1
@@ -133,6 +135,18 @@ B2E_API int b2e_engine_wait(b2e_engine* e, float* preds);
  * Slots outside the table step no row and set a flag read by b2e_engine_device_error. */
 B2E_API int b2e_engine_step_device(b2e_engine* e, const int32_t* d_slots, const float* d_features, int32_t n,
                            float* d_preds, void* stream);
+/* Device-buffer steps that overlap: each submit reads d_slots / d_features after
+ * the work enqueued on `stream` so far and writes d_preds when its step ends, but
+ * does not make `stream` wait for that end; b2e_engine_join_device(e, stream)
+ * does, for every step submitted before it. Until the join the caller leaves
+ * the step's three buffers alone. Consecutive steps are ordered per tower (a
+ * tower's chain waits for the same tower's previous step), so one step's towers
+ * run beside the next step's; results are those of the steps run one by one.
+ * Refused while a host step (b2e_engine_submit) is in flight. No counterpart in
+ * the reference, which steps one round at a time (example_model.py:848-883). */
+B2E_API int b2e_engine_submit_device(b2e_engine* e, const int32_t* d_slots, const float* d_features, int32_t n,
+                             float* d_preds, void* stream);
+B2E_API int b2e_engine_join_device(b2e_engine* e, void* stream);
 B2E_API int b2e_engine_device_error(b2e_engine* e, int32_t* flag);
 B2E_API int b2e_engine_reset_slots(b2e_engine* e, const int32_t* slots, int32_t n);
 /* One slot's whole state, every leaf in iter_state_tensors order

@@ -1,7 +1,13 @@
-"""Two host steps in flight on one engine (b2e_engine_submit twice, then
-b2e_engine_wait): the second step's input copies overlap the first step, and the
-results equal one-step-at-a-time stepping bit for bit, also when consecutive
-steps share symbols (the state dependency that orders them)."""
+"""Pipelined steps (a tower's chain waits only for the same tower's previous step,
+so consecutive steps overlap) against the same steps run one at a time.
+
+The pipelined engine and an engine with B2E_FLAG_NO_PIPELINE run the same kernels
+on the same inputs, so predictions and state must agree bit for bit. The steps
+share most of their slots - a symbol stepped by two consecutive steps is the case
+the per-tower ordering must get right - change batch bucket, and (host path) put
+one-kernel latency steps between pipelined ones. Dims: the benchmark's D2 with
+bf16 weights, and the small test model with fp32 weights.
+"""
 
 import numpy as np
 import pytest
@@ -12,65 +18,99 @@ from hackathon_b200 import weights as Wt
 from hackathon_b200.engine import EnsembleEngine
 
 pytestmark = pytest.mark.gpu
-CFG = C.ModelConfig(hidden_size=64, proj_size=128, tower_depth=2, num_heads=4, num_features=79)
-CAP = 400
+
+CASES = {"d2-bf16": (C.D2, "bf16", 1024), "small-fp32": (C.SMALL, "fp32", 256)}
 
 
-def _workload(steps, seed=6):
+def _plan(rows, seed, with_small):
+    """Step sizes and slots: full, ragged and smaller buckets over a pool only
+    1.5x the batch, so consecutive steps share most of their slots."""
     rng = np.random.default_rng(seed)
-    out = []
-    for k in range(steps):
-        n = int(rng.integers(200, 320)) if k % 3 else int(rng.integers(1, 40))
-        slots = rng.choice(330 if k % 2 else CAP, n, replace=False).astype(np.int32)  # symbols recur
-        out.append((slots, rng.standard_normal((n, CFG.num_features), dtype=np.float32)))
-    return out
+    pool = rows + rows // 2
+    sizes = [rows, rows, rows - 24, rows // 2 - 7, rows, 3 if with_small else rows // 4, rows, rows - 1, 2 if with_small else 5, rows]
+    return pool, [rng.permutation(pool)[:n].astype(np.int32) for n in sizes]
 
 
-def test_two_host_steps_in_flight_equal_sequential_steps():
-    sd = Wt.generate_model(CFG, seed=3)
-    a = EnsembleEngine(CFG, sd, capacity=CAP, max_batch=512)
-    b = EnsembleEngine(CFG, sd, capacity=CAP, max_batch=512)
-    work = _workload(6, seed=8)
-    want = [a.step(s, f) for s, f in work]
+def _engines(cfg, lp, rows, pool):
+    sd = Wt.generate_model(cfg, seed=0)
+    kw = dict(device=0, linear_dtype=lp, capacity=pool, max_batch=rows)
+    return EnsembleEngine(cfg, sd, **kw), EnsembleEngine(cfg, sd, flags=_lib.FLAG_NO_PIPELINE, **kw)
+
+
+def _state(eng, slots):
+    return [np.concatenate([np.asarray(leaf).reshape(-1) for leaf in eng.read_slot(int(s))]) for s in slots]
+
+
+def _same_state(a, b, pool, rng):
+    check = rng.choice(pool, 24, replace=False)
+    for s, x, y in zip(check, _state(a, check), _state(b, check)):
+        assert np.array_equal(x.view(np.uint8), y.view(np.uint8)), f"slot {s}: state differs"
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_host_steps_two_in_flight_match_one_by_one(case):
+    cfg, lp, rows = CASES[case]
+    pool, plan = _plan(rows, 11, with_small=True)
+    pipe, ref = _engines(cfg, lp, rows, pool)
+    rng = np.random.default_rng(5)
+    feats = [rng.standard_normal((len(s), cfg.num_features), dtype=np.float32) for s in plan]
+    want = [ref.step(s, f) for s, f in zip(plan, feats)]
     got = []
-    b.submit(*work[0])
-    for k in range(1, len(work)):
-        b.submit(*work[k])
-        if k == 1:
-            with pytest.raises(_lib.B2EError):
-                b.submit(*work[0])  # a third step in flight is refused
-        got.append(b.wait())
-    got.append(b.wait())
-    for k, (x, y) in enumerate(zip(want, got)):
-        assert np.array_equal(x.view(np.uint32), y.view(np.uint32)), f"step {k}"
-    with pytest.raises(_lib.B2EError):
-        b.wait()  # nothing in flight
-    a.close()
-    b.close()
+    pipe.submit(plan[0], feats[0])
+    for s, f in zip(plan[1:], feats[1:]):
+        pipe.submit(s, f)  # two steps in flight: this one's towers start beside the last one's
+        got.append(pipe.wait())
+    got.append(pipe.wait())
+    for i, (g, w) in enumerate(zip(got, want)):
+        assert np.array_equal(g, w), f"step {i} ({len(plan[i])} rows): predictions differ"
+    assert pipe.device_error() == 0 and ref.device_error() == 0
+    _same_state(pipe, ref, pool, rng)
+    pipe.close()
+    ref.close()
 
 
-@pytest.mark.parametrize("lanes", [1, 2])
-def test_device_and_host_steps_interleave_in_step_order(lanes):
-    """Device-buffer steps (on a torch stream) between host steps: each step sees
-    the state the one before it left, whichever path either took."""
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_device_submits_match_step_device(case):
     import torch
 
-    dev = torch.device("cuda", 0)
-    sd = Wt.generate_model(CFG, seed=3)
-    a = EnsembleEngine(CFG, sd, capacity=CAP, max_batch=512, lanes=lanes)
-    b = EnsembleEngine(CFG, sd, capacity=CAP, max_batch=512, lanes=lanes)
-    work = _workload(8, seed=9)
-    want = [a.step(s, f) for s, f in work]
-    got = []
-    for k, (s, f) in enumerate(work):
-        if k % 3 == 1:
-            p = torch.empty(len(s), 4, device=dev)
-            b.step_device(torch.from_numpy(s).to(dev), torch.from_numpy(f).to(dev), p, len(s))
-            got.append(p.cpu().numpy())
-        else:
-            b.submit(s, f)
-            got.append(b.wait())
-    for k, (x, y) in enumerate(zip(want, got)):
-        assert np.array_equal(x.view(np.uint32), y.view(np.uint32)), f"step {k}"
-    a.close()
-    b.close()
+    cfg, lp, rows = CASES[case]
+    pool, plan = _plan(rows, 12, with_small=False)
+    pipe, ref = _engines(cfg, lp, rows, pool)
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(6)
+    slots = [torch.from_numpy(s).to(dev) for s in plan]
+    feats = [torch.from_numpy(rng.standard_normal((len(s), cfg.num_features), dtype=np.float32)).to(dev) for s in plan]
+    out_p = [torch.full((len(s), 4), float("nan"), device=dev) for s in plan]
+    out_r = [torch.full((len(s), 4), float("nan"), device=dev) for s in plan]
+    st = torch.cuda.current_stream(dev)
+    for s, f, o in zip(slots, feats, out_p):
+        pipe.submit_device(s, f, o, len(s), stream=st)
+    pipe.join_device(stream=st)
+    for s, f, o in zip(slots, feats, out_r):
+        ref.step_device(s, f, o, len(s), stream=st)
+    torch.cuda.synchronize()
+    for i, (g, w) in enumerate(zip(out_p, out_r)):
+        assert torch.equal(g, w), f"step {i}: predictions differ"
+    assert pipe.device_error() == 0 and ref.device_error() == 0
+    _same_state(pipe, ref, pool, rng)
+    pipe.close()
+    ref.close()
+
+
+def test_device_submit_refuses_bad_slots_on_the_device():
+    import torch
+
+    cfg = C.SMALL
+    sd = Wt.generate_model(cfg, seed=0)
+    eng = EnsembleEngine(cfg, sd, capacity=16, max_batch=8)
+    dev = torch.device("cuda:0")
+    before = eng.read_slot(3)
+    slots = torch.tensor([3, 99], dtype=torch.int32, device=dev)  # 99 is outside the table
+    feats = torch.ones(2, cfg.num_features, device=dev)
+    preds = torch.empty(2, 4, device=dev)
+    eng.submit_device(slots, feats, preds, 2)
+    eng.join_device()
+    assert eng.device_error() == 1
+    after = eng.read_slot(3)
+    assert all(np.array_equal(a, b) for a, b in zip(before, after)), "a refused step changed state"
+    eng.close()
