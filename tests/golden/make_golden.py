@@ -24,8 +24,15 @@ Cases
              round-robin, one request per step (about 30 min on 8 cores)
   micro      BASELINE configs 2 and 3: the Mamba2, RetNet and xLSTM layers at
              their stated dims and fills, float32 and float64
+  d0batch    BASELINE config 4: default dims, 256 symbols per step - its first 16
+             rows, fp32 weights and the reference's bf16 CastLinear, 100 steps,
+             and the first 4 rows in float64 (the arbiter)
   d0arbiter  the first 320 requests of d0stream through the reference model in
              float64 and in float32 (the arbiter of the fp32 D0 tolerance)
+  d0emu      config 4's first 4 rows through the oracle's exact CastLinear bf16
+             emulation (oracle/model.py, not the reference): a second correct bf16
+             implementation, whose distance from the reference's bf16 run measures
+             how far two such implementations drift apart over 100 steps
 """
 
 from __future__ import annotations
@@ -273,6 +280,88 @@ def case_d0stream(mods, n_requests):
           preds=preds, **summ)
 
 
+def case_d0batch(mods, steps):
+    """BASELINE config 4 (default dims, 256 symbols, one request each per step) on
+    its first D0_BATCH_ROWS rows - rows are independent, and the reference's step
+    over all 256 needs more host memory than this machine has: the reference in
+    float32 with fp32 weights and with its own convert_linears to bf16, `steps`
+    steps from zero state; predictions per step and per-leaf state summaries of
+    the first row at the end."""
+    cfg = C.D0
+    sd = Wt.generate_model(cfg, seed=0)
+    rows = streams.D0_BATCH_ROWS
+    out = {}
+    for lp in (None, "bf16"):
+        m = _model(mods, cfg, sd, lp)
+        state = m.init_state(rows, torch.device("cpu"))
+        preds = np.zeros((steps, rows, 4), np.float32)
+        t0 = time.time()
+        with torch.inference_mode():
+            for s in range(steps):
+                x = streams.d0_batch_features(s)[:rows]
+                p, state = m(torch.from_numpy(x), state)
+                preds[s] = p.float().numpy()
+                if s % 10 == 0:
+                    print(f"d0batch {lp or 'fp32'} {s}/{steps} {time.time() - t0:.0f} s", flush=True)
+        tag = lp or "fp32"
+        out[f"{tag}_preds"] = preds
+        for li, leaf in enumerate(_leaves(state)):
+            out[f"{tag}_row0_leaf{li}"] = streams.leaf_summary(leaf[0].float().numpy() if leaf.is_floating_point()
+                                                               else leaf[0].numpy())
+        del m, state
+    # the float64 arbiter on the first D0_BATCH_ARBITER rows (weights and state in double)
+    m = _model(mods, cfg, sd).to(torch.float64)
+    ra = streams.D0_BATCH_ARBITER
+    state = _cast_state(m.init_state(ra, torch.device("cpu")), torch.float64)
+    preds = np.zeros((steps, ra, 4), np.float64)
+    t0 = time.time()
+    with torch.inference_mode():
+        for s in range(steps):
+            x = torch.from_numpy(streams.d0_batch_features(s)[:ra]).to(torch.float64)
+            p, state = m(x, state)
+            preds[s] = p.numpy()
+            if s % 10 == 0:
+                print(f"d0batch f64 {s}/{steps} {time.time() - t0:.0f} s", flush=True)
+    out["f64_preds"] = preds
+    del m, state
+    _save("d0batch", {"steps": steps, "rows": rows, "arbiter_rows": ra, "weight_seed": 0}, **out)
+
+
+def case_d0emu(steps):
+    """The oracle's bf16 CastLinear emulation (input and weights rounded to bf16,
+    float32 accumulation, one rounding of the sum) on config 4's arbiter rows."""
+    from oracle import model as O
+
+    cfg = C.D0
+    sd = Wt.generate_model(cfg, seed=0)
+    ra = streams.D0_BATCH_ARBITER
+    # the oracle rounds a weight to bf16 on every call; the weight matrices (the
+    # only arrays of a million elements or more here) are rounded once instead
+    lowp, memo = O.lowp, {}
+
+    def lowp_once(a, lp):
+        if a.size < (1 << 20):
+            return lowp(a, lp)
+        key = (id(a), lp)
+        if key not in memo:
+            memo[key] = lowp(a, lp)
+        return memo[key]
+
+    O.lowp = lowp_once
+    orc = O.Oracle(cfg, sd, lp="bf16")
+    st = O.init_state(cfg, ra)
+    preds = np.zeros((steps, ra, 4), np.float32)
+    t0 = time.time()
+    for s in range(steps):
+        p, st = orc.step(streams.d0_batch_features(s)[:ra], st)
+        preds[s] = p
+        if s % 10 == 0:
+            print(f"d0emu {s}/{steps} {time.time() - t0:.0f} s", flush=True)
+    O.lowp = lowp
+    _save("d0batch_emu", {"steps": steps, "rows": ra, "weight_seed": 0,
+                          "source": "oracle/model.py Oracle(lp='bf16'), not the reference"}, emu_preds=preds)
+
+
 def case_d0arbiter(mods, n_requests):
     """The first n_requests of BASELINE config 1 through the reference's model in
     float64 (same seeded weights, module and state in double) and again in
@@ -354,6 +443,7 @@ def main():
     ap.add_argument("cases", nargs="+")
     ap.add_argument("--d0-requests", type=int, default=10_000)
     ap.add_argument("--arbiter-requests", type=int, default=320)
+    ap.add_argument("--d0batch-steps", type=int, default=100)
     a = ap.parse_args()
     mods = _import_reference(a.ref)
     for c in a.cases:
@@ -372,6 +462,10 @@ def main():
             case_d0stream(mods, a.d0_requests)
         elif c == "micro":
             case_micro(mods)
+        elif c == "d0batch":
+            case_d0batch(mods, a.d0batch_steps)
+        elif c == "d0emu":
+            case_d0emu(a.d0batch_steps)
         elif c == "d0arbiter":
             case_d0arbiter(mods, a.arbiter_requests)
         else:

@@ -154,3 +154,14 @@ def micro_inputs(kind: str, steps: int = MICRO_STEPS, batch: int = MICRO_BATCH, 
 
     h = MICRO_CONFIGS[kind].hidden_size
     return _rng(seed).standard_normal((steps, batch, h), dtype=F32)
+
+
+# default dims, 256 symbols, one N(0,1) request each per step
+D0_BATCH = 256
+D0_BATCH_ROWS = 16  # rows the fixture follows (rows are independent)
+D0_BATCH_ARBITER = 4  # of those, rows also run in float64
+
+
+def d0_batch_features(step: int) -> np.ndarray:
+    """Config 4's features of one step: 256 x 79 N(0,1) float32, seed (4, step)."""
+    return np.random.default_rng([4, step]).standard_normal((D0_BATCH, 79), dtype=F32)

@@ -167,3 +167,23 @@ def test_micro_fills_are_the_stated_ones():
     np.testing.assert_allclose(sd["decay"], 1.0 - 2.0 ** (-5.0 - np.arange(4)), rtol=0, atol=1e-7)
     cfg, _ = Wt.micro_layer("xlstm")
     assert 2 * cfg.hidden_size // cfg.num_heads == 64
+
+
+def test_config4_fixtures_agree_with_each_other():
+    """BASELINE config 4's fixtures (make_golden.py d0batch, d0emu): the
+    reference's float64 run is within 1e-3 (normwise) of its float32 run per
+    tower, and the oracle's exact bf16 emulation is closer to the reference's bf16
+    run than bf16 weights move the answer (on the same rows and steps)."""
+    g, meta = load_golden("d0batch")
+    e, em = load_golden("d0batch_emu")
+    ra, steps = meta["arbiter_rows"], meta["steps"]
+    assert em["rows"] == ra and em["steps"] == steps
+    assert g["fp32_preds"].shape == g["bf16_preds"].shape == (steps, meta["rows"], 4)
+    assert g["f64_preds"].shape == e["emu_preds"].shape == (steps, ra, 4)
+    r32 = g["fp32_preds"][:, :ra].astype(np.float64)
+    rbf = g["bf16_preds"][:, :ra].astype(np.float64)
+    f64 = g["f64_preds"].astype(np.float64)
+    emu = e["emu_preds"].astype(np.float64)
+    for c in range(4):
+        assert np.linalg.norm(r32[..., c] - f64[..., c]) <= 1e-3 * np.linalg.norm(f64[..., c]), c
+        assert np.mean((emu[..., c] - rbf[..., c]) ** 2) < np.mean((rbf[..., c] - r32[..., c]) ** 2), c
