@@ -6,6 +6,11 @@ Each csrc/*.cu compiles to an object under hackathon_b200/_build/ (in parallel),
 then they link into hackathon_b200/lib/libb2e.so. An object is rebuilt when its
 source or any header is newer. The library links the CUDA runtime statically, so
 it loads without a toolkit on the library path.
+
+A second library, hackathon_b200/lib/libb2e_trace.so, is the same objects with
+latency.cu compiled under B2E_LAT_TRACE: the one-kernel latency path stamps
+each stage with %globaltimer (python -m hackathon_b200.profiling latency-trace).
+The product loads libb2e.so; only that profiling command loads the trace build.
 """
 
 from __future__ import annotations
@@ -23,6 +28,7 @@ REPO = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "lib" / "libb2e.so"
+TRACE_LIB = PKG / "lib" / "libb2e_trace.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
@@ -65,16 +71,32 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
                 print(r.stderr, file=sys.stderr)
         return obj
 
+    def compile_trace():
+        src, obj = CSRC / "latency.cu", BUILD / "latency_trace.o"
+        if force or _stale(src, obj, newest):
+            cmd = [cc, *ARCH, *NVCC_FLAGS, "-DB2E_LAT_TRACE", "-c", str(src), "-o", str(obj)]
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"nvcc failed on {src.name} (trace):\n{r.stdout}\n{r.stderr}")
+        return obj
+
     with ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
+        trace_obj = ex.submit(compile_trace)
         objs = list(ex.map(compile_one, srcs))
-    if force or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
-        tmp = LIB.with_suffix(".so.tmp")
+        trace_obj = trace_obj.result()
+    _link(cc, LIB, objs, force)
+    _link(cc, TRACE_LIB, [o for o in objs if o.stem != "latency"] + [trace_obj], force)
+    return LIB
+
+
+def _link(cc: str, lib: Path, objs, force: bool) -> None:
+    if force or not lib.exists() or any(o.stat().st_mtime > lib.stat().st_mtime for o in objs):
+        tmp = lib.with_suffix(".so.tmp")
         cmd = [cc, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-        os.replace(tmp, LIB)
-    return LIB
+        os.replace(tmp, lib)
 
 
 def main():

@@ -51,6 +51,18 @@ constexpr float kF32Eps = 1.1920928955078125e-07f;  // nn.RMSNorm(eps=None) in f
 
 // ----------------------------------------------------------- primitives
 
+#ifdef B2E_LAT_TRACE
+// Profiling build only (libb2e_trace.so): %globaltimer stamps around each stage
+// of cluster rank 0's thread 0 per tower, read by b2e_lat_trace_read.
+constexpr int kTraceStages = 512, kTraceFields = 8;
+__device__ unsigned long long g_lat_trace[4][kTraceStages][kTraceFields];
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#endif
+
 __device__ __forceinline__ void cp16(void* dst, const void* src) {
   const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
@@ -1392,16 +1404,39 @@ __device__ __noinline__ void tower_main(const LatModel& M, const LatIO& io, uint
   tw.prefetch(0, buf[0]);
   cp_commit();
   cluster_arrive();
+#ifdef B2E_LAT_TRACE
+  const bool tr = rank == 0 && threadIdx.x == 0;
+  unsigned long long ts[kTraceFields] = {};
+#define B2E_STAMP(i) \
+  if (tr) ts[i] = gtime()
+#else
+#define B2E_STAMP(i)
+#endif
   for (int s = 0; s < ns; ++s) {
-    if (s + 1 < ns) tw.prefetch(s + 1, buf[(s + 1) & 1]);
+    B2E_STAMP(0);
+    uint32_t nb = 0;
+    if (s + 1 < ns) nb = tw.prefetch(s + 1, buf[(s + 1) & 1]);
+    (void)nb;
     cp_commit();
+    B2E_STAMP(1);
     cluster_wait();  // every CTA's outputs of stage s-1 are in this CTA's shared memory
+    B2E_STAMP(2);
     cp_wait_prev();  // this CTA's loads for stage s have landed
     __syncthreads();
+    B2E_STAMP(3);
     tw.run(s, buf[s & 1]);
     __syncthreads();
+    B2E_STAMP(4);
     cluster_arrive();
+    B2E_STAMP(5);
+#ifdef B2E_LAT_TRACE
+    if (tr && s < kTraceStages) {
+      ts[6] = nb;  // bytes of stage s+1's copies
+      for (int f = 0; f < kTraceFields; ++f) g_lat_trace[KIND][s][f] = ts[f];
+    }
+#endif
   }
+#undef B2E_STAMP
   cluster_wait();
   cp_wait_all();
   // output_proj of this tower's column (model/inference_model.py:142), f32
@@ -1622,3 +1657,12 @@ void LatencyPath::launch(const LatIO& io, cudaStream_t s) const {
 }
 
 }  // namespace b2e
+
+#ifdef B2E_LAT_TRACE
+// Profiling build only: the last step's stage stamps, [4 towers][512 stages][8]
+// u64 (prefetch start, issued, cluster barrier passed, copies landed, run done,
+// arrived, next stage's bytes, 0); returns a cudaError_t.
+extern "C" __attribute__((visibility("default"))) int b2e_lat_trace_read(void* host) {
+  return int(cudaMemcpyFromSymbol(host, b2e::g_lat_trace, sizeof(b2e::g_lat_trace)));
+}
+#endif

@@ -8,6 +8,10 @@
         the whole ensemble step on device buffers (its GEMMs, for ncu -k)
     python -m hackathon_b200.profiling latency --preset D2 --reps 8
         single-request steps on the one-kernel latency path (for ncu -k)
+    python -m hackathon_b200.profiling latency-trace --preset D2
+        the same steps through the trace build (lib/libb2e_trace.so): per tower
+        and stage kind, the time a stage spends issuing the next stage's copies,
+        waiting at the cluster barrier and for its copies, computing, arriving
     python -m hackathon_b200.profiling launches <launch list csv>
         per-kernel launches, total time and share of an ncu launch list
     python -m hackathon_b200.profiling metrics <raw csv from ncu -i ... --page raw --csv>
@@ -184,6 +188,57 @@ def latency(preset: str, reps: int, dtype: str) -> None:
     eng.close()
 
 
+def latency_trace(preset: str, reps: int, dtype: str) -> None:
+    """Per-stage %globaltimer stamps of cluster rank 0 (thread 0) of each tower on
+    the last of `reps` single-request steps, averaged per stage kind: each tower
+    starts with input_up and input_down, then per block its layer's stages and the
+    MLP's two (xLSTM six per block, the others five)."""
+    import ctypes
+    import os
+
+    import numpy as np
+
+    from . import build as B
+
+    if not B.TRACE_LIB.exists():
+        raise SystemExit(f"{B.TRACE_LIB} is missing: python -m hackathon_b200.build")
+    os.environ["B2E_LIB"] = str(B.TRACE_LIB)
+    from . import _lib
+    from . import config as C
+    from . import weights as W
+    from .engine import EnsembleEngine
+
+    cfg = C.PRESETS[preset]
+    eng = EnsembleEngine(cfg, W.generate_model(cfg, 0), linear_dtype=dtype, capacity=16, max_batch=16)
+    assert eng.latency_rows()[0] >= 1, "the latency path is off for this configuration"
+    one = np.zeros((1, cfg.num_features), np.float32)
+    for i in range(reps):
+        eng.step(np.asarray([i % 16], np.int32), one)
+    buf = np.zeros((4, 512, 8), np.uint64)
+    rc = _lib.lib().b2e_lat_trace_read(ctypes.c_void_p(buf.ctypes.data))
+    assert rc == 0, f"b2e_lat_trace_read: cudaError {rc}"
+    eng.close()
+    cols = ("issue next", "cluster wait", "copies+sync", "run+sync", "arrive")
+    towers = ("xLSTM", "Mamba2", "RetNet", "Hawk")
+    kinds = {0: ("A sLSTM", "B proj+qkv", "C mLSTM cell", "D down", "MLP1 fc1", "MLP2 fc2"),
+             1: ("M1 proj+conv", "M2 ssm", "M3 out", "MLP1 fc1", "MLP2 fc2"),
+             2: ("R1 proj+rotary", "R2 retention", "R3 out", "MLP1 fc1", "MLP2 fc2"),
+             3: ("K1 proj+conv", "K2 rg-lru", "K3 out", "MLP1 fc1", "MLP2 fc2")}
+    print(f"latency-trace {preset} {dtype}, one request, cluster rank 0; us per stage (bytes: the stage's copies)")
+    for t in range(4):
+        per = len(kinds[t])
+        ns = 2 + cfg.tower_depth * per
+        tr = buf[t, :ns].astype(np.int64)
+        d = np.diff(tr[:, :6], axis=1) / 1e3
+        total = (tr[-1, 5] - tr[0, 0]) / 1e3
+        print(f"{towers[t]}: {ns} stages, {total:.1f} us; mean " + ", ".join(f"{c} {d[:, i].mean():.2f}" for i, c in enumerate(cols)))
+        for j in range(per):
+            idx = [2 + b * per + j for b in range(cfg.tower_depth)]
+            dd = d[idx].mean(axis=0)
+            nb = float(np.mean(tr[[i - 1 for i in idx], 6]))
+            print(f"  {kinds[t][j]:<16} " + "  ".join(f"{c} {dd[i]:5.2f}" for i, c in enumerate(cols)) + f"  bytes {nb:7.0f}")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -214,6 +269,10 @@ def main(argv=None):
     lt.add_argument("--preset", default="D2")
     lt.add_argument("--reps", type=int, default=8)
     lt.add_argument("--dtype", default="bf16")
+    lq = sub.add_parser("latency-trace")
+    lq.add_argument("--preset", default="D2")
+    lq.add_argument("--reps", type=int, default=30)
+    lq.add_argument("--dtype", default="bf16")
     sub.add_parser("launches").add_argument("csv")
     sub.add_parser("metrics").add_argument("csv")
     a = ap.parse_args(argv)
@@ -227,6 +286,8 @@ def main(argv=None):
         step(a.preset, a.rows, a.reps, a.dtype)
     elif a.cmd == "latency":
         latency(a.preset, a.reps, a.dtype)
+    elif a.cmd == "latency-trace":
+        latency_trace(a.preset, a.reps, a.dtype)
     elif a.cmd == "launches":
         launches(a.csv)
     else:
