@@ -68,6 +68,7 @@ _SIGS = {
     "b2e_engine_wait": (C.c_int, [_P, _P]),
     "b2e_engine_step_device": (C.c_int, [_P, _P, _P, _I32, _P, _P]),
     "b2e_engine_submit_device": (C.c_int, [_P, _P, _P, _I32, _P, _P]),
+    "b2e_set_state_kernel_waves": (C.c_int, [_I32, _P]),
     "b2e_engine_join_device": (C.c_int, [_P, _P]),
     "b2e_engine_device_error": (C.c_int, [_P, _PI32]),
     "b2e_engine_reset_slots": (C.c_int, [_P, _P, _I32]),

@@ -170,6 +170,14 @@ int b2e_engine_step_device(b2e_engine* e, const int32_t* d_slots, const float* d
   return guard([&] { E(e).step_device(d_slots, d_features, n, d_preds, static_cast<cudaStream_t>(stream)); });
 }
 
+int b2e_set_state_kernel_waves(int32_t waves, int32_t* previous) {
+  return guard([&] {
+    B2E_CHECK(waves >= 0 && waves <= 64, kErrInvalid, "state kernel waves must be in 0..64");
+    const int old = set_state_kernel_waves(waves);
+    if (previous) *previous = old;
+  });
+}
+
 int b2e_engine_submit_device(b2e_engine* e, const int32_t* d_slots, const float* d_features, int32_t n,
                              float* d_preds, void* stream) {
   return guard([&] { E(e).submit_device(d_slots, d_features, n, d_preds, static_cast<cudaStream_t>(stream)); });

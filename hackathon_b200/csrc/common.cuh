@@ -159,6 +159,12 @@ struct LaunchCfg {
   bool pdl = false;
   bool set_prio = false;
   int prio = 0;
+  // Grid of the HBM-streaming state kernels (stream.cuh): -1 = the process-wide
+  // default (state_kernel_grid), 0 = one persistent CTA per SM, items strided over
+  // the CTAs (the ensemble step: its state kernels run beside other work); w > 0
+  // = short CTAs of a few consecutive items, about w waves of two CTAs per SM (a
+  // state kernel streaming alone).
+  int bulk_waves = -1;
 };
 
 template <typename... KArgs, typename... Args>

@@ -189,6 +189,7 @@ Engine::Engine(const Dims& d, const EngineOptions& o, WeightSource& src) : d_(d)
   int prio_low = 0, prio_high = 0;
   B2E_CUDA(cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high));
   ln_.pdl = ln_bulk_.pdl = o.pdl;
+  ln_bulk_.bulk_waves = 0;  // persistent state kernels: they run beside the other towers' work
   prio_hi_ = prio_high;
   prio_lo_ = prio_low;
   seen_.assign(o.capacity, 0);

@@ -23,6 +23,10 @@ constexpr size_t kStreamSmem = 128 + size_t(kStages) * (kStateMax + kOpsMax) + 2
 }  // namespace stream_cfg
 
 void stream_init();  // per device (idempotent); the engine calls it before any capture
+// Waves of the state kernels' grid when a launch leaves it to the process
+// (LaunchCfg::bulk_waves < 0): 8 unless set; set returns the previous value.
+int state_kernel_waves();
+int set_state_kernel_waves(int waves);
 bool outer_rows_bulk_ok(const OuterRowsParams& p);
 bool ssm_cols_bulk_ok(const SsmColsParams& p);
 void outer_rows_bulk(const OuterRowsParams& p, int rows_max, cudaStream_t s, const LaunchCfg& ln);

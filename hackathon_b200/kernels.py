@@ -110,6 +110,17 @@ def mamba2_step(ssm, x, b, c, dt, decay, mask):
 _TORCH_DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 
+def set_state_kernel_waves(waves: int) -> int:
+    """Grid of the state kernels when they stream alone (this module's three steps
+    and the layer engine): waves > 0 short CTAs of a few items, ~waves waves of two
+    CTAs per SM (default 8, the fastest alone); 0 one persistent CTA per SM, the
+    grid the ensemble engine's step uses. Results are identical bit for bit.
+    Process-wide; returns the previous value (b2e_set_state_kernel_waves)."""
+    prev = C.c_int32()
+    _lib.check(_lib.lib().b2e_set_state_kernel_waves(int(waves), C.byref(prev)))
+    return prev.value
+
+
 def cast_linear(x, weight, bias=None, relu: bool = False, err=None):
     """CastLinear.forward (example_model.py:92-95) / nn.Linear on the GPU.
 

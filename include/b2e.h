@@ -114,6 +114,14 @@ typedef struct b2e_engine b2e_engine;
 typedef struct b2e_layer b2e_layer;
 
 B2E_API const char* b2e_last_error(void);
+/* Grid of the state-streaming kernels (Mamba2 ssm, mLSTM C, RetNet S) when they
+ * stream alone: b2e_mlstm_step / b2e_retnet_step / b2e_mamba2_step and the layer
+ * engine. waves > 0 (default 8): short CTAs of a few items, ~waves waves of two
+ * CTAs per SM; 0: one persistent CTA per SM, the grid the ensemble engine's step
+ * always uses (its state kernels run beside the other towers' work). Results are
+ * the same bit for bit; only the speed differs. Process-wide; *previous (may be
+ * NULL) receives the old value. No counterpart in the reference. */
+B2E_API int b2e_set_state_kernel_waves(int32_t waves, int32_t* previous);
 B2E_API const char* b2e_version(void);
 
 /* ---- ensemble engine (one per device) ---- */

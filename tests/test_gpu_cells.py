@@ -117,3 +117,29 @@ def test_state_advances_over_repeated_steps():
         out = K.retnet_step(st, *[_t(a) for a in rest], _mask(masks["mixed"]))
     assert_close(st.cpu().numpy(), st_ref, 1e-4, 1e-4, "state after 50 steps")
     assert_close(out.cpu().numpy(), want, 1e-4, 1e-4, "out after 50 steps")
+
+
+@pytest.mark.parametrize("tag,dims,batch", [
+    ("mamba2", (8, 64, 128), 300), ("mlstm", (8, 64, 64), 300), ("retnet", (8, 32, 32), 300),
+    ("mamba2", (3, 17, 64), 37), ("mlstm", (3, 40, 64), 29),
+])
+def test_state_kernel_grids_agree_bit_for_bit(tag, dims, batch):
+    """The persistent grid (the ensemble step's) and the short-CTA grids (alone)
+    run the same per-item arithmetic: outputs and state agree bit for bit, idle
+    rows included, for several wave counts and a ragged last CTA."""
+    state0, rest, masks = streams.cell_inputs(tag, batch, dims, seed=9)
+    results = []
+    prev = K.set_state_kernel_waves(0)
+    try:
+        for waves in (0, 1, 8, 64):
+            K.set_state_kernel_waves(waves)
+            st = _t(state0)
+            out = getattr(K, f"{tag}_step")(st, *[_t(a) for a in rest], _mask(masks["mixed"]))
+            torch.cuda.synchronize()
+            results.append((waves, out.cpu().numpy(), st.cpu().numpy()))
+    finally:
+        K.set_state_kernel_waves(prev)
+    w0, out0, st0 = results[0]
+    for waves, out, st in results[1:]:
+        assert np.array_equal(out.view(np.uint32), out0.view(np.uint32)), f"waves {waves}: outputs differ"
+        assert np.array_equal(st.view(np.uint32), st0.view(np.uint32)), f"waves {waves}: state differs"
