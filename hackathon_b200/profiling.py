@@ -72,11 +72,16 @@ def metrics(path: str) -> None:
                 print(f"  {m} = {d[m]} {u}")
 
 
-def cell(kind: str, rows: int, heads: int, sh: int, sk: int, reps: int) -> None:
+def cell(kind: str, rows: int, heads: int, sh: int, sk: int, reps: int, waves: int | None = None) -> None:
+    """`reps` launches of one fused state step on a dense state; `waves` picks the
+    state kernel's grid (0: the ensemble step's persistent grid; None: the
+    library's default for a step launched alone)."""
     import torch
 
     from . import kernels as K
 
+    if waves is not None:
+        K.set_state_kernel_waves(waves)
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     state = torch.randn(rows, heads, sh, sk, device=dev, generator=g)
@@ -99,7 +104,8 @@ def cell(kind: str, rows: int, heads: int, sh: int, sk: int, reps: int) -> None:
     for _ in range(reps):
         fn(state, *args, None)
     torch.cuda.synchronize()
-    print(f"{kind} rows={rows} heads={heads} sh={sh} sk={sk}: {reps} launches, state {state.numel() * 4 / 1e9:.2f} GB")
+    print(f"{kind} rows={rows} heads={heads} sh={sh} sk={sk} waves={waves}: {reps} launches, "
+          f"state {state.numel() * 4 / 1e9:.2f} GB")
 
 
 def layer(kind: str, rows: int, reps: int, dtype: str) -> None:
@@ -249,6 +255,7 @@ def main(argv=None):
     c.add_argument("--sh", type=int, default=64)
     c.add_argument("--sk", type=int, default=128)
     c.add_argument("--reps", type=int, default=4)
+    c.add_argument("--waves", type=int, default=None, help="0: the step's persistent grid; default: the alone grid")
     li = sub.add_parser("linear")
     li.add_argument("--m", type=int, default=4096)
     li.add_argument("--k", type=int, default=512)
@@ -277,7 +284,7 @@ def main(argv=None):
     sub.add_parser("metrics").add_argument("csv")
     a = ap.parse_args(argv)
     if a.cmd == "cell":
-        cell(a.kind, a.rows, a.heads, a.sh, a.sk, a.reps)
+        cell(a.kind, a.rows, a.heads, a.sh, a.sk, a.reps, a.waves)
     elif a.cmd == "linear":
         linear(a.m, a.k, a.n, a.reps, a.dtype)
     elif a.cmd == "layer":
