@@ -428,6 +428,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline(cfg, wl)
+    ingest = ingest_rate(F) if rank == 0 and world == 1 and not a.no_targets else None
 
     per_req = np.repeat(step_ms, [len(batches[Wm + K + k]) for k in range(len(step_ms))])
     tg = None
@@ -463,6 +464,7 @@ def main():
             "cpu_baseline": cpu,
             "clocks": clk,
             "targets": tg,
+            "ingest": ingest,
         }
         print(json.dumps(line), flush=True)
     eng.close()
@@ -558,6 +560,70 @@ def _device_steps(step, K, W, stream):
     e1.record(stream)
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / K
+
+
+def ingest_rate(F, n_requests=32768, per_line=16, n_symbols=256):
+    """Host side of the request path, per request (microseconds): the native
+    ingest (hackathon_b200.ingest.RequestIngest: protocol JSON lines straight into
+    per-symbol queues, then micro-batches of up to 4096 rows as float32 arrays)
+    beside the reference's way - json.loads per line, a Python list of floats per
+    request into per-symbol queues, np.asarray per request (protocol.py:86-103,
+    client.py:156-173, example_model.py:854-855) - on the same bytes; and
+    response encoding (b2e_encode_response against json.dumps of the response)."""
+    from hackathon_b200.ingest import RequestIngest, encode_response
+
+    rng = np.random.default_rng(7)
+    lines = []
+    uid = 0
+    for i in range(n_requests // per_line):
+        syms = [f"SYM_{(i * per_line + j) % n_symbols:03d}" for j in range(per_line)]
+        feats = rng.standard_normal((per_line, F)).astype(np.float32).tolist()
+        d = {"unique_ids": list(range(uid, uid + per_line)), "symbols": syms, "features": feats,
+             "timestamp": 1.5, "message_type": "inference_request"}
+        uid += per_line
+        lines.append((json.dumps(d) + "\n").encode())
+    data = b"".join(lines)
+    out = {"requests": n_requests, "requests_per_line": per_line, "bytes": len(data)}
+    # 64 KB reads (a socket's) on one thread and on the host's threads; 1 MB reads (a backlog)
+    for name, chunk, threads in (("native_us_per_request_64k_reads_1thread", 1 << 16, 1),
+                                 ("native_us_per_request_64k_reads", 1 << 16, None),
+                                 ("native_us_per_request_1m_reads", 1 << 20, None)):
+        ing = RequestIngest(F, max_queue_size=0, threads=threads)
+        t0 = time.perf_counter()
+        for i in range(0, len(data), chunk):
+            ing.feed(data[i:i + chunk])
+        got = 0
+        while True:
+            rows = ing.take_batch(4096)
+            if len(rows.unique_ids) == 0:
+                break
+            got += len(rows.unique_ids)
+        dt = time.perf_counter() - t0
+        ing.close()
+        assert got == n_requests, (got, n_requests)
+        out[name] = dt / n_requests * 1e6
+    t0 = time.perf_counter()
+    queues = {}
+    for ln in lines:
+        d = json.loads(ln.decode("utf-8").strip())
+        for u, sym, f in zip(d["unique_ids"], d["symbols"], d["features"]):
+            queues.setdefault(sym, []).append((u, f))
+    rows = [np.asarray(f, np.float32) for q in queues.values() for _, f in q]
+    out["python_json_us_per_request"] = (time.perf_counter() - t0) / n_requests * 1e6
+    assert len(rows) == n_requests
+    preds = rng.standard_normal((4096, 4)).astype(np.float32)
+    ids = np.arange(4096, dtype=np.int64)
+    t0 = time.perf_counter()
+    for _ in range(8):
+        encode_response(ids, preds, 1.5)
+    out["native_encode_us_per_answer"] = (time.perf_counter() - t0) / (8 * 4096) * 1e6
+    t0 = time.perf_counter()
+    for _ in range(8):
+        json.dumps({"unique_ids": ids.tolist(), "predictions": preds.tolist(), "client_timestamp": 1.5,
+                    "message_type": "inference_response"})
+    out["python_json_encode_us_per_answer"] = (time.perf_counter() - t0) / (8 * 4096) * 1e6
+    out["host_threads"] = os.cpu_count()
+    return out
 
 
 def _device_submits(eng, slots, feats, rows, K, W, stream):
