@@ -1160,6 +1160,143 @@ __global__ void __launch_bounds__(kRowThreads, 3) k_mlstm_mid(const MlstmMidP p)
 
 constexpr size_t kMidSmemMax = 96 * 1024;
 // Rows per k_mlstm_mid CTA: up to 4, within kMidSmemMax of shared memory.
+// k_mlstm_mid for steps of a few rows, where one CTA per four rows leaves most
+// SMs idle (one request at the default dims: 56 us on one SM), in two kernels
+// with the same arithmetic:
+// (a) conv1d + SiLU and the q/k/v BlockLinears, one CTA per 256 channels and
+//     four rows (a 4-channel block never straddles two CTAs); q and v to qkv,
+//     the unscaled k to `kraw`;
+// (b) one CTA per (head, row): the head's input and forget gate projections over
+//     cat(q, k, v) with the CTA's threads splitting the 3*mi terms, then the
+//     stabilized gates, the normalizer state and the denominator as in
+//     k_mlstm_mid, and k / sqrt(hs) into qkv.
+constexpr int kMidSplitRows = 64;  // steps up to this many rows take the two kernels
+__global__ void __launch_bounds__(kRowThreads) k_mlstm_qkv_cols(const MlstmMidP p, float* kraw) {
+  pdl_wait();
+  constexpr int RM = 4;
+  const int r0 = blockIdx.y * RM;
+  const int nr = min(RM, live_rows(p.rc.n_dev, p.rc.rows) - r0);
+  if (nr <= 0) return;
+  const int mi = p.mi, tid = threadIdx.x;
+  const int c = blockIdx.x * kRowThreads + tid;  // this thread's channel and q/k/v output
+  __shared__ long long sslot[RM];
+  __shared__ float4 xs4[RM][kRowThreads / 4];  // conv + SiLU of the CTA's channels, per row
+  float* xs = reinterpret_cast<float*>(xs4);
+  if (tid < nr) sslot[tid] = row_slot(p.rc, r0 + tid);
+  __syncthreads();
+  if (c < mi) {
+    float s0[RM], s1[RM], s2[RM], xv[RM];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      if (rr < nr) {
+        const float* st = p.conv + sslot[rr] * p.cs;
+        s0[rr] = st[c];
+        s1[rr] = st[mi + c];
+        s2[rr] = st[2 * mi + c];
+        xv[rr] = p.proj[size_t(r0 + rr) * 2 * mi + c];
+      }
+    }
+    const float w0 = p.cw[c], w1 = p.cw[mi + c], w2 = p.cw[2 * mi + c], w3 = p.cw[3 * mi + c], cb = p.cb[c];
+#pragma unroll
+    for (int rr = 0; rr < RM; ++rr) {
+      if (rr < nr) {
+        // CausalConv1d over [state, x] (model/modules.py:37-41)
+        float acc = w0 * s0[rr];
+        acc = fmaf(w1, s1[rr], acc);
+        acc = fmaf(w2, s2[rr], acc);
+        acc = fmaf(w3, xv[rr], acc);
+        float* st = p.conv + sslot[rr] * p.cs;
+        st[c] = s1[rr];
+        st[mi + c] = s2[rr];
+        st[2 * mi + c] = xv[rr];
+        const float v = siluf_(acc + cb);
+        xs[rr * kRowThreads + tid] = v;
+        p.xca[size_t(r0 + rr) * mi + c] = v;
+      }
+    }
+  }
+  __syncthreads();
+  if (c >= mi) return;
+  // q/k from the conv branch, v from x_mlstm: 4x4 BlockLinear blocks (xlstm.py:209-211)
+  const float4 wq = __ldg(reinterpret_cast<const float4*>(p.wq) + c);
+  const float4 wk = __ldg(reinterpret_cast<const float4*>(p.wk) + c);
+  const float4 wv = __ldg(reinterpret_cast<const float4*>(p.wv) + c);
+#pragma unroll
+  for (int rr = 0; rr < RM; ++rr) {
+    if (rr >= nr) break;
+    const int r = r0 + rr;
+    const float4 xc = xs4[rr][tid >> 2];
+    const float4 x0 = reinterpret_cast<const float4*>(p.proj + size_t(r) * 2 * mi)[c >> 2];
+    p.qkv[size_t(r) * 3 * mi + c] = fmaf(xc.w, wq.w, fmaf(xc.z, wq.z, fmaf(xc.y, wq.y, xc.x * wq.x)));
+    kraw[size_t(r) * mi + c] = fmaf(xc.w, wk.w, fmaf(xc.z, wk.z, fmaf(xc.y, wk.y, xc.x * wk.x)));
+    p.qkv[size_t(r) * 3 * mi + 2 * mi + c] = fmaf(x0.w, wv.w, fmaf(x0.z, wv.z, fmaf(x0.y, wv.y, x0.x * wv.x)));
+  }
+}
+
+__global__ void __launch_bounds__(kRowThreads) k_mlstm_cell_heads(const MlstmMidP p, const float* kraw) {
+  pdl_wait();
+  const int h = blockIdx.x, r = blockIdx.y;
+  if (!row_live(p.rc, r)) return;
+  const int mi = p.mi, nh = p.nh, hs = p.hs, tid = threadIdx.x;
+  __shared__ float red[2][kRowThreads / 32];
+  const long long slot = row_slot(p.rc, r);
+  const float* q = p.qkv + size_t(r) * 3 * mi;
+  const float* kr = kraw + size_t(r) * mi;
+  // igate / fgate of head h over cat(q, k, v) (xlstm.py:119-120), fp32
+  const float4* wi = reinterpret_cast<const float4*>(p.gw + size_t(h) * 3 * mi);
+  const float4* wf = reinterpret_cast<const float4*>(p.gw + size_t(nh + h) * 3 * mi);
+  const int m4 = mi >> 2;
+  float ai = 0.f, af = 0.f;
+  for (int k = tid; k < 3 * m4; k += kRowThreads) {
+    const float4 x = k < m4 ? reinterpret_cast<const float4*>(q)[k]
+                            : (k < 2 * m4 ? reinterpret_cast<const float4*>(kr)[k - m4]
+                                          : reinterpret_cast<const float4*>(q + 2 * mi)[k - 2 * m4]);
+    const float4 a = __ldg(wi + k), b = __ldg(wf + k);
+    ai = fmaf(x.w, a.w, fmaf(x.z, a.z, fmaf(x.y, a.y, fmaf(x.x, a.x, ai))));
+    af = fmaf(x.w, b.w, fmaf(x.z, b.z, fmaf(x.y, b.y, fmaf(x.x, b.x, af))));
+  }
+  ai = warp_sum(ai);
+  af = warp_sum(af);
+  if ((tid & 31) == 0) {
+    red[0][tid >> 5] = ai;
+    red[1][tid >> 5] = af;
+  }
+  __syncthreads();
+  float ig = p.gb[h], fg = p.gb[nh + h];
+  for (int w = 0; w < kRowThreads / 32; ++w) {
+    ig += red[0][w];
+    fg += red[1][w];
+  }
+  // MLSTMCell gates and normalizer (xlstm.py:92-103, 121-132)
+  const float mo = p.m[slot * p.m_s + h];
+  const float lf = logsigmoidf_(fg);
+  const float mn = fmaxf(ig, mo + lf);
+  const float i_g = expf(ig - mn), f_g = expf(lf + mo - mn);
+  const float sq = sqrtf(float(hs));
+  float* nst = p.n + slot * p.n_s;
+  float qn = 0.f;
+  for (int j = tid; j < hs; j += kRowThreads) {
+    const int e = h * hs + j;
+    const float ks = kr[e] / sq;  // k / sqrt(head_size) (xlstm.py:99)
+    const float nv = f_g * nst[e] + i_g * ks;
+    p.qkv[size_t(r) * 3 * mi + mi + e] = ks;
+    nst[e] = nv;
+    qn = fmaf(q[e], nv, qn);
+  }
+  qn = warp_sum(qn);
+  __syncthreads();  // every thread has read red[] and m
+  if ((tid & 31) == 0) red[0][tid >> 5] = qn;
+  __syncthreads();
+  if (tid == 0) {
+    float v = 0.f;
+    for (int w = 0; w < kRowThreads / 32; ++w) v += red[0][w];
+    p.m[slot * p.m_s + h] = mn;
+    p.g2[size_t(r) * 2 * nh + h] = i_g;
+    p.g2[size_t(r) * 2 * nh + nh + h] = f_g;
+    p.den[size_t(r) * nh + h] = fmaxf(fabsf(v), expf(-mn)) + 1e-6f;  // xlstm.py:130-132
+  }
+}
+
 int mid_rows(int mi, int nh) {
   const size_t per = size_t(4 * mi + 2 * nh) * sizeof(float);
   B2E_CHECK(per <= kMidSmemMax, kErrInvalid, "mLSTM inner size too large for one CTA");
@@ -1424,8 +1561,16 @@ class XLSTMLayer : public Layer {
     const int rpc = mid_rows(mi_, nh_);
     MlstmMidP mp{rc, b.proj, mi_, nh_, hs_, mconv_, smconv_, mcw_, mcb_, wq_, wk_, wv_, gw_, gb_,
                  n_, sn2_, m_, sm2_, b.xca, b.qkv, b.g2, b.den, rpc};
-    launch_k(c.ln, k_mlstm_mid, dim3(ceil_div(c.rows, rpc)), dim3(kRowThreads),
-             size_t(rpc) * (4 * mi_ + 2 * nh_) * sizeof(float), c.s, mp);
+    if (c.rows <= kMidSplitRows) {
+      // b.num (written by the state step below) holds the unscaled k meanwhile
+      launch_k(c.ln, k_mlstm_qkv_cols, dim3(ceil_div(mi_, kRowThreads), ceil_div(c.rows, 4)), dim3(kRowThreads), 0,
+               c.s, mp, b.num);
+      launch_k(c.ln, k_mlstm_cell_heads, dim3(nh_, c.rows), dim3(kRowThreads), 0, c.s, mp,
+               static_cast<const float*>(b.num));
+    } else {
+      launch_k(c.ln, k_mlstm_mid, dim3(ceil_div(c.rows, rpc)), dim3(kRowThreads),
+               size_t(rpc) * (4 * mi_ + 2 * nh_) * sizeof(float), c.s, mp);
+    }
     OuterRowsParams op;
     op.at = {C_, sC_, c.slots, nullptr, c.rows, c.n_dev};
     op.nh = nh_; op.sh = hs_; op.sk = hs_;
