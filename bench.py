@@ -650,7 +650,8 @@ def targets(dev, peak, K):
     """The north_star's target row and BASELINE configs 2 and 3, beside the headline:
     * d1_4096: the full ensemble at D1 (depth 12), 4096 symbols per step, bf16
       weights, fp32 state: requests/s and the whole step's HBM fraction;
-    * single-request latency (host API, one row) at D1 and D2;
+    * single-request latency (host API, one row) at D1 and D2, and at the default
+      dims (config 1's shape);
     * config2 / config3: the Mamba2 layer (d_state 64, stated a / dt fills), the
       RetNet layer (4 heads of 64, gamma_h = 1 - 2^(-5-h)) and the xLSTM layer
       whose mLSTM cell has 4 heads of 64, each 4096 symbols x 1,000 steps, bf16
@@ -682,6 +683,18 @@ def targets(dev, peak, K):
                                    if lr else "batch graph"}
     eng.close()
     del sd
+    # BASELINE config 1's shape: one request at a time at the default dims (batch
+    # graph: the latency kernel's stage slices do not fit at hidden 2048)
+    cfg0 = C.D0
+    sd = Wt.generate_model(cfg0, seed=0)
+    eng = EnsembleEngine(cfg0, sd, device=dev.index, linear_dtype="bf16", capacity=16, max_batch=16)
+    del sd
+    lr, cl = eng.latency_rows()
+    p50, p99 = _lat(eng, list(range(16)), cfg0.num_features)
+    out["config1_single_request_us"] = {"p50": p50, "p99": p99, "dims": "D0 (hidden 2048, depth 12)",
+                                        "weights": "bf16", "path": f"one kernel, {cl}-CTA cluster per tower"
+                                        if lr else "batch graph"}
+    eng.close()
     for name, kinds in (("config2", ["mamba2"]), ("config3", ["retnet", "xlstm"])):
         res = {}
         for kind in kinds:

@@ -426,18 +426,22 @@ void outer_rows(const OuterRowsParams& p, int rows_max, cudaStream_t s, const La
     outer_rows_bulk(p, rows_max, s, ln);
     return;
   }
-  const int kt = std::min(kKT, p.sk);
+  int kt = std::min(kKT, p.sk);
+  // a step of few rows: narrower column tiles, so the launch still covers the SMs
+  // (one request at the default dims: 8 heads x 4 tiles of 128 -> 8 x 16 of 32)
+  while (kt > 32 && p.sk % kt == 0 && long(p.sk / kt) * p.nh * rows_max < 2L * 148) kt /= 2;
   const int per_head = p.sh * (kt / 4);
   const int L = kt / 4, RH = kThreads / L;
   auto smem_of = [&](int hg) {
     return (2 * ((size_t(hg) * p.sh + 3) & ~size_t(3)) + size_t(hg) * kKT + ((hg + 3) & ~3) + size_t(hg) * RH * kt) * 4;
   };
-  int HG = p.sk <= kKT ? std::max(1, std::min(p.nh, kItems / per_head)) : 1;
+  const bool narrowed = kt < std::min(kKT, p.sk);  // then one head per CTA, for the same reason
+  int HG = (p.sk <= kKT && !narrowed) ? std::max(1, std::min(p.nh, kItems / per_head)) : 1;
   while (HG > 1 && (p.nh % HG || smem_of(HG) > 48 * 1024)) --HG;
   const size_t smem = smem_of(HG);
   B2E_CHECK(smem <= 48 * 1024, kErrInvalid, "outer_rows: head too large for one CTA");
-  dim3 grid(ceil_div(p.sk, kKT), ceil_div(p.nh, HG), rows_max);
   const bool tiles = p.sk % kt == 0;  // every tile full width
+  dim3 grid(ceil_div(p.sk, tiles ? kt : kKT), ceil_div(p.nh, HG), rows_max);
   if (tiles && kt == 128)
     launch_k(ln, outer_rows_fast<32>, grid, dim3(kThreads), smem, s, p, HG);
   else if (tiles && kt == 64)
