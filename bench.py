@@ -626,6 +626,39 @@ def ingest_rate(F, n_requests=32768, per_line=16, n_symbols=256):
     return out
 
 
+def client_rate(dev, n_symbols=4096, calls=20):
+    """The drop-in API itself: B200InferenceClient.process_batch (example_model.py:769-905)
+    at D2 dims with bf16 weights, every call one request for each of n_symbols
+    symbols (PendingRequest objects with Python lists of 79 floats, as the
+    reference client queues them): wall-clock requests/s and ms per call, host
+    work (grouping, np.asarray of the feature lists, the answer lists) included."""
+    from hackathon_b200 import config as C
+    from hackathon_b200 import weights as Wt
+    from hackathon_b200.client import B200InferenceClient, PendingRequest
+
+    cfg = C.D2
+    cl = B200InferenceClient(n_symbols, config=cfg, weights=Wt.generate_model(cfg, seed=0), linear_dtype="bf16",
+                             devices=[dev.index])
+    rng = np.random.default_rng(11)
+    uid = 0
+    batches = []
+    for _ in range(calls + 3):
+        f = rng.standard_normal((n_symbols, cfg.num_features)).astype(np.float32).tolist()
+        batches.append({f"SYM_{i:05d}": [PendingRequest(uid + i, f"SYM_{i:05d}", f[i], 0.0)] for i in range(n_symbols)})
+        uid += n_symbols
+    for b in batches[:3]:
+        cl.process_batch(b)
+    t0 = time.perf_counter()
+    for b in batches[3:]:
+        resp = cl.process_batch(b)
+    dt = time.perf_counter() - t0
+    assert len(resp.unique_ids) == n_symbols
+    for e in cl.engines:
+        e.close()
+    return {"requests_per_s": calls * n_symbols / dt, "ms_per_call": dt / calls * 1e3, "symbols_per_call": n_symbols,
+            "dims": "D2", "weights": "bf16"}
+
+
 def _device_submits(eng, slots, feats, rows, K, W, stream):
     """Mean ms of one step over K device-timed b2e_engine_submit_device steps and
     their join, after W warm-up ones."""
@@ -652,6 +685,7 @@ def targets(dev, peak, K):
       weights, fp32 state: requests/s and the whole step's HBM fraction;
     * single-request latency (host API, one row) at D1 and D2, and at the default
       dims (config 1's shape);
+    * process_batch: the drop-in client API's requests/s with 4096 symbols a call;
     * config2 / config3: the Mamba2 layer (d_state 64, stated a / dt fills), the
       RetNet layer (4 heads of 64, gamma_h = 1 - 2^(-5-h)) and the xLSTM layer
       whose mLSTM cell has 4 heads of 64, each 4096 symbols x 1,000 steps, bf16
@@ -695,6 +729,7 @@ def targets(dev, peak, K):
                                         "weights": "bf16", "path": f"one kernel, {cl}-CTA cluster per tower"
                                         if lr else "batch graph"}
     eng.close()
+    out["process_batch"] = client_rate(dev)
     for name, kinds in (("config2", ["mamba2"]), ("config3", ["retnet", "xlstm"])):
         res = {}
         for kind in kinds:

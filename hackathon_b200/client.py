@@ -25,6 +25,7 @@ symbol whose home GPU is full takes a slot on another one).
 from __future__ import annotations
 
 import importlib
+import itertools
 import math
 import os
 import time
@@ -111,6 +112,16 @@ def load_reference_weights(token: Optional[str] = None) -> Dict[str, np.ndarray]
     path = hf_hub_download(repo_id="jane-street-gpu-mode/hackathon", filename="state_dict.pt", token=token)
     sd = torch.load(path, weights_only=True, map_location="cpu")
     return {k: v.float().numpy() for k, v in sd.items()}
+
+
+def _feature_rows(feats, nf: int) -> np.ndarray:
+    """np.asarray(feats, float32) of rows of nf values (example_model.py:854-855):
+    the same float32 values, a third faster for thousands of Python lists; a row
+    of another length raises as the reference's reshape does."""
+    if all(len(f) == nf for f in feats):
+        return np.fromiter(itertools.chain.from_iterable(feats), dtype=np.float32,
+                           count=len(feats) * nf).reshape(len(feats), nf)
+    return np.asarray(feats, dtype=np.float32).reshape(len(feats), nf)
 
 
 class B200InferenceClient(_Base):
@@ -265,13 +276,13 @@ class B200InferenceClient(_Base):
                         locs.append(loc)
                         feats.append(reqs[k].features)
                         batch_requests.append(reqs[k])
-                rows = np.asarray(feats, dtype=np.float32).reshape(len(locs), self.num_features)
+                rows = _feature_rows(feats, self.num_features)
                 rounds.append((locs, rows))
                 reqs_of.append(batch_requests)
             for batch_requests, preds in zip(reqs_of, self._run_rounds(rounds)):
-                for req, p in zip(batch_requests, preds):
-                    all_unique_ids.append(req.unique_id)
-                    all_predictions.append(p.astype(float).tolist())
+                # one conversion a round: the same Python floats, row by row
+                all_unique_ids.extend(req.unique_id for req in batch_requests)
+                all_predictions.extend(preds.astype(float).tolist())
         return InferenceResponse(unique_ids=all_unique_ids, predictions=all_predictions,
                                  client_timestamp=time.time())
 
