@@ -46,6 +46,21 @@ def test_library_loads_and_reports_errors_without_a_gpu():
         _lib.check(L.b2e_engine_slot_bytes(None, None))
 
 
+def test_state_kernel_grid_setting_is_checked_and_returns_the_previous_value():
+    """b2e_set_state_kernel_waves only records a process-wide launch choice (no
+    device work): out-of-range values are refused with B2E_ERR_INVALID and leave
+    it unchanged; a valid one returns the previous value."""
+    L = _lib.lib()
+    prev = C.c_int32(-1)
+    assert L.b2e_set_state_kernel_waves(8, C.byref(prev)) == 0
+    start = prev.value
+    for bad in (-1, 65, 1000):
+        assert L.b2e_set_state_kernel_waves(bad, C.byref(prev)) == -1  # B2E_ERR_INVALID
+        assert b"waves" in L.b2e_last_error()
+    assert L.b2e_set_state_kernel_waves(0, C.byref(prev)) == 0 and prev.value == 8
+    assert L.b2e_set_state_kernel_waves(start, None) == 0
+
+
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_lib", None)
     monkeypatch.setenv("B2E_LIB", str(tmp_path / "absent.so"))
