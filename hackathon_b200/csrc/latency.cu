@@ -45,8 +45,17 @@ namespace {
 
 namespace cg = cooperative_groups;
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 288;
 constexpr int kWarps = kThreads / 32;
+// Warps 0-7 run the stages; warp 8 (the producer) issues the next stage's copies
+// meanwhile. Barriers inside a stage are over the compute warps only (named
+// barrier 1); the producer joins the CTA only at the stage's end (barrier 0).
+// Nine warps cap registers at 168 a thread (a few spill to the stack): measured
+// faster than eight compute warps without a producer (D1 one request 517 -> 461
+// us) and than seven compute warps with one (480 us).
+constexpr int kCThreads = kThreads - 32;
+constexpr int kCWarps = kCThreads / 32;
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory"); }
 constexpr float kF32Eps = 1.1920928955078125e-07f;  // nn.RMSNorm(eps=None) in float32
 
 // ----------------------------------------------------------- primitives
@@ -78,7 +87,8 @@ __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // rows x row_bytes from src (src_stride bytes apart) into shared memory
-// (dst_stride bytes apart), spread over the CTA's threads; asynchronous.
+// (dst_stride bytes apart), spread over the producer warp's lanes (other
+// threads return); asynchronous.
 __device__ __forceinline__ void pf2d(void* dst, const void* src, int rows, int row_bytes, long long src_stride,
                                   int dst_stride) {
   if (rows <= 0 || row_bytes <= 0) return;
@@ -87,7 +97,9 @@ __device__ __forceinline__ void pf2d(void* dst, const void* src, int rows, int r
   const int unit = v16 ? 16 : 4;
   const int per_row = row_bytes / unit;
   const int total = rows * per_row;
-  for (int i = threadIdx.x; i < total; i += kThreads) {
+  const int pt = int(threadIdx.x) - kCThreads;
+  if (pt < 0) return;
+  for (int i = pt; i < total; i += 32) {
     const int r = i / per_row, c = i - r * per_row;
     char* d = static_cast<char*>(dst) + size_t(r) * dst_stride + size_t(c) * unit;
     const char* s = static_cast<const char*>(src) + r * src_stride + size_t(c) * unit;
@@ -99,13 +111,14 @@ __device__ __forceinline__ void pf2d(void* dst, const void* src, int rows, int r
 }
 // One contiguous segment: no per-chunk row arithmetic.
 __device__ __forceinline__ void pf1d(void* dst, const void* src, int bytes) {
-  if (bytes <= 0) return;
+  const int pt = int(threadIdx.x) - kCThreads;
+  if (bytes <= 0 || pt < 0) return;
   char* d = static_cast<char*>(dst);
   const char* sp = static_cast<const char*>(src);
   if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | uintptr_t(bytes)) & 15) == 0) {
-    for (int i = threadIdx.x * 16; i < bytes; i += kThreads * 16) cp16(d + i, sp + i);
+    for (int i = pt * 16; i < bytes; i += 32 * 16) cp16(d + i, sp + i);
   } else {
-    for (int i = threadIdx.x * 4; i < bytes; i += kThreads * 4) cp4(d + i, sp + i);
+    for (int i = pt * 4; i < bytes; i += 32 * 4) cp4(d + i, sp + i);
   }
 }
 
@@ -177,7 +190,7 @@ __device__ __forceinline__ void gemv(const WT* W, int ldw, int K, int nrows, con
   constexpr int V = WVec<WT>::N;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, sub = lane & 7, grp = lane >> 3;
   const int KV = K / V;
-  for (int n0 = warp * 4; n0 < nrows; n0 += kWarps * 4) {
+  for (int n0 = warp * 4; n0 < nrows; n0 += kCWarps * 4) {
     const int n = n0 + grp;
     float a[kLatMaxRows] = {0.f, 0.f, 0.f, 0.f};
     if (n < nrows) {
@@ -216,12 +229,12 @@ __device__ __forceinline__ void gemv(const WT* W, int ldw, int K, int nrows, con
 }
 
 // out[r*2 + j] = sum_k W[j*ldw + k] * X[r*ldx + k] for j < 2 rows of a long K,
-// with every thread of the CTA (f32 weights). `red` holds kWarps*8 floats.
+// with every thread of the CTA (f32 weights). `red` holds kCWarps*8 floats.
 __device__ __forceinline__ void dot2_wide(const float* W, int ldw, int K, const float* X, int ldx, int R, float* out,
                                        float* red) {
   float a[2][kLatMaxRows] = {};
   const int K4 = K / 4;
-  for (int v = threadIdx.x; v < K4; v += kThreads) {
+  for (int v = threadIdx.x; v < K4; v += kCThreads) {
     const float4 w0 = *reinterpret_cast<const float4*>(W + 4 * v);
     const float4 w1 = *reinterpret_cast<const float4*>(W + ldw + 4 * v);
 #pragma unroll
@@ -233,7 +246,7 @@ __device__ __forceinline__ void dot2_wide(const float* W, int ldw, int K, const 
       }
     }
   }
-  for (int k = 4 * K4 + threadIdx.x; k < K; k += kThreads) {
+  for (int k = 4 * K4 + threadIdx.x; k < K; k += kCThreads) {
 #pragma unroll
     for (int r = 0; r < kLatMaxRows; ++r) {
       if (r < R) {
@@ -250,14 +263,14 @@ __device__ __forceinline__ void dot2_wide(const float* W, int ldw, int K, const 
       const float s = warp_sum(a[j][r]);
       if (lane == 0) red[warp * 8 + j * kLatMaxRows + r] = s;
     }
-  __syncthreads();
+  csync();
   if (threadIdx.x < 2 * kLatMaxRows) {
     float s = 0.f;
-    for (int w = 0; w < kWarps; ++w) s += red[w * 8 + threadIdx.x];
+    for (int w = 0; w < kCWarps; ++w) s += red[w * 8 + threadIdx.x];
     const int j = threadIdx.x / kLatMaxRows, r = threadIdx.x % kLatMaxRows;
     if (r < R) out[r * 2 + j] = s;
   }
-  __syncthreads();
+  csync();
 }
 
 // Per row r < R: the sum of f(x[r*ld + i]) over i < n, computed by every warp
@@ -286,7 +299,7 @@ __device__ __forceinline__ void rmsnorm(const float* x, int ld, int n, int R, co
   float inv[kLatMaxRows];
 #pragma unroll
   for (int r = 0; r < kLatMaxRows; ++r) inv[r] = 1.0f / sqrtf(ss[r] / float(n) + eps);
-  for (int i = threadIdx.x; i < n; i += kThreads)
+  for (int i = threadIdx.x; i < n; i += kCThreads)
 #pragma unroll
     for (int r = 0; r < kLatMaxRows; ++r) {
       if (r < R) {
@@ -296,7 +309,7 @@ __device__ __forceinline__ void rmsnorm(const float* x, int ld, int n, int R, co
         if (yl) yl[r * ldl + i] = WVec<WT>::round(y);
       }
     }
-  __syncthreads();
+  csync();
 }
 
 // LayerNorm rows (no bias): y = (x - mean) / sqrt(var + eps) * w.
@@ -312,18 +325,18 @@ __device__ __forceinline__ void layernorm(const float* x, int ld, int n, int R, 
   float inv[kLatMaxRows];
 #pragma unroll
   for (int r = 0; r < kLatMaxRows; ++r) inv[r] = 1.0f / sqrtf(q[r] / float(n) + eps);
-  for (int i = threadIdx.x; i < n; i += kThreads)
+  for (int i = threadIdx.x; i < n; i += kCThreads)
 #pragma unroll
     for (int r = 0; r < kLatMaxRows; ++r)
       if (r < R) y[r * ldy + i] = (x[r * ld + i] - mu[r]) * inv[r] * w[i];
-  __syncthreads();
+  csync();
 }
 
 // Mean and 1/sqrt(var + eps) of G groups of gs values per row, one warp per
 // (row, group): gm[r*G + g], gr[r*G + g]. Ends with a barrier.
 __device__ __forceinline__ void group_stats(const float* x, int ld, int G, int gs, int R, float eps, float* gm, float* gr) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int p = warp; p < R * G; p += kWarps) {
+  for (int p = warp; p < R * G; p += kCWarps) {
     const int r = p / G, g = p - r * G;
     const float* v = x + r * ld + g * gs;
     float s = 0.f;
@@ -340,7 +353,7 @@ __device__ __forceinline__ void group_stats(const float* x, int ld, int G, int g
       gr[p] = 1.0f / sqrtf(q + eps);
     }
   }
-  __syncthreads();
+  csync();
 }
 
 // Write src[r*sld + i] (local shared memory, i < cnt) to dst[r*ld + off + i]
@@ -351,14 +364,14 @@ __device__ __forceinline__ void bcast(const float* src, int sld, int cnt, int R,
   const bool v4 = (cnt & 3) == 0 && (off & 3) == 0 && (ld & 3) == 0 && (sld & 3) == 0;
   if (v4) {
     const int c4 = cnt >> 2, per = R * c4, total = CL * per;
-    for (int i = threadIdx.x; i < total; i += kThreads) {
+    for (int i = threadIdx.x; i < total; i += kCThreads) {
       const int peer = i / per, rem = i - peer * per, r = rem / c4, j = rem - r * c4;
       float4* d = reinterpret_cast<float4*>(cluster.map_shared_rank(dst + r * ld + off + 4 * j, peer));
       *d = *reinterpret_cast<const float4*>(src + r * sld + 4 * j);
     }
   } else {
     const int per = R * cnt, total = CL * per;
-    for (int i = threadIdx.x; i < total; i += kThreads) {
+    for (int i = threadIdx.x; i < total; i += kCThreads) {
       const int peer = i / per, rem = i - peer * per, r = rem / cnt, j = rem - r * cnt;
       *cluster.map_shared_rank(dst + r * ld + off + j, peer) = src[r * sld + j];
     }
@@ -461,7 +474,7 @@ struct Tower {
     a.V1 = b.take<float>(RM * a.ld1);
     a.V2 = b.take<float>(RM * a.ld2);
     a.stg = b.take<float>(RM * stg_len());
-    a.red = b.take<float>(kWarps * 8);
+    a.red = b.take<float>(kCWarps * 8);
     a.gm = b.take<float>(RM * 64);
     a.gr = b.take<float>(RM * 64);
     a.OW = b.take<float>(a.ldH);
@@ -674,7 +687,7 @@ struct Tower {
       const int ld = rup4(q.sl.n());
       gemv<WT>(w1, H, H, nl, a.T, a.ldT, R, a.stg, ld);
       gemv<float>(dtw, H, H, q.dh - q.dl, a.U0, a.ldH, R, a.stg + nl, ld);  // dt_proj keeps fp32 (example_model.py:106)
-      __syncthreads();
+      csync();
       const int cc[3][2] = {{q.xl, q.xh}, {q.bl, q.bh}, {q.cl, q.ch}};
       const int base[3] = {0, 2 * mi, 2 * mi + bc};
       const int CC[3] = {mi, bc, bc};
@@ -688,7 +701,7 @@ struct Tower {
         cs[t] = b.take<float>(RM * 3 * n);
       }
       const float* dtb = sv.p[1];
-      for (int i = threadIdx.x; i < q.sl.n() * R; i += kThreads) {
+      for (int i = threadIdx.x; i < q.sl.n() * R; i += kCThreads) {
         const int r = i / q.sl.n(), e = i - r * q.sl.n(), idx = q.sl.lo + e;
         float& v = a.stg[r * ld + e];
         if (idx < 2 * mi + 2 * bc) {
@@ -710,7 +723,7 @@ struct Tower {
           v = softplusf_(v + dtb[h]);  // mamba2.py:96
         }
       }
-      __syncthreads();
+      csync();
       bcast(a.stg, ld, q.sl.n(), R, a.V1, a.ld1, q.sl.lo, CL);
       return;
     }
@@ -721,7 +734,7 @@ struct Tower {
       const float* a_ = sv.p[1];
       const float* d_ = sv.p[2];
       const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-      for (int pr = warp; pr < sl.n() * R; pr += kWarps) {
+      for (int pr = warp; pr < sl.n() * R; pr += kCWarps) {
         const int r = pr / sl.n(), p = sl.lo + (pr - r * sl.n()), n = p / hs_m;
         const float* v = a.V1 + r * a.ld1;
         const float x = v[p], dt = v[2 * mi + 2 * bc + n];
@@ -741,7 +754,7 @@ struct Tower {
           a.stg[r * rup4(sl.n()) + (p - sl.lo)] = y * siluf_(v[mi + p]);  // y * silu(z) (mamba2.py:160)
         }
       }
-      __syncthreads();
+      csync();
       bcast(a.stg, rup4(sl.n()), sl.n(), R, a.V2, a.ld2, sl.lo, CL);
       return;
     }
@@ -756,14 +769,14 @@ struct Tower {
   __device__ void residual_out(const WT* w, int K, Slice sl, const WT* bias) {
     const int ld = rup4(sl.n());
     gemv<WT>(w, K, K, sl.n(), a.T, a.ldT, R, a.stg, ld);
-    __syncthreads();
-    for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+    csync();
+    for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
       const int r = i / sl.n(), e = i - r * sl.n();
       float v = a.stg[r * ld + e];
       if (bias) v += WVec<WT>::one(bias, e);
       a.stg[r * ld + e] = a.X[r * a.ldH + sl.lo + e] + WVec<WT>::round(v);
     }
-    __syncthreads();
+    csync();
     bcast(a.stg, ld, sl.n(), R, a.X, a.ldH, sl.lo, CL);
   }
 
@@ -805,18 +818,18 @@ struct Tower {
       const int* posv = reinterpret_cast<const int*>(b.take<float>(RM));
       const int ld = rup4(sl.n());
       gemv<WT>(w, H, H, sl.n(), a.T, a.ldT, R, a.stg, ld);
-      __syncthreads();
-      for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+      csync();
+      for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
         const int r = i / sl.n(), e = i - r * sl.n();
         a.stg[r * ld + e] = WVec<WT>::round(a.stg[r * ld + e]);  // CastLinear outputs q, k, v, g
       }
-      __syncthreads();
+      csync();
       const float* angle = sv.p[1];
       const float* decay = sv.p[2];
       const float scaling = powf(float(hs_r), -0.5f);
       // rotary and scaling into a second half of the staging area (pairs read both lanes' inputs)
       float* out = a.stg + R * ld;
-      for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+      for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
         const int r = i / sl.n(), e = i - r * sl.n(), idx = sl.lo + e;
         float v = a.stg[r * ld + e];
         if (idx < 2 * H) {
@@ -839,10 +852,10 @@ struct Tower {
         }
         out[r * ld + e] = v;
       }
-      __syncthreads();
+      csync();
       // the CTA holding a head's first q element advances that head's scale;
       // the first CTA advances the position (retnet.py:93, 172)
-      for (int i = threadIdx.x; i < nh * R; i += kThreads) {
+      for (int i = threadIdx.x; i < nh * R; i += kCThreads) {
         const int r = i / nh, n = i - r * nh;
         if (n * hs_r >= sl.lo && n * hs_r < sl.hi) L.st[1][slot[r] * L.ss[1] + n] = sc[r * nh + n] * decay[n] + 1.0f;
       }
@@ -857,7 +870,7 @@ struct Tower {
       float* S = b.take<float>(RM * hs_r * sl.n());
       const float* decay = sv.p[2];
       const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, ld = rup4(sl.n());
-      for (int pc = warp; pc < sl.n() * R; pc += kWarps) {
+      for (int pc = warp; pc < sl.n() * R; pc += kCWarps) {
         const int r = pc / sl.n(), c = pc - r * sl.n(), e = sl.lo + c, n = e / hs_r, kk = e - n * hs_r;
         const float* v1 = a.V1 + r * a.ld1;
         const float ve = v1[2 * H + e], g = decay[n];
@@ -872,13 +885,13 @@ struct Tower {
         o = warp_sum(o);
         if (lane == 0) a.stg[r * ld + c] = o;
       }
-      __syncthreads();
+      csync();
       bcast(a.stg, ld, sl.n(), R, a.V2, a.ld2, sl.lo, CL);
       return;
     }
     // R3: silu(g) * headRMSNorm(O) -> out_proj + X (retnet.py:168-170)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int p = warp; p < R * nh; p += kWarps) {
+    for (int p = warp; p < R * nh; p += kCWarps) {
       const int r = p / nh, n = p - r * nh;
       const float* o = a.V2 + r * a.ld2 + n * hs_r;
       float ss = 0.f;
@@ -886,13 +899,13 @@ struct Tower {
       ss = warp_sum(ss);
       if (lane == 0) a.gr[p] = 1.0f / sqrtf(ss / float(hs_r) + 1e-6f);
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < H * R; i += kThreads) {
+    csync();
+    for (int i = threadIdx.x; i < H * R; i += kCThreads) {
       const int r = i / H, e = i - r * H;
       const float g = a.V1[r * a.ld1 + 3 * H + e];
       a.T[r * a.ldT + e] = WVec<WT>::round(siluf_(g) * (a.V2[r * a.ld2 + e] * a.gr[r * nh + e / hs_r]));
     }
-    __syncthreads();
+    csync();
     const Slice sl = slice_of(H, rank, CL);
     residual_out(b.take<WT>(size_t(sl.n()) * H), H, sl, nullptr);
   }
@@ -941,8 +954,8 @@ struct Tower {
       const float* cs = b.take<float>(RM * 3 * n);
       const int ld = rup4(sl.n());
       gemv<WT>(w, H, H, sl.n(), a.T, a.ldT, R, a.stg, ld);
-      __syncthreads();
-      for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+      csync();
+      for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
         const int r = i / sl.n(), e = i - r * sl.n(), idx = sl.lo + e;
         float v = WVec<WT>::round(a.stg[r * ld + e]);
         if (idx >= H) {  // recurrent branch -> conv (hawk.py:79-80)
@@ -957,7 +970,7 @@ struct Tower {
         }
         a.stg[r * ld + e] = v;
       }
-      __syncthreads();
+      csync();
       bcast(a.stg, ld, sl.n(), R, a.V1, a.ld1, sl.lo, CL);
       return;
     }
@@ -969,7 +982,7 @@ struct Tower {
       const float* av = b.take<float>(sl.n());
       const float* hs = b.take<float>(RM * sl.n());
       const int ld = rup4(sl.n()), lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-      for (int pc = warp; pc < sl.n() * R; pc += kWarps) {
+      for (int pc = warp; pc < sl.n() * R; pc += kCWarps) {
         const int r = pc / sl.n(), c = pc - r * sl.n(), ch = sl.lo + c, jb = ch / hb;
         const float* xc = a.V1 + r * a.ld1 + H + jb * hb;
         float gi = 0.f, gr = 0.f;
@@ -989,15 +1002,15 @@ struct Tower {
           a.stg[r * ld + c] = geluf_(a.V1[r * a.ld1 + ch]) * hn;
         }
       }
-      __syncthreads();
+      csync();
       bcast(a.stg, ld, sl.n(), R, a.V2, a.ld2, sl.lo, CL);
       return;
     }
-    for (int i = threadIdx.x; i < H * R; i += kThreads) {
+    for (int i = threadIdx.x; i < H * R; i += kCThreads) {
       const int r = i / H, e = i - r * H;
       a.T[r * a.ldT + e] = WVec<WT>::round(a.V2[r * a.ld2 + e]);
     }
-    __syncthreads();
+    csync();
     const Slice sl = slice_of(H, rank, CL);
     residual_out(b.take<WT>(size_t(sl.n()) * H), H, sl, nullptr);
   }
@@ -1079,7 +1092,7 @@ struct Tower {
       // gate inputs per row: xa = [silu(conv(LN u)) | h], xb = [LN u | h] over the head block
       float* xa = a.V2;                      // [R][2bs] (V2 is free until stage C)
       float* xb = a.V2 + RM * 2 * bs;
-      for (int i = threadIdx.x; i < bs * R; i += kThreads) {
+      for (int i = threadIdx.x; i < bs * R; i += kCThreads) {
         const int r = i / bs, k = i - r * bs, c = b0 + k;
         const float v = a.O1[r * a.ldH + c];
         const float* st = cs + r * 3 * bs;
@@ -1095,13 +1108,13 @@ struct Tower {
         xa[r * 2 * bs + bs + k] = hp[r * bs + k];
         xb[r * 2 * bs + bs + k] = hp[r * bs + k];
       }
-      __syncthreads();
+      csync();
       float* G = a.stg;  // [R][4n]
       gemv<float>(wg, 2 * bs, 2 * bs, 2 * n, xa, 2 * bs, R, G, 4 * n);             // i, f
       gemv<float>(wg + size_t(2) * n * 2 * bs, 2 * bs, 2 * bs, 2 * n, xb, 2 * bs, R, G + 2 * n, 4 * n);  // z, o
-      __syncthreads();
+      csync();
       float* hout = a.stg + RM * 4 * n;
-      for (int i = threadIdx.x; i < n * R; i += kThreads) {
+      for (int i = threadIdx.x; i < n * R; i += kCThreads) {
         const int r = i / n, e = i - r * n, c = sl.lo + e;
         const float* gr = G + r * 4 * n;
         float cc = cst[r * n + e], nn = nst[r * n + e], mm = mst[r * n + e];
@@ -1113,7 +1126,7 @@ struct Tower {
         L.st[4][slot[r] * L.ss[4] + c] = mm;
         hout[r * n + e] = y;
       }
-      __syncthreads();
+      csync();
       bcast(hout, n, n, R, a.HN, a.ldH, sl.lo, CL);
       return;
     }
@@ -1122,18 +1135,18 @@ struct Tower {
       group_stats(a.HN, a.ldH, nbl, bs, R, 1e-5f, a.gm, a.gr);
       const float* gnw = sv.p[1];
       const float* gnb = sv.p[2];
-      for (int i = threadIdx.x; i < H * R; i += kThreads) {
+      for (int i = threadIdx.x; i < H * R; i += kCThreads) {
         const int r = i / H, e = i - r * H, g = e / bs;
         const float y = (a.HN[r * a.ldH + e] - a.gm[r * nbl + g]) * a.gr[r * nbl + g];
         a.O1[r * a.ldH + e] = (y * gnw[e] + gnb[e]) + a.U0[r * a.ldH + e];
       }
-      __syncthreads();
+      csync();
       layernorm(a.O1, a.ldH, H, R, sv.p[3], 1e-5f, a.T, a.ldT, a.red);
-      for (int i = threadIdx.x; i < H * R; i += kThreads) {
+      for (int i = threadIdx.x; i < H * R; i += kCThreads) {
         const int r = i / H, e = i - r * H;
         a.T[r * a.ldT + e] = WVec<WT>::round(a.T[r * a.ldT + e]);
       }
-      __syncthreads();
+      csync();
       const Slice sl = slice_of(2 * mi, rank, CL);
       const WT* w = b.take<WT>(size_t(sl.n()) * H);
       const int lo = min(sl.lo, mi), hi = min(sl.hi, mi), n = hi - lo;
@@ -1145,10 +1158,10 @@ struct Tower {
       const float* cs = b.take<float>(RM * 3 * n);
       const int ld = rup4(sl.n());
       gemv<WT>(w, H, H, sl.n(), a.T, a.ldT, R, a.stg, ld);
-      __syncthreads();
+      csync();
       // x rows: xm (rounded), xc = silu(conv(xm)); gate rows: xg (rounded)
       float* xcv = a.stg + RM * ld;  // [R][n] conv+SiLU of the x rows
-      for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+      for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
         const int r = i / sl.n(), e = i - r * sl.n(), idx = sl.lo + e;
         float v = WVec<WT>::round(a.stg[r * ld + e]);
         a.stg[r * ld + e] = v;
@@ -1163,10 +1176,10 @@ struct Tower {
           xcv[r * n + k] = siluf_(y);
         }
       }
-      __syncthreads();
+      csync();
       // q, k from xc and v from xm: 4x4 blocks (BlockLinear, model/modules.py:71-79)
       float* qkv = xcv + RM * rup4(n);  // [R][3][n]
-      for (int i = threadIdx.x; i < n * R; i += kThreads) {
+      for (int i = threadIdx.x; i < n * R; i += kCThreads) {
         const int r = i / n, k = i - r * n, q4 = k & ~3, o = k & 3;
         const float* xc = xcv + r * n + q4;
         const float* xm = a.stg + r * ld + (lo - sl.lo) + q4;
@@ -1181,7 +1194,7 @@ struct Tower {
         qkv[(r * 3 + 1) * n + k] = kv;
         qkv[(r * 3 + 2) * n + k] = vv;
       }
-      __syncthreads();
+      csync();
       if (n > 0) {
         bcast(xcv, n, n, R, a.V1, a.ld1, lo, CL);  // xc
         for (int t = 0; t < 3; ++t)  // q, k, v: row r of each at qkv + (3r + t) n
@@ -1190,7 +1203,7 @@ struct Tower {
       const int glo = max(sl.lo, mi), ghi = max(sl.hi, mi);
       if (ghi > glo) {  // gate rows -> xg at [mi, 2mi)
         cg::cluster_group cluster = cg::this_cluster();
-        for (int i = threadIdx.x; i < CL * R * (ghi - glo); i += kThreads) {
+        for (int i = threadIdx.x; i < CL * R * (ghi - glo); i += kCThreads) {
           const int peer = i / (R * (ghi - glo)), rem = i - peer * R * (ghi - glo), r = rem / (ghi - glo),
                     k = rem - r * (ghi - glo);
           *cluster.map_shared_rank(a.V1 + r * a.ld1 + glo + k, peer) = a.stg[r * ld + (glo - sl.lo) + k];
@@ -1224,32 +1237,32 @@ struct Tower {
         gf[r * 4 + 1] = expf(lf + mo - mn);
         gf[r * 4 + 2] = mn;
       }
-      __syncthreads();
+      csync();
       const float sq = sqrtf(float(hs_x));
-      for (int i = threadIdx.x; i < hs_x * R; i += kThreads) {
+      for (int i = threadIdx.x; i < hs_x * R; i += kCThreads) {
         const int r = i / hs_x, h = i - r * hs_x;
         const float k = a.V1[r * a.ld1 + 3 * mi + n * hs_x + h] / sq;  // k / sqrt(head_size) (xlstm.py:99)
         ks[r * hs_x + h] = k;
         nn[r * hs_x + h] = gf[r * 4 + 1] * nold[r * hs_x + h] + gf[r * 4 + 0] * k;
       }
-      __syncthreads();
-      for (int r = warp; r < R; r += kWarps) {
+      csync();
+      for (int r = warp; r < R; r += kCWarps) {
         float qn = 0.f;
         for (int h = lane; h < hs_x; h += 32) qn = fmaf(a.V1[r * a.ld1 + 2 * mi + n * hs_x + h], nn[r * hs_x + h], qn);
         qn = warp_sum(qn);
         if (lane == 0) gf[r * 4 + 3] = fmaxf(fabsf(qn), expf(-gf[r * 4 + 2])) + 1e-6f;  // xlstm.py:130-132
       }
       if (k0 == 0) {  // the head's first CTA writes n and m
-        for (int i = threadIdx.x; i < hs_x * R; i += kThreads) {
+        for (int i = threadIdx.x; i < hs_x * R; i += kCThreads) {
           const int r = i / hs_x, h = i - r * hs_x;
           L.st[7][slot[r] * L.ss[7] + n * hs_x + h] = nn[r * hs_x + h];
         }
         if (threadIdx.x < R) L.st[8][slot[threadIdx.x] * L.ss[8] + n] = gf[threadIdx.x * 4 + 2];
       }
-      __syncthreads();
+      csync();
       // C = f*C + (i*k) v; num = q.C per column (xlstm.py:108-118)
       float* out = a.stg + 2 * RM * hs_x + 4 * RM;
-      for (int pc = warp; pc < nc * R; pc += kWarps) {
+      for (int pc = warp; pc < nc * R; pc += kCWarps) {
         const int r = pc / nc, c = pc - r * nc, col = k0 + c;
         const float ig = gf[r * 4 + 0], fg = gf[r * 4 + 1];
         const float v = a.V1[r * a.ld1 + 4 * mi + n * hs_x + col];
@@ -1263,7 +1276,7 @@ struct Tower {
         num = warp_sum(num);
         if (lane == 0) out[r * nc + c] = num / gf[r * 4 + 3];  // xlstm.py:133
       }
-      __syncthreads();
+      csync();
       bcast(out, nc, nc, R, a.V2, a.ld2, sl.lo, CL);
       return;
     }
@@ -1272,23 +1285,23 @@ struct Tower {
     const float* ow = sv.p[1];
     const float* ob = sv.p[2];
     const float* skip = sv.p[3];
-    for (int i = threadIdx.x; i < mi * R; i += kThreads) {
+    for (int i = threadIdx.x; i < mi * R; i += kCThreads) {
       const int r = i / mi, e = i - r * mi, g = e / hs_x;
       const float y = (a.V2[r * a.ld2 + e] - a.gm[r * nh_x + g]) * a.gr[r * nh_x + g] * ow[e] + ob[e];
       const float* v1 = a.V1 + r * a.ld1;
       a.T[r * a.ldT + e] = WVec<WT>::round((y + skip[e] * v1[e]) * siluf_(v1[mi + e]));
     }
-    __syncthreads();
+    csync();
     const Slice sl = slice_of(H, rank, CL);
     const WT* w = b.take<WT>(size_t(sl.n()) * mi);
     const int ld = rup4(sl.n());
     gemv<WT>(w, mi, mi, sl.n(), a.T, a.ldT, R, a.stg, ld);
-    __syncthreads();
-    for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+    csync();
+    for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
       const int r = i / sl.n(), e = i - r * sl.n();
       a.stg[r * ld + e] = WVec<WT>::round(a.stg[r * ld + e]) + a.O1[r * a.ldH + sl.lo + e];
     }
-    __syncthreads();
+    csync();
     bcast(a.stg, ld, sl.n(), R, a.OUT2, a.ldH, sl.lo, CL);
   }
 
@@ -1298,22 +1311,22 @@ struct Tower {
     Bump b{buf};
     if (s == 0) {
       // input_up: relu(CastLinear(features)) (model/inference_model.py:88)
-      for (int i = threadIdx.x; i < R * fpad; i += kThreads) {
+      for (int i = threadIdx.x; i < R * fpad; i += kCThreads) {
         const int r = i / fpad, k = i - r * fpad;
         a.T[r * a.ldT + k] = k < F ? WVec<WT>::round(io.feats[r * F + k]) : 0.f;
       }
-      __syncthreads();
+      csync();
       const Slice sl = slice_of(P, rank, CL);
       const WT* w = b.take<WT>(sl.n() * fpadw());
       const WT* bias = b.take<WT>(sl.n());
       const int ld = rup4(sl.n());
       gemv<WT>(w, fpadw(), fpad, sl.n(), a.T, a.ldT, R, a.stg, ld);
-      __syncthreads();
-      for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+      csync();
+      for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
         const int r = i / sl.n(), e = i - r * sl.n();
         a.stg[r * ld + e] = fmaxf(WVec<WT>::round(a.stg[r * ld + e] + WVec<WT>::one(bias, e)), 0.f);
       }
-      __syncthreads();
+      csync();
       bcast(a.stg, ld, sl.n(), R, a.U1, a.ldP, sl.lo, CL);
       return;
     }
@@ -1324,12 +1337,12 @@ struct Tower {
       const WT* bias = b.take<WT>(sl.n());
       const int ld = rup4(sl.n());
       gemv<WT>(w, P, P, sl.n(), a.U1, a.ldP, R, a.stg, ld);
-      __syncthreads();
-      for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+      csync();
+      for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
         const int r = i / sl.n(), e = i - r * sl.n();
         a.stg[r * ld + e] = WVec<WT>::round(a.stg[r * ld + e] + WVec<WT>::one(bias, e));
       }
-      __syncthreads();
+      csync();
       bcast(a.stg, ld, sl.n(), R, a.X, a.ldH, sl.lo, CL);
       return;
     }
@@ -1341,11 +1354,11 @@ struct Tower {
       const float* xin = a.X;
       if (kind == kXLSTM) {
         layernorm(a.OUT2, a.ldH, H, R, v.p[1], 1e-5f, a.Xa, a.ldH, a.red);
-        for (int i = threadIdx.x; i < H * R; i += kThreads) {
+        for (int i = threadIdx.x; i < H * R; i += kCThreads) {
           const int r = i / H, e = i - r * H;
           a.Xa[r * a.ldH + e] = a.Xa[r * a.ldH + e] + a.X[r * a.ldH + e];  // y + x (inference_model.py:64)
         }
-        __syncthreads();
+        csync();
         xin = a.Xa;
       }
       rmsnorm<WT>(xin, a.ldH, H, R, v.p[0], kF32Eps, nullptr, 0, a.T, a.ldT, a.red);
@@ -1354,12 +1367,12 @@ struct Tower {
       const WT* bias = b.take<WT>(sl.n());
       const int ld = rup4(sl.n());
       gemv<WT>(w, H, H, sl.n(), a.T, a.ldT, R, a.stg, ld);
-      __syncthreads();
-      for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+      csync();
+      for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
         const int r = i / sl.n(), e = i - r * sl.n();
         a.stg[r * ld + e] = fmaxf(WVec<WT>::round(a.stg[r * ld + e] + WVec<WT>::one(bias, e)), 0.f);
       }
-      __syncthreads();
+      csync();
       bcast(a.stg, ld, sl.n(), R, a.Y, a.ldP, sl.lo, CL);
       return;
     }
@@ -1371,12 +1384,12 @@ struct Tower {
       const float* xres = kind == kXLSTM ? a.Xa : a.X;
       const int ld = rup4(sl.n());
       gemv<WT>(w, P, P, sl.n(), a.Y, a.ldP, R, a.stg, ld);
-      __syncthreads();
-      for (int i = threadIdx.x; i < sl.n() * R; i += kThreads) {
+      csync();
+      for (int i = threadIdx.x; i < sl.n() * R; i += kCThreads) {
         const int r = i / sl.n(), e = i - r * sl.n();
         a.stg[r * ld + e] = xres[r * a.ldH + sl.lo + e] + WVec<WT>::round(a.stg[r * ld + e] + WVec<WT>::one(bias, e));
       }
-      __syncthreads();
+      csync();
       bcast(a.stg, ld, sl.n(), R, a.X, a.ldH, sl.lo, CL);
       return;
     }
@@ -1389,9 +1402,10 @@ struct Tower {
   }
 };
 
-// One tower's whole step on its cluster: prefetch of stage s+1 (every thread's
-// share of 16- and 4-byte cp.async copies) while stage s runs, the stages
-// separated by cluster barriers, then output_proj of the tower's column.
+// One tower's whole step on its cluster: the producer warp copies stage s+1's
+// slice (16- and 4-byte cp.async) while the compute warps run stage s, the
+// stages separated by a CTA barrier and cluster barriers, then output_proj of
+// the tower's column.
 template <class WT, int KIND, int RT>
 __device__ __noinline__ void tower_main(const LatModel& M, const LatIO& io, uint8_t* smem, int rank, int CL) {
   Tower<WT, KIND, RT> tw(M, M.t[KIND], io, rank, CL, smem);
@@ -1400,39 +1414,53 @@ __device__ __noinline__ void tower_main(const LatModel& M, const LatIO& io, uint
   uint8_t* buf[2] = {smem + act_bytes, smem + act_bytes + buf_bytes};
   const int ns = tw.nstages();
   if (KIND == 0 && rank == 0 && threadIdx.x == 0 && io.err_out) *io.err_out = *M.err;
+  // the producer warp loads output_proj's weights and the first stage's slice
   if (rank == 0) pf1d(tw.a.OW, M.ow, tw.H * 4);
   tw.prefetch(0, buf[0]);
   cp_commit();
+  cp_wait_all();
+  __syncthreads();
   cluster_arrive();
 #ifdef B2E_LAT_TRACE
-  const bool tr = rank == 0 && threadIdx.x == 0;
+  // cluster rank 0's thread 0 (compute) and first producer lane stamp each stage
+  const bool trc = rank == 0 && threadIdx.x == 0, trp = rank == 0 && threadIdx.x == kCThreads;
   unsigned long long ts[kTraceFields] = {};
 #define B2E_STAMP(i) \
-  if (tr) ts[i] = gtime()
+  if (trc || trp) ts[i] = gtime()
 #else
 #define B2E_STAMP(i)
 #endif
+  const bool producer = threadIdx.x >= kCThreads;
   for (int s = 0; s < ns; ++s) {
     B2E_STAMP(0);
-    uint32_t nb = 0;
-    if (s + 1 < ns) nb = tw.prefetch(s + 1, buf[(s + 1) & 1]);
-    (void)nb;
-    cp_commit();
-    B2E_STAMP(1);
     cluster_wait();  // every CTA's outputs of stage s-1 are in this CTA's shared memory
-    B2E_STAMP(2);
-    cp_wait_prev();  // this CTA's loads for stage s have landed
-    __syncthreads();
+    B2E_STAMP(1);
+    uint32_t nb = 0;
+    if (producer) {
+      // the next stage's slice, beside this stage's work (its buffer was last
+      // read by stage s-1, finished before the barrier that ended it)
+      if (s + 1 < ns) nb = tw.prefetch(s + 1, buf[(s + 1) & 1]);
+      cp_commit();
+      cp_wait_all();
+    } else {
+      tw.run(s, buf[s & 1]);
+    }
+    (void)nb;
+    B2E_STAMP(2);     // compute: the stage's work done; producer: the copies landed
+    __syncthreads();  // both: stage s is complete here and stage s+1's copies are visible
     B2E_STAMP(3);
-    tw.run(s, buf[s & 1]);
-    __syncthreads();
-    B2E_STAMP(4);
     cluster_arrive();
-    B2E_STAMP(5);
+    B2E_STAMP(4);
 #ifdef B2E_LAT_TRACE
-    if (tr && s < kTraceStages) {
-      ts[6] = nb;  // bytes of stage s+1's copies
-      for (int f = 0; f < kTraceFields; ++f) g_lat_trace[KIND][s][f] = ts[f];
+    if (s < kTraceStages) {
+      unsigned long long* g = g_lat_trace[KIND][s];
+      if (trc) {
+        g[0] = ts[0]; g[1] = ts[1]; g[2] = ts[2]; g[4] = ts[3]; g[5] = ts[4];
+      }
+      if (trp) {
+        g[3] = ts[2];
+        g[6] = nb;  // bytes of stage s+1's copies
+      }
     }
 #endif
   }
@@ -1660,8 +1688,9 @@ void LatencyPath::launch(const LatIO& io, cudaStream_t s) const {
 
 #ifdef B2E_LAT_TRACE
 // Profiling build only: the last step's stage stamps, [4 towers][512 stages][8]
-// u64 (prefetch start, issued, cluster barrier passed, copies landed, run done,
-// arrived, next stage's bytes, 0); returns a cudaError_t.
+// u64 (stage start, cluster barrier passed, compute warps' work done, producer's
+// copies of the next stage landed, CTA barrier passed, arrived, next stage's
+// bytes, 0); returns a cudaError_t.
 extern "C" __attribute__((visibility("default"))) int b2e_lat_trace_read(void* host) {
   return int(cudaMemcpyFromSymbol(host, b2e::g_lat_trace, sizeof(b2e::g_lat_trace)));
 }
