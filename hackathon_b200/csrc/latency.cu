@@ -49,7 +49,8 @@ constexpr int kThreads = 288;
 constexpr int kWarps = kThreads / 32;
 // Warps 0-7 run the stages; warp 8 (the producer) issues the next stage's copies
 // meanwhile. Barriers inside a stage are over the compute warps only (named
-// barrier 1); the producer joins the CTA only at the stage's end (barrier 0).
+// barrier 1); the producer joins them only at the stage's end (the cluster
+// barrier).
 // Nine warps cap registers at 168 a thread (a few spill to the stack): measured
 // faster than eight compute warps without a producer (D1 one request 517 -> 461
 // us) and than seven compute warps with one (480 us).
@@ -1404,8 +1405,7 @@ struct Tower {
 
 // One tower's whole step on its cluster: the producer warp copies stage s+1's
 // slice (16- and 4-byte cp.async) while the compute warps run stage s, the
-// stages separated by a CTA barrier and cluster barriers, then output_proj of
-// the tower's column.
+// stages separated by cluster barriers, then output_proj of the tower's column.
 template <class WT, int KIND, int RT>
 __device__ __noinline__ void tower_main(const LatModel& M, const LatIO& io, uint8_t* smem, int rank, int CL) {
   Tower<WT, KIND, RT> tw(M, M.t[KIND], io, rank, CL, smem);
@@ -1446,9 +1446,12 @@ __device__ __noinline__ void tower_main(const LatModel& M, const LatIO& io, uint
       tw.run(s, buf[s & 1]);
     }
     (void)nb;
-    B2E_STAMP(2);     // compute: the stage's work done; producer: the copies landed
-    __syncthreads();  // both: stage s is complete here and stage s+1's copies are visible
+    B2E_STAMP(2);  // compute: the stage's work done; producer: the copies landed
     B2E_STAMP(3);
+    // Every thread of every CTA arrives (release) and, at the next stage's start,
+    // waits (acquire): this CTA's stage-s work and the producer's copies of stage
+    // s+1 are visible to all its threads then, and stage s's buffer is free for
+    // the copies of stage s+2. No CTA barrier is needed besides.
     cluster_arrive();
     B2E_STAMP(4);
 #ifdef B2E_LAT_TRACE

@@ -11,8 +11,8 @@
     python -m hackathon_b200.profiling latency-trace --preset D2
         the same steps through the trace build (lib/libb2e_trace.so): per tower
         and stage kind, the wait at the cluster barrier, the compute warps' work,
-        the producer warp's copies of the next stage (beside that work), the wait
-        at the CTA barrier for the later of the two, and the cluster arrive
+        the producer warp's copies of the next stage (beside that work), and the
+        cluster arrive
     python -m hackathon_b200.profiling launches <launch list csv>
         per-kernel launches, total time and share of an ncu launch list
     python -m hackathon_b200.profiling metrics <raw csv from ncu -i ... --page raw --csv>
@@ -225,7 +225,7 @@ def latency_trace(preset: str, reps: int, dtype: str) -> None:
     rc = _lib.lib().b2e_lat_trace_read(ctypes.c_void_p(buf.ctypes.data))
     assert rc == 0, f"b2e_lat_trace_read: cudaError {rc}"
     eng.close()
-    cols = ("cluster wait", "work", "next copies", "CTA wait", "arrive")
+    cols = ("cluster wait", "work", "next copies", "arrive")
     towers = ("xLSTM", "Mamba2", "RetNet", "Hawk")
     kinds = {0: ("A sLSTM", "B proj+qkv", "C mLSTM cell", "D down", "MLP1 fc1", "MLP2 fc2"),
              1: ("M1 proj+conv", "M2 ssm", "M3 out", "MLP1 fc1", "MLP2 fc2"),
@@ -236,10 +236,10 @@ def latency_trace(preset: str, reps: int, dtype: str) -> None:
         per = len(kinds[t])
         ns = 2 + cfg.tower_depth * per
         tr = buf[t, :ns].astype(np.int64)
-        # fields: 0 start, 1 cluster barrier passed, 2 work done, 3 copies landed,
-        # 4 CTA barrier passed, 5 arrived, 6 next stage's bytes
+        # fields: 0 start, 1 cluster barrier passed, 2 work done, 3 copies landed
+        # (producer), 4 arrive issued, 5 arrived, 6 next stage's bytes
         d = np.stack([tr[:, 1] - tr[:, 0], tr[:, 2] - tr[:, 1], tr[:, 3] - tr[:, 1],
-                      tr[:, 4] - np.maximum(tr[:, 2], tr[:, 3]), tr[:, 5] - tr[:, 4]], axis=1) / 1e3
+                      tr[:, 5] - tr[:, 4]], axis=1) / 1e3
         total = (tr[-1, 5] - tr[0, 0]) / 1e3
         print(f"{towers[t]}: {ns} stages, {total:.1f} us; mean " + ", ".join(f"{c} {d[:, i].mean():.2f}" for i, c in enumerate(cols)))
         for j in range(per):
