@@ -45,16 +45,17 @@ namespace {
 
 namespace cg = cooperative_groups;
 
-constexpr int kThreads = 288;
+constexpr int kCThreads = 256;  // compute warps
+constexpr int kPThreads = 64;   // producer warps
+constexpr int kThreads = kCThreads + kPThreads;
 constexpr int kWarps = kThreads / 32;
-// Warps 0-7 run the stages; warp 8 (the producer) issues the next stage's copies
-// meanwhile. Barriers inside a stage are over the compute warps only (named
-// barrier 1); the producer joins them only at the stage's end (the cluster
-// barrier).
-// Nine warps cap registers at 168 a thread (a few spill to the stack): measured
-// faster than eight compute warps without a producer (D1 one request 517 -> 461
-// us) and than seven compute warps with one (480 us).
-constexpr int kCThreads = kThreads - 32;
+// Warps 0-7 run the stages; warps 8-9 (the producer) issue the next stage's
+// copies meanwhile. Barriers inside a stage are over the compute warps only
+// (named barrier 1); the producer joins them only at the stage's end (the
+// cluster barrier). Ten warps cap registers at 168 a thread (a few spill to the
+// stack). Measured, one request at D1: 517 us with eight warps and no producer,
+// 480 us with seven compute warps and one producer warp, 458 us with eight and
+// one, 442 us with eight and two (three or four producer warps: no better).
 constexpr int kCWarps = kCThreads / 32;
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory"); }
 constexpr float kF32Eps = 1.1920928955078125e-07f;  // nn.RMSNorm(eps=None) in float32
@@ -100,7 +101,7 @@ __device__ __forceinline__ void pf2d(void* dst, const void* src, int rows, int r
   const int total = rows * per_row;
   const int pt = int(threadIdx.x) - kCThreads;
   if (pt < 0) return;
-  for (int i = pt; i < total; i += 32) {
+  for (int i = pt; i < total; i += kPThreads) {
     const int r = i / per_row, c = i - r * per_row;
     char* d = static_cast<char*>(dst) + size_t(r) * dst_stride + size_t(c) * unit;
     const char* s = static_cast<const char*>(src) + r * src_stride + size_t(c) * unit;
@@ -117,9 +118,9 @@ __device__ __forceinline__ void pf1d(void* dst, const void* src, int bytes) {
   char* d = static_cast<char*>(dst);
   const char* sp = static_cast<const char*>(src);
   if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | uintptr_t(bytes)) & 15) == 0) {
-    for (int i = pt * 16; i < bytes; i += 32 * 16) cp16(d + i, sp + i);
+    for (int i = pt * 16; i < bytes; i += kPThreads * 16) cp16(d + i, sp + i);
   } else {
-    for (int i = pt * 4; i < bytes; i += 32 * 4) cp4(d + i, sp + i);
+    for (int i = pt * 4; i < bytes; i += kPThreads * 4) cp4(d + i, sp + i);
   }
 }
 
