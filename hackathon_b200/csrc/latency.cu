@@ -314,9 +314,10 @@ __device__ __forceinline__ void rmsnorm(const float* x, int ld, int n, int R, co
   csync();
 }
 
-// LayerNorm rows (no bias): y = (x - mean) / sqrt(var + eps) * w.
-__device__ __forceinline__ void layernorm(const float* x, int ld, int n, int R, const float* w, float eps, float* y, int ldy,
-                          float* red) {
+// LayerNorm rows (no bias): y = (x - mean) / sqrt(var + eps) * w, handed to
+// put(r, i, y), which stores it (and whatever follows from it element-wise).
+template <class Put>
+__device__ __forceinline__ void layernorm_to(const float* x, int ld, int n, int R, const float* w, float eps, Put put, float* red) {
   float s[kLatMaxRows];
   row_sums(x, ld, n, R, [](float v, int) { return v; }, red, s);
   float mu[kLatMaxRows];
@@ -330,8 +331,13 @@ __device__ __forceinline__ void layernorm(const float* x, int ld, int n, int R, 
   for (int i = threadIdx.x; i < n; i += kCThreads)
 #pragma unroll
     for (int r = 0; r < kLatMaxRows; ++r)
-      if (r < R) y[r * ldy + i] = (x[r * ld + i] - mu[r]) * inv[r] * w[i];
+      if (r < R) put(r, i, (x[r * ld + i] - mu[r]) * inv[r] * w[i]);
   csync();
+}
+
+__device__ __forceinline__ void layernorm(const float* x, int ld, int n, int R, const float* w, float eps, float* y, int ldy,
+                          float* red) {
+  layernorm_to(x, ld, n, R, w, eps, [=](int r, int i, float v) { y[r * ldy + i] = v; }, red);
 }
 
 // Mean and 1/sqrt(var + eps) of G groups of gs values per row, one warp per
@@ -1143,12 +1149,9 @@ struct Tower {
         a.O1[r * a.ldH + e] = (y * gnw[e] + gnb[e]) + a.U0[r * a.ldH + e];
       }
       csync();
-      layernorm(a.O1, a.ldH, H, R, sv.p[3], 1e-5f, a.T, a.ldT, a.red);
-      for (int i = threadIdx.x; i < H * R; i += kCThreads) {
-        const int r = i / H, e = i - r * H;
-        a.T[r * a.ldT + e] = WVec<WT>::round(a.T[r * a.ldT + e]);
-      }
-      csync();
+      float* T = a.T;
+      const int ldT = a.ldT;
+      layernorm_to(a.O1, a.ldH, H, R, sv.p[3], 1e-5f, [=](int r, int e, float y) { T[r * ldT + e] = WVec<WT>::round(y); }, a.red);
       const Slice sl = slice_of(2 * mi, rank, CL);
       const WT* w = b.take<WT>(size_t(sl.n()) * H);
       const int lo = min(sl.lo, mi), hi = min(sl.hi, mi), n = hi - lo;
@@ -1355,12 +1358,11 @@ struct Tower {
       // MLP1: (xLSTM: X += LayerNorm(OUT2), xlstm.py:365) fc1 + ReLU on norm2(X) (inference_model.py:64-65)
       const float* xin = a.X;
       if (kind == kXLSTM) {
-        layernorm(a.OUT2, a.ldH, H, R, v.p[1], 1e-5f, a.Xa, a.ldH, a.red);
-        for (int i = threadIdx.x; i < H * R; i += kCThreads) {
-          const int r = i / H, e = i - r * H;
-          a.Xa[r * a.ldH + e] = a.Xa[r * a.ldH + e] + a.X[r * a.ldH + e];  // y + x (inference_model.py:64)
-        }
-        csync();
+        float* Xa = a.Xa;
+        const float* X = a.X;
+        const int ld = a.ldH;
+        // y + x (inference_model.py:64), rounded as a separate add after the norm
+        layernorm_to(a.OUT2, ld, H, R, v.p[1], 1e-5f, [=](int r, int e, float y) { Xa[r * ld + e] = __fadd_rn(y, X[r * ld + e]); }, a.red);
         xin = a.Xa;
       }
       rmsnorm<WT>(xin, a.ldH, H, R, v.p[0], kF32Eps, nullptr, 0, a.T, a.ldT, a.red);
