@@ -24,12 +24,14 @@ struct b2e_layer {
   StateArena arena;
   std::unique_ptr<Layer> layer;
   uint8_t* scratch = nullptr;
+  void* x_lp = nullptr;  // the step's input in the CastLinear type (low-precision weights only)
   int* d_n = nullptr;
   int* d_err = nullptr;
   ~b2e_layer() {
     cudaSetDevice(device);
     cudaDeviceSynchronize();
     if (scratch) cudaFree(scratch);
+    if (x_lp) cudaFree(x_lp);
     if (d_n) cudaFree(d_n);
   }
 };
@@ -115,6 +117,15 @@ __global__ void k_validate_slots(const int* slots, int n, int capacity, int* n_d
     *n_dev = bad ? 0 : n;
     if (bad) *err = 1;
   }
+}
+
+// x rounded to the CastLinear type, rows < *n_dev: the cast CastLinear.forward
+// applies to its input (example_model.py:93-94). A layer whose first projection
+// reads it runs that GEMM with same-type operands (the tensor-core path).
+__global__ void k_layer_in_lp(const float* x, int H, int lp, void* out, const int* n_dev) {
+  const long long total = (long long)(*n_dev) * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x)
+    store_as(lp, out, size_t(i), x[i]);
 }
 
 void check_cell(int batch, int heads, int a, int b) {
@@ -361,6 +372,8 @@ int b2e_layer_create(int32_t kind, const b2e_model_config* cfg, const b2e_engine
     h->arena.allocate(o.capacity);
     h->layer->resolve(h->pack, h->arena);
     B2E_CUDA(cudaMalloc(&h->scratch, h->layer->scratch_bytes(o.max_batch) + 256));
+    // the xLSTM layer's first projections read normalised rows it computes itself
+    if (o.lp != kF32 && kind != kXLSTM) B2E_CUDA(cudaMalloc(&h->x_lp, size_t(o.max_batch) * h->d.H * dtype_size(o.lp)));
     B2E_CUDA(cudaMalloc(&h->d_n, 16));
     h->d_err = h->d_n + 1;
     B2E_CUDA(cudaMemset(h->d_n, 0, 16));
@@ -380,7 +393,7 @@ int b2e_layer_step_device(b2e_layer* l, const int32_t* d_slots, const float* d_x
     B2E_CHECK(d_slots && d_x && d_y, kErrInvalid, "null device buffer");
     B2E_CUDA(cudaSetDevice(h.device));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    k_validate_slots<<<1, 256, 0, s>>>(d_slots, n, h.capacity, h.d_n, h.d_err);
+    k_validate_slots<<<1, 1024, 0, s>>>(d_slots, n, h.capacity, h.d_n, h.d_err);
     B2E_CUDA(cudaGetLastError());
     StepCtx c;
     c.s = s;
@@ -390,7 +403,12 @@ int b2e_layer_step_device(b2e_layer* l, const int32_t* d_slots, const float* d_x
     c.lp = h.lp;
     c.err = h.d_err;
     c.ln.pdl = c.ln_bulk.pdl = h.pdl;
-    h.layer->forward(c, d_x, nullptr, d_y, nullptr, h.scratch);
+    if (h.x_lp) {
+      const int blocks = std::max(1, std::min(ceil_div(long(n) * h.d.H, 256 * 4), 148 * 8));
+      k_layer_in_lp<<<blocks, 256, 0, s>>>(d_x, h.d.H, h.lp, h.x_lp, h.d_n);
+      B2E_CUDA(cudaGetLastError());
+    }
+    h.layer->forward(c, d_x, h.x_lp, d_y, nullptr, h.scratch);
   });
 }
 

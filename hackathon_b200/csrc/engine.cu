@@ -604,7 +604,7 @@ void Engine::step_device(const int* d_slots, const float* d_feats, int n, float*
   if (io.used) B2E_CUDA(cudaStreamWaitEvent(s, io.done, 0));
   B2E_CUDA(cudaMemcpyAsync(io.d_slots, d_slots, size_t(n) * 4, cudaMemcpyDeviceToDevice, s));
   B2E_CUDA(cudaMemcpyAsync(io.d_feats, d_feats, size_t(n) * d_.F * 4, cudaMemcpyDeviceToDevice, s));
-  k_validate<<<1, 256, 0, s>>>(io.d_slots, n, opt_.capacity, io.d_n, d_err_);
+  k_validate<<<1, 1024, 0, s>>>(io.d_slots, n, opt_.capacity, io.d_n, d_err_);
   B2E_CUDA(cudaGetLastError());
   launch(n, 0, s);
   B2E_CUDA(cudaMemcpyAsync(d_preds, io.d_preds, size_t(n) * 16, cudaMemcpyDeviceToDevice, s));
@@ -632,7 +632,7 @@ void Engine::submit_device(const int* d_slots, const float* d_feats, int n, floa
   if (!pipe || !last_pipelined_) order_after_last_step(s_head_);
   B2E_CUDA(cudaMemcpyAsync(io.d_slots, d_slots, size_t(n) * 4, cudaMemcpyDeviceToDevice, s_head_));
   B2E_CUDA(cudaMemcpyAsync(io.d_feats, d_feats, size_t(n) * d_.F * 4, cudaMemcpyDeviceToDevice, s_head_));
-  k_validate<<<1, 256, 0, s_head_>>>(io.d_slots, n, opt_.capacity, io.d_n, d_err_);
+  k_validate<<<1, 1024, 0, s_head_>>>(io.d_slots, n, opt_.capacity, io.d_n, d_err_);
   B2E_CUDA(cudaGetLastError());
   if (pipe) {
     launch_pipelined(n, b);

@@ -2,8 +2,9 @@
 
     python -m hackathon_b200.profiling cell --kind mamba2 --rows 4096 --heads 8 --sh 64 --sk 128
         run one state-step kernel `--reps` times on a dense state (for ncu -k)
-    python -m hackathon_b200.profiling layer --kind xlstm --rows 4096 --reps 4
-        one layer at the bench's dims `--reps` steps (its kernels, for ncu -k)
+    python -m hackathon_b200.profiling layer --kind xlstm --rows 4096 --reps 4 [--micro]
+        one layer at the bench's dims `--reps` steps (its kernels, for ncu -k);
+        --micro: BASELINE config 2 / 3's layer
     python -m hackathon_b200.profiling step --preset D2 --rows 2048 --reps 4
         the whole ensemble step on device buffers (its GEMMs, for ncu -k)
     python -m hackathon_b200.profiling latency --preset D2 --reps 8
@@ -109,10 +110,11 @@ def cell(kind: str, rows: int, heads: int, sh: int, sk: int, reps: int, waves: i
           f"state {state.numel() * 4 / 1e9:.2f} GB")
 
 
-def layer(kind: str, rows: int, reps: int, dtype: str) -> None:
+def layer(kind: str, rows: int, reps: int, dtype: str, micro: bool = False) -> None:
     """One layer (xlstm / mamba2 / retnet / hawk) at the bench's dims (D2), `reps`
     steps over `rows` rows with random slots: its kernels at their bench shapes,
-    with only that layer's state on the device."""
+    with only that layer's state on the device. micro: the layer of BASELINE
+    config 2 (mamba2) or 3 (retnet, xlstm) with its stated fills instead."""
     import numpy as np
     import torch
 
@@ -120,17 +122,21 @@ def layer(kind: str, rows: int, reps: int, dtype: str) -> None:
     from . import weights as W
     from .engine import LayerEngine
 
-    cfg = C.D2
+    if micro:
+        cfg, sd = W.micro_layer(kind, seed=0)
+    else:
+        cfg = C.D2
+        sd = W.generate(W.layer_specs(kind, "", cfg), seed=0)
     dev = torch.device("cuda", 0)
-    eng = LayerEngine(kind, cfg, W.generate(W.layer_specs(kind, "", cfg), seed=0), linear_dtype=dtype,
-                      capacity=rows, max_batch=rows)
+    eng = LayerEngine(kind, cfg, sd, linear_dtype=dtype, capacity=rows, max_batch=rows)
     slots = torch.from_numpy(np.random.default_rng(0).permutation(rows).astype(np.int32)).to(dev)
     x = torch.randn(rows, cfg.hidden_size, device=dev)
     y = torch.empty_like(x)
     for _ in range(reps):
         eng.step_device(slots, x, y)
     torch.cuda.synchronize()
-    print(f"{kind} layer at D2, rows={rows}: {reps} steps, state {eng.slot_bytes * rows / 1e9:.2f} GB")
+    dims = "its config's dims" if micro else "D2"
+    print(f"{kind} layer at {dims}, rows={rows}: {reps} steps, state {eng.slot_bytes * rows / 1e9:.2f} GB")
     eng.close()
 
 
@@ -271,6 +277,7 @@ def main(argv=None):
     la.add_argument("--rows", type=int, default=4096)
     la.add_argument("--reps", type=int, default=4)
     la.add_argument("--dtype", default="bf16")
+    la.add_argument("--micro", action="store_true", help="BASELINE config 2 / 3's layer (stated fills)")
     st = sub.add_parser("step")
     st.add_argument("--preset", default="D2")
     st.add_argument("--rows", type=int, default=2048)
@@ -292,7 +299,7 @@ def main(argv=None):
     elif a.cmd == "linear":
         linear(a.m, a.k, a.n, a.reps, a.dtype)
     elif a.cmd == "layer":
-        layer(a.kind, a.rows, a.reps, a.dtype)
+        layer(a.kind, a.rows, a.reps, a.dtype, a.micro)
     elif a.cmd == "step":
         step(a.preset, a.rows, a.reps, a.dtype)
     elif a.cmd == "latency":
