@@ -809,6 +809,9 @@ __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) 
 // row of the CTA; the weights are packed k-major ([2bs][4][H]) so a warp's 32
 // units read 128 contiguous bytes per gate and k, shared by the CTA's rows.
 constexpr int kSlRows = 16;
+// Rows per CTA at hidden <= 128, where a CTA is only H/32 <= 4 warps: more CTAs
+// of fewer rows keep more warps resident for the kernel's latency-bound phases.
+constexpr int kSlRowsNarrow = 8;
 // SLSTMCell.forward for one unit of one row (xlstm.py:247-262): gates i, f, z, o
 // in, (c, n, m) updated in place, h out. Out of line, so that the rows of a
 // k_slstm_fused CTA share one copy of the transcendental code.
@@ -927,7 +930,7 @@ __global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
   __syncthreads();  // xc, xn, hb are free
   {
     const float bi = p.bias[u], bf = p.bias[H + u], bz = p.bias[2 * H + u], bo = p.bias[3 * H + u];
-    constexpr int RC = 8;  // rows whose state loads are in flight together
+    constexpr int RC = RB < 8 ? RB : 8;  // rows whose state loads are in flight together
 #pragma unroll
     for (int rc = 0; rc < RB; rc += RC) {
       float co[RC], no[RC], mo[RC];
@@ -1398,16 +1401,19 @@ class XLSTMLayer : public Layer {
     B2E_CUDA(cudaFuncSetAttribute(k_mlstm_mid, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMidSmemMax)));
     // the fused sLSTM kernel: one thread per hidden unit, 16-byte activation
     // vectors inside a block, kSlRows rows of three activation planes in smem
-    fused_ = H_ % 32 == 0 && H_ >= kSlRows && H_ <= 512 && bs_ % 4 == 0 && nbl_ <= kSlMaxGroups &&
+    fused_ = H_ % 32 == 0 && H_ >= sl_rows() && H_ <= 512 && bs_ % 4 == 0 && nbl_ <= kSlMaxGroups &&
              fused_smem() <= kSlSmemMax;
     if (fused_) {
       B2E_CUDA(cudaFuncSetAttribute(k_slstm_fused<kSlRows, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(fused_smem())));
       B2E_CUDA(cudaFuncSetAttribute(k_slstm_fused<kSlRows, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(fused_smem())));
+      B2E_CUDA(cudaFuncSetAttribute(k_slstm_fused<kSlRowsNarrow, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(fused_smem())));
     }
   }
-  size_t fused_smem() const { return size_t(3) * kSlRows * H_ * sizeof(float); }
+  int sl_rows() const { return H_ <= 128 ? kSlRowsNarrow : kSlRows; }
+  size_t fused_smem() const { return size_t(3) * sl_rows() * H_ * sizeof(float); }
   void declare_state(StateArena& a) override {
     // (xlstm.py:331-336, 276-282, 232-236, 150-156) in init_state order
     l_sconv_ = a.add_conv(H_, 3);
@@ -1531,6 +1537,9 @@ class XLSTMLayer : public Layer {
                      swt_, sbias_, sgnw_, sgnb_, mlnw_, b.x1, b.xn2, lp_};
       if (H_ == 256)
         launch_k(c.ln, k_slstm_fused<kSlRows, 256>, dim3(ceil_div(c.rows, kSlRows)), dim3(H_), fused_smem(), c.s, fp);
+      else if (sl_rows() == kSlRowsNarrow)
+        launch_k(c.ln, k_slstm_fused<kSlRowsNarrow, 0>, dim3(ceil_div(c.rows, kSlRowsNarrow)), dim3(H_), fused_smem(),
+                 c.s, fp);
       else
         launch_k(c.ln, k_slstm_fused<kSlRows, 0>, dim3(ceil_div(c.rows, kSlRows)), dim3(H_), fused_smem(), c.s, fp);
     } else {
