@@ -827,6 +827,23 @@ __device__ __noinline__ float slstm_cell(float i, float f, float z, float o, flo
   return og * c / (n + 1e-6f);
 }
 constexpr int kSlMaxGroups = 16;  // sLSTM heads (GroupNorm groups) per row
+// The gate loop's operands in shared memory: rows 2q and 2q+1 of unit k side by
+// side, so one 64-bit load is the operand pair of an fma.rn.f32x2.
+__device__ __forceinline__ int sl_pair(int r, int k, int H) { return (((r >> 1) * H + k) << 1) + (r & 1); }
+__device__ __forceinline__ unsigned long long f32x2(float lo, float hi) {
+  unsigned long long v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+  return v;
+}
+__device__ __forceinline__ float2 f32x2_split(unsigned long long v) {
+  float2 f;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(v));
+  return f;
+}
+// d = a * b + d on both halves, each rounded as fmaf rounds it
+__device__ __forceinline__ void fma_f32x2(unsigned long long& d, unsigned long long a, unsigned long long b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
 constexpr size_t kSlSmemMax = 96 * 1024;
 struct SlstmFusedP {
   RowCtx rc;
@@ -849,9 +866,11 @@ __global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
   if (nr <= 0) return;
   extern __shared__ float4 sl_raw[];
   const int H = HT ? HT : p.H, u = threadIdx.x;  // blockDim.x == H
-  float* xc = reinterpret_cast<float*>(sl_raw);  // [RB][H] conv+SiLU branch, later the cell output y
-  float* xn = xc + RB * H;                       // [RB][H] input, then LayerNorm(input), later x1
-  float* hb = xn + RB * H;                       // [RB][H] old h
+  // three planes of RB x H floats: row-major [RB][H], except in the gate loop,
+  // whose operands are stored pair-interleaved (sl_pair)
+  float* xc = reinterpret_cast<float*>(sl_raw);  // conv+SiLU branch (pairs), later the cell output y
+  float* xn = xc + RB * H;                       // input, then LayerNorm(input) (pairs), later x1
+  float* hb = xn + RB * H;                       // old h (pairs)
   __shared__ float gm[RB * kSlMaxGroups], gr[RB * kSlMaxGroups];
   __shared__ long long slot[RB];
   if (u < RB) slot[u] = u < nr ? row_slot(p.rc, r0 + u) : 0;
@@ -875,17 +894,22 @@ __global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
       }
     }
     const float w0 = p.cw[u], w1 = p.cw[H + u], w2 = p.cw[2 * H + u], w3 = p.cw[3 * H + u], cb = p.cb[u], lw = p.lnw[u];
+    float xv[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) xv[r] = (xn[r * H + u] - gm[r]) * gr[r] * lw;
+    __syncthreads();  // every row-major input read before the pair-interleaved writes
 #pragma unroll
     for (int r = 0; r < RB; ++r) {
-      const float x = (xn[r * H + u] - gm[r]) * gr[r] * lw;
+      const float x = xv[r];
       // CausalConv1d over [state, x] (model/modules.py:37-41) and SiLU (xlstm.py:309-310)
       float acc = w0 * s0[r];
       acc = fmaf(w1, s1[r], acc);
       acc = fmaf(w2, s2[r], acc);
       acc = fmaf(w3, x, acc);
-      xc[r * H + u] = r < nr ? siluf_(acc + cb) : 0.f;
-      xn[r * H + u] = x;
-      hb[r * H + u] = ho[r];
+      const int ip = sl_pair(r, u, H);
+      xc[ip] = r < nr ? siluf_(acc + cb) : 0.f;
+      xn[ip] = x;
+      hb[ip] = ho[r];
       if (r < nr) {
         float* st = p.conv + slot[r] * p.cs;
         st[u] = s1[r];
@@ -897,18 +921,20 @@ __global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
   __syncthreads();
   // gates: acc[g][r] = sum_k W_g[u][k] * a_g[r][k] over k < bs (input half:
   // the conv branch for i, f, the normed input for z, o) and bs <= k < 2bs
-  // (the old h of u's block, all gates) (xlstm.py:250-253, 312-315)
+  // (the old h of u's block, all gates) (xlstm.py:250-253, 312-315). Rows 2q
+  // and 2q+1 of a gate are one f32x2 pair, updated by one fma.rn.f32x2 in the
+  // same order of k as one fmaf per row.
   const int bs = p.bs, j0 = (u / bs) * bs;
-  float acc[4][RB];
+  unsigned long long acc2[4][RB / 2];
 #pragma unroll
   for (int g = 0; g < 4; ++g)
 #pragma unroll
-    for (int r = 0; r < RB; ++r) acc[g][r] = 0.f;
+    for (int q = 0; q < RB / 2; ++q) acc2[g][q] = 0ull;  // (+0.f, +0.f)
   const float* wt = p.wt + u;
   const size_t kst = size_t(4) * H;  // one k of the packed weights
   for (int half = 0; half < 2; ++half) {
-    const float* a0 = (half ? hb : xc) + j0;
-    const float* a1 = (half ? hb : xn) + j0;
+    const unsigned long long* a0 = reinterpret_cast<const unsigned long long*>(half ? hb : xc) + j0;
+    const unsigned long long* a1 = reinterpret_cast<const unsigned long long*>(half ? hb : xn) + j0;
     const float* wk = wt + size_t(half) * bs * kst;
     for (int k = 0; k < bs; k += 4) {
       float w[4][4];  // [kk][gate]
@@ -917,13 +943,17 @@ __global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
 #pragma unroll
         for (int g = 0; g < 4; ++g) w[kk][g] = __ldg(wk + (k + kk) * kst + size_t(g) * H);
 #pragma unroll
-      for (int r = 0; r < RB; ++r) {
-        const float4 a = *reinterpret_cast<const float4*>(a0 + r * H + k);
-        const float4 b = *reinterpret_cast<const float4*>(a1 + r * H + k);
-        acc[0][r] = fmaf(a.w, w[3][0], fmaf(a.z, w[2][0], fmaf(a.y, w[1][0], fmaf(a.x, w[0][0], acc[0][r]))));
-        acc[1][r] = fmaf(a.w, w[3][1], fmaf(a.z, w[2][1], fmaf(a.y, w[1][1], fmaf(a.x, w[0][1], acc[1][r]))));
-        acc[2][r] = fmaf(b.w, w[3][2], fmaf(b.z, w[2][2], fmaf(b.y, w[1][2], fmaf(b.x, w[0][2], acc[2][r]))));
-        acc[3][r] = fmaf(b.w, w[3][3], fmaf(b.z, w[2][3], fmaf(b.y, w[1][3], fmaf(b.x, w[0][3], acc[3][r]))));
+      for (int kk = 0; kk < 4; ++kk) {
+        const unsigned long long wi = f32x2(w[kk][0], w[kk][0]), wf = f32x2(w[kk][1], w[kk][1]);
+        const unsigned long long wz = f32x2(w[kk][2], w[kk][2]), wo = f32x2(w[kk][3], w[kk][3]);
+#pragma unroll
+        for (int q = 0; q < RB / 2; ++q) {
+          const unsigned long long a = a0[size_t(q) * H + k + kk], b = a1[size_t(q) * H + k + kk];
+          fma_f32x2(acc2[0][q], a, wi);
+          fma_f32x2(acc2[1][q], a, wf);
+          fma_f32x2(acc2[2][q], b, wz);
+          fma_f32x2(acc2[3][q], b, wo);
+        }
       }
     }
   }
@@ -946,7 +976,11 @@ __global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
       for (int q = 0; q < RC; ++q) {
         const int r = rc + q;
         float cn = co[q], nv = no[q], mn = mo[q];
-        const float yv = slstm_cell(acc[0][r] + bi, acc[1][r] + bf, acc[2][r] + bz, acc[3][r] + bo, cn, nv, mn);
+        const float2 gi = f32x2_split(acc2[0][r >> 1]), gf = f32x2_split(acc2[1][r >> 1]);
+        const float2 gz = f32x2_split(acc2[2][r >> 1]), go = f32x2_split(acc2[3][r >> 1]);
+        const bool odd = r & 1;
+        const float yv = slstm_cell((odd ? gi.y : gi.x) + bi, (odd ? gf.y : gf.x) + bf, (odd ? gz.y : gz.x) + bz,
+                                    (odd ? go.y : go.x) + bo, cn, nv, mn);
         xc[r * H + u] = yv;
         if (r < nr) {
           p.cs_[slot[r] * p.c_s + u] = cn;
