@@ -1105,32 +1105,43 @@ __global__ void __launch_bounds__(kRowThreads, 3) k_mlstm_mid(const MlstmMidP p)
   }
   __syncthreads();
   // igate / fgate projections of cat(q, k, v) (xlstm.py:119-120): one warp per
-  // gate, its weight row in registers (U vectors per lane at a time) against
-  // every row of the CTA
+  // head, its igate and fgate weight rows in registers (UG vectors each per lane
+  // at a time), so each q/k/v vector read from shared memory feeds both gates,
+  // against every row of the CTA
+  constexpr int UG = U / 2;
   const int k4n = (3 * mi) >> 2;
-  for (int g = warp; g < 2 * nh; g += nw) {
-    const float4* w4 = reinterpret_cast<const float4*>(p.gw + size_t(g) * 3 * mi);
-    float acc[RM] = {0.f, 0.f, 0.f, 0.f};
-    for (int k0 = lane; k0 < k4n; k0 += 32 * U) {
-      float4 w[U];
+  for (int h = warp; h < nh; h += nw) {
+    const float4* wi4 = reinterpret_cast<const float4*>(p.gw + size_t(h) * 3 * mi);
+    const float4* wf4 = reinterpret_cast<const float4*>(p.gw + size_t(nh + h) * 3 * mi);
+    float ai[RM] = {0.f, 0.f, 0.f, 0.f}, af[RM] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = lane; k0 < k4n; k0 += 32 * UG) {
+      float4 wi[UG], wf[UG];
 #pragma unroll
-      for (int u = 0; u < U; ++u) w[u] = k0 + 32 * u < k4n ? __ldg(w4 + k0 + 32 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int u = 0; u < UG; ++u) {
+        const bool in = k0 + 32 * u < k4n;
+        wi[u] = in ? __ldg(wi4 + k0 + 32 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+        wf[u] = in ? __ldg(wf4 + k0 + 32 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
 #pragma unroll
       for (int rr = 0; rr < RM; ++rr) {
         if (rr >= nr) break;
         const float4* a = reinterpret_cast<const float4*>(smid + size_t(rr) * 3 * mi);
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
+        for (int u = 0; u < UG; ++u) {
           if (k0 + 32 * u >= k4n) break;
           const float4 x = a[k0 + 32 * u];
-          acc[rr] = fmaf(x.w, w[u].w, fmaf(x.z, w[u].z, fmaf(x.y, w[u].y, fmaf(x.x, w[u].x, acc[rr]))));
+          ai[rr] = fmaf(x.w, wi[u].w, fmaf(x.z, wi[u].z, fmaf(x.y, wi[u].y, fmaf(x.x, wi[u].x, ai[rr]))));
+          af[rr] = fmaf(x.w, wf[u].w, fmaf(x.z, wf[u].z, fmaf(x.y, wf[u].y, fmaf(x.x, wf[u].x, af[rr]))));
         }
       }
     }
 #pragma unroll
     for (int rr = 0; rr < RM; ++rr) {
-      const float v = warp_sum(acc[rr]);
-      if (lane == 0 && rr < nr) gpre[rr * 2 * nh + g] = v + p.gb[g];
+      const float vi = warp_sum(ai[rr]), vf = warp_sum(af[rr]);
+      if (lane == 0 && rr < nr) {
+        gpre[rr * 2 * nh + h] = vi + p.gb[h];
+        gpre[rr * 2 * nh + nh + h] = vf + p.gb[nh + h];
+      }
     }
   }
   __syncthreads();
