@@ -43,6 +43,11 @@ const char* layer_name(int kind) {
 namespace {
 
 constexpr int kRowThreads = 256;
+// Per-row kernels walk a row in chunks of kEU elements per thread and issue all
+// of a chunk's loads before its first store: a load placed after a store waits
+// for it (the compiler cannot tell the stores from the loads' sources), which
+// at hidden 2048 made a row loop a chain of one memory round trip per element.
+constexpr int kEU = 8;
 
 struct RowCtx {
   const int* n_dev;
@@ -109,13 +114,17 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const RmsP p) {
   const int n4 = p.H >> 2;
   constexpr int V = 16;  // rows of up to 32*V vectors (hidden 2048) stay in registers
   if (n4 <= 32 * V) {
-    // every load of the row in flight at once, one pass over memory
-    float4 v[V];
+    // every load of the row and of the weights in flight at once, before any
+    // store (a load after a store waits for it: the compiler cannot tell that
+    // the output does not alias the weights)
+    float4 v[V], wv[V];
     float ss = 0.f;
+    const float4* w4 = reinterpret_cast<const float4*>(p.w);
 #pragma unroll
     for (int t = 0; t < V; ++t) {
       const int i = lane + 32 * t;
       v[t] = i < n4 ? x[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      wv[t] = (i < n4 && w4) ? w4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
     }
 #pragma unroll
     for (int t = 0; t < V; ++t) ss = fmaf(v[t].x, v[t].x, fmaf(v[t].y, v[t].y, fmaf(v[t].z, v[t].z, fmaf(v[t].w, v[t].w, ss))));
@@ -125,7 +134,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const RmsP p) {
     for (int t = 0; t < V; ++t) {
       const int i = lane + 32 * t;
       if (i >= n4) break;
-      const float4 w = p.w ? reinterpret_cast<const float4*>(p.w)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+      const float4 w = wv[t];
       const float4 o = make_float4(v[t].x * inv * w.x, v[t].y * inv * w.y, v[t].z * inv * w.z, v[t].w * inv * w.w);
       if (p.out) reinterpret_cast<float4*>(p.out + size_t(r) * p.H)[i] = o;
       if (p.out_lp) {
@@ -739,14 +748,38 @@ __global__ void __launch_bounds__(kRowThreads) k_slstm_pre(const SlstmPreP p) {
   const float* h = p.h + slot * p.hst;
   float* axc = p.axc + size_t(r) * 2 * p.H;
   float* axn = p.axn + size_t(r) * 2 * p.H;
-  for (int c = threadIdx.x; c < p.H; c += blockDim.x) {
-    const float x = (t[c] - mu) * rs * p.lnw[c];
-    const float xc = siluf_(conv_step(p.cw, p.cb, st, p.H, c, x));  // conv + SiLU (xlstm.py:309-310)
-    const int j = c / p.bs, e = c - j * p.bs;
-    axc[j * 2 * p.bs + e] = xc;
-    axn[j * 2 * p.bs + e] = x;
-    axc[j * 2 * p.bs + p.bs + e] = h[c];
-    axn[j * 2 * p.bs + p.bs + e] = h[c];
+  const int H = p.H;
+  for (int c0 = threadIdx.x; c0 < H; c0 += kEU * blockDim.x) {
+    float tv[kEU], lw[kEU], s0[kEU], s1[kEU], s2[kEU], hv[kEU], w0[kEU], w1[kEU], w2[kEU], w3[kEU], cb[kEU];
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int c = c0 + u * blockDim.x;
+      if (c < H) {
+        tv[u] = t[c]; lw[u] = p.lnw[c]; hv[u] = h[c];
+        s0[u] = st[c]; s1[u] = st[H + c]; s2[u] = st[2 * H + c];
+        w0[u] = p.cw[c]; w1[u] = p.cw[H + c]; w2[u] = p.cw[2 * H + c]; w3[u] = p.cw[3 * H + c]; cb[u] = p.cb[c];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int c = c0 + u * blockDim.x;
+      if (c >= H) break;
+      const float x = (tv[u] - mu) * rs * lw[u];
+      // CausalConv1d over [state, x] (model/modules.py:37-41) + SiLU (xlstm.py:309-310)
+      float acc = w0[u] * s0[u];
+      acc = fmaf(w1[u], s1[u], acc);
+      acc = fmaf(w2[u], s2[u], acc);
+      acc = fmaf(w3[u], x, acc);
+      st[c] = s1[u];
+      st[H + c] = s2[u];
+      st[2 * H + c] = x;
+      const float xc = siluf_(acc + cb[u]);
+      const int j = c / p.bs, e = c - j * p.bs;
+      axc[j * 2 * p.bs + e] = xc;
+      axn[j * 2 * p.bs + e] = x;
+      axc[j * 2 * p.bs + p.bs + e] = hv[u];
+      axn[j * 2 * p.bs + p.bs + e] = hv[u];
+    }
   }
 }
 
@@ -771,34 +804,71 @@ __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) 
   float* cc = p.cs_ + slot * p.c_s;
   float* nn = p.ns_ + slot * p.n_s;
   float* mm = p.ms_ + slot * p.m_s;
-  for (int e = threadIdx.x; e < p.H; e += blockDim.x) {
-    // SLSTMCell.forward (xlstm.py:247-262)
-    const float i = G[e], f = G[p.H + e], z = G[2 * p.H + e], o = G[3 * p.H + e];
-    const float lfm = mm[e] + logsigmoidf_(f);
-    const float mn = fmaxf(i, lfm);
-    const float og = sigmoidf_(o);
-    const float ig = expf(i - mn);
-    const float fg = expf(lfm - mn);
-    const float cn = fg * cc[e] + ig * tanhf(z);
-    const float nv = fg * nn[e] + ig;
-    const float yv = og * cn / (nv + 1e-6f);
-    cc[e] = cn; nn[e] = nv; mm[e] = mn; hh[e] = yv;
-    y[e] = yv;
+  const int H = p.H;
+  for (int e0 = threadIdx.x; e0 < H; e0 += kEU * blockDim.x) {
+    float gi[kEU], gf[kEU], gz[kEU], go[kEU], mo[kEU], co[kEU], no[kEU];
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e < H) {
+        gi[u] = G[e]; gf[u] = G[H + e]; gz[u] = G[2 * H + e]; go[u] = G[3 * H + e];
+        mo[u] = mm[e]; co[u] = cc[e]; no[u] = nn[e];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e >= H) break;
+      // SLSTMCell.forward (xlstm.py:247-262)
+      const float lfm = mo[u] + logsigmoidf_(gf[u]);
+      const float mn = fmaxf(gi[u], lfm);
+      const float og = sigmoidf_(go[u]);
+      const float ig = expf(gi[u] - mn);
+      const float fg = expf(lfm - mn);
+      const float cn = fg * co[u] + ig * tanhf(gz[u]);
+      const float nv = fg * no[u] + ig;
+      const float yv = og * cn / (nv + 1e-6f);
+      cc[e] = cn; nn[e] = nv; mm[e] = mn; hh[e] = yv;
+      y[e] = yv;
+    }
   }
   __syncthreads();
-  group_stats(y, p.nbl, p.H / p.nbl, 1e-5f, gm, gr);  // GroupNorm(num_heads) (xlstm.py:300,316)
-  const float* t = p.t + size_t(r) * p.H;
-  const int gs = p.H / p.nbl;
-  for (int e = threadIdx.x; e < p.H; e += blockDim.x) {
-    const int g = e / gs;
-    const float v = (y[e] - gm[g]) * gr[g] * p.gnw[e] + p.gnb[e] + t[e];  // + skip (xlstm.py:318)
-    x1[e] = v;
-    p.x1[size_t(r) * p.H + e] = v;
+  group_stats(y, p.nbl, H / p.nbl, 1e-5f, gm, gr);  // GroupNorm(num_heads) (xlstm.py:300,316)
+  const float* t = p.t + size_t(r) * H;
+  const int gs = H / p.nbl;
+  for (int e0 = threadIdx.x; e0 < H; e0 += kEU * blockDim.x) {
+    float gw[kEU], gb[kEU], tv[kEU];
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e < H) { gw[u] = p.gnw[e]; gb[u] = p.gnb[e]; tv[u] = t[e]; }
+    }
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e >= H) break;
+      const int g = e / gs;
+      const float v = (y[e] - gm[g]) * gr[g] * gw[u] + gb[u] + tv[u];  // + skip (xlstm.py:318)
+      x1[e] = v;
+      p.x1[size_t(r) * H + e] = v;
+    }
   }
   __syncthreads();
-  group_stats(x1, 1, p.H, 1e-5f, gm, gr);  // mLSTM block LayerNorm (xlstm.py:182,202)
-  for (int e = threadIdx.x; e < p.H; e += blockDim.x)
-    store_as(p.at, p.xn2, size_t(r) * p.H + e, (x1[e] - gm[0]) * gr[0] * p.mlnw[e]);
+  group_stats(x1, 1, H, 1e-5f, gm, gr);  // mLSTM block LayerNorm (xlstm.py:182,202)
+  for (int e0 = threadIdx.x; e0 < H; e0 += kEU * blockDim.x) {
+    float mw[kEU];
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e < H) mw[u] = p.mlnw[e];
+    }
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e >= H) break;
+      store_as(p.at, p.xn2, size_t(r) * H + e, (x1[e] - gm[0]) * gr[0] * mw[u]);
+    }
+  }
 }
 
 // The whole sLSTM block for kSlRows rows per CTA (xlstm.py:239-318) and the
@@ -1380,6 +1450,7 @@ __global__ void __launch_bounds__(kRowThreads) k_mlstm_post(const MlstmPostP p) 
 // lane, so GroupNorm's sums close with warp shuffles, with no shared memory,
 // barrier or per-element division of indices. Heads of up to 512 columns.
 constexpr int kPostWarps = 8;  // warps per CTA
+template <int TM>  // columns per lane at most (hs <= 32 * TM)
 __global__ void __launch_bounds__(256) k_mlstm_post_w(const MlstmPostP p) {
   pdl_wait();
   const int w = blockIdx.x * kPostWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -1392,29 +1463,37 @@ __global__ void __launch_bounds__(256) k_mlstm_post_w(const MlstmPostP p) {
   {
     const float den = p.den[size_t(r) * p.nh + g];
     const int e0 = g * hs + lane;
-    float o[16];
+    // every operand of the head's columns loaded before the first store
+    float o[TM], gw[TM], gb[TM], sk[TM], xc[TM], xg2[TM];
+#pragma unroll
+    for (int t = 0; t < TM; ++t)
+      if (t < T) {
+        const int e = e0 + 32 * t;
+        o[t] = num[e];
+        gw[t] = p.gnw[e]; gb[t] = p.gnb[e]; sk[t] = p.skip[e]; xc[t] = xca[e]; xg2[t] = xg[e];
+      }
     float s = 0.f;
 #pragma unroll
-    for (int t = 0; t < 16; ++t)
+    for (int t = 0; t < TM; ++t)
       if (t < T) {
-        o[t] = num[e0 + 32 * t] / den;  // xlstm.py:133
+        o[t] = o[t] / den;  // xlstm.py:133
         s += o[t];
       }
     const float mu = warp_sum(s) / float(hs);
     float q = 0.f;
 #pragma unroll
-    for (int t = 0; t < 16; ++t)
+    for (int t = 0; t < TM; ++t)
       if (t < T) {
         const float d = o[t] - mu;
         q = fmaf(d, d, q);
       }
     const float rs = 1.0f / sqrtf(warp_sum(q) / float(hs) + 1e-5f);  // outnorm GroupNorm (xlstm.py:135)
 #pragma unroll
-    for (int t = 0; t < 16; ++t)
+    for (int t = 0; t < TM; ++t)
       if (t < T) {
         const int e = e0 + 32 * t;
-        const float on = (o[t] - mu) * rs * p.gnw[e] + p.gnb[e];
-        store_as(p.at, p.A, size_t(r) * mi + e, (on + p.skip[e] * xca[e]) * siluf_(xg[e]));  // xlstm.py:215-216
+        const float on = (o[t] - mu) * rs * gw[t] + gb[t];
+        store_as(p.at, p.A, size_t(r) * mi + e, (on + sk[t] * xc[t]) * siluf_(xg2[t]));  // xlstm.py:215-216
       }
   }
 }
@@ -1432,9 +1511,23 @@ __global__ void __launch_bounds__(kRowThreads) k_xlstm_final(const XFinalP p) {
   for (int e = threadIdx.x; e < p.H; e += blockDim.x) x[e] = p.x2[size_t(r) * p.H + e];
   __syncthreads();
   group_stats(x, 1, p.H, 1e-5f, gm, gr);  // final LayerNorm (xlstm.py:365)
-  for (int e = threadIdx.x; e < p.H; e += blockDim.x) {
-    const float y = (x[e] - gm[0]) * gr[0] * p.w[e];
-    p.out[size_t(r) * p.H + e] = p.res ? p.res[size_t(r) * p.H + e] + y : y;
+  for (int e0 = threadIdx.x; e0 < p.H; e0 += kEU * blockDim.x) {
+    float wv[kEU], rv[kEU];
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e < p.H) {
+        wv[u] = p.w[e];
+        rv[u] = p.res ? p.res[size_t(r) * p.H + e] : 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e >= p.H) break;
+      const float y = (x[e] - gm[0]) * gr[0] * wv[u];
+      p.out[size_t(r) * p.H + e] = p.res ? rv[u] + y : y;
+    }
   }
 }
 
@@ -1637,10 +1730,20 @@ class XLSTMLayer : public Layer {
     op.err = c.err;
     outer_rows(op, c.rows, c.s, c.ln_bulk);
     MlstmPostP pp{rc, b.num, b.den, b.xca, b.proj, mi_, nh_, ongw_, ongb_, skip_, b.A, lp_};
-    if (hs_ % 32 == 0 && hs_ <= 512)
-      launch_k(c.ln, k_mlstm_post_w, dim3(ceil_div(c.rows * nh_, kPostWarps)), dim3(256), 0, c.s, pp);
-    else
+    if (hs_ % 32 == 0 && hs_ <= 512) {
+      const dim3 pg(ceil_div(c.rows * nh_, kPostWarps));
+      const int T = hs_ / 32;
+      if (T <= 2)
+        launch_k(c.ln, k_mlstm_post_w<2>, pg, dim3(256), 0, c.s, pp);
+      else if (T <= 4)
+        launch_k(c.ln, k_mlstm_post_w<4>, pg, dim3(256), 0, c.s, pp);
+      else if (T <= 8)
+        launch_k(c.ln, k_mlstm_post_w<8>, pg, dim3(256), 0, c.s, pp);
+      else
+        launch_k(c.ln, k_mlstm_post_w<16>, pg, dim3(256), 0, c.s, pp);
+    } else {
       launch_k(c.ln, k_mlstm_post, dim3(c.rows), dim3(kRowThreads), mi_ * sizeof(float), c.s, pp);
+    }
     if (post) {
       // proj_down + skip, final LayerNorm, Block residual and the Block's norm2,
       // all in the GEMM epilogue (xlstm.py:217-219, 365; inference_model.py:65-67)

@@ -61,10 +61,13 @@ WeightPack::~WeightPack() {
 }
 
 size_t WeightPack::reserve(size_t bytes, std::function<void(uint8_t*)> fill) {
-  total_ = (total_ + 255) & ~size_t(255);
-  const size_t off = total_;
+  B2E_CHECK(dev_ == nullptr, kErrInternal, "weights reserved after upload");
+  const bool small = bytes <= kSmallEntry;
+  size_t& region = small ? small_total_ : total_;
+  region = (region + 255) & ~size_t(255);
+  const size_t off = region | (small ? kSmallTag : 0);
   entries_.push_back({off, bytes, std::move(fill)});
-  total_ += bytes;
+  region += bytes;
   return off;
 }
 
@@ -94,9 +97,12 @@ size_t WeightPack::add_conv(const float* src, int channels, int taps) {
 
 void WeightPack::upload() {
   B2E_CHECK(dev_ == nullptr, kErrInternal, "weights uploaded twice");
-  const size_t total = std::max<size_t>(total_, 256);
+  constexpr size_t kPage = size_t(2) << 20;
+  big_base_ = (small_total_ + kPage - 1) / kPage * kPage;
+  const size_t total = std::max<size_t>(big_base_ + total_, 256);
   std::vector<uint8_t> host(total, 0);
-  for (auto& e : entries_) e.fill(host.data() + e.off);
+  for (auto& e : entries_)
+    e.fill(host.data() + ((e.off & kSmallTag) ? (e.off & ~kSmallTag) : big_base_ + e.off));
   B2E_CUDA(cudaMalloc(&dev_, total));
   B2E_CUDA(cudaMemcpy(dev_, host.data(), total, cudaMemcpyHostToDevice));
   entries_.clear();

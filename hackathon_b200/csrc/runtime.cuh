@@ -35,9 +35,17 @@ class WeightSource {
 
 // One device allocation holding every packed weight. Entries are planned with a
 // fill callback, then filled into a single host buffer and uploaded in one copy.
+// Entries of at most kSmallEntry bytes (norm weights, biases, conv taps, the 4x4
+// BlockLinears) are packed together at the start of the allocation, the matrices
+// after them from the next 2 MiB boundary. A step streams every matrix once,
+// which evicts the GPU's address translations of the pages it passes; the small
+// entries, which every per-row kernel reads, then share a few pages of their
+// own instead of one page next to each matrix.
 class WeightPack {
  public:
+  static constexpr size_t kSmallEntry = 256 * 1024;
   ~WeightPack();
+  // Returns the entry's offset, resolved by ptr() once upload() has run.
   size_t reserve(size_t bytes, std::function<void(uint8_t*)> fill);
   // Convenience packers (src is f32; `t` is the stored type).
   size_t add(const float* src, size_t n, int t);
@@ -45,16 +53,21 @@ class WeightPack {
   size_t add_conv(const float* src, int channels, int taps);  // (C,1,taps) -> (taps, C)
   void upload();
   template <class T = void>
-  T* ptr(size_t off) const { return reinterpret_cast<T*>(dev_ + off); }
-  size_t bytes() const { return total_; }
+  T* ptr(size_t off) const {
+    return reinterpret_cast<T*>(dev_ + ((off & kSmallTag) ? (off & ~kSmallTag) : big_base_ + off));
+  }
+  size_t bytes() const { return big_base_ + total_; }
 
  private:
+  static constexpr size_t kSmallTag = size_t(1) << 62;  // offset bit: the entry is in the small region
   struct Entry {
     size_t off, bytes;
     std::function<void(uint8_t*)> fill;
   };
   std::vector<Entry> entries_;
-  size_t total_ = 0;
+  size_t total_ = 0;        // bytes of the matrix region
+  size_t small_total_ = 0;  // bytes of the small region
+  size_t big_base_ = 0;     // where the matrix region starts (set by upload)
   uint8_t* dev_ = nullptr;
 };
 
