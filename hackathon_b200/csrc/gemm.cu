@@ -168,6 +168,32 @@ __global__ void __launch_bounds__(TPB) gemm_tiled(const __grid_constant__ GemmPa
   }
 }
 
+// U consecutive 128-wide K steps of one W row at lane offset k: the U weight
+// loads are issued together, then each row's accumulator takes the steps in
+// increasing k (the same order of fmas whatever U is).
+template <int AT, int WT, int MM, int U>
+__device__ __forceinline__ void skinny_steps(const GemmParams& p, const GemmGroup& g, size_t wrow, int k, int M,
+                                             float (&acc)[MM]) {
+  constexpr bool round_a = (AT == kF32 && WT != kF32);
+  float4 w[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) w[u] = load4_vec<WT>(g.W, wrow + k + u * 128);
+#pragma unroll
+  for (int r = 0; r < MM; ++r) {
+    if (r < M) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float4 a = load4_vec<AT>(g.A, size_t(r) * p.lda + k + u * 128);
+        if (round_a) a = round4<WT>(a);
+        acc[r] = fmaf(a.x, w[u].x, acc[r]);
+        acc[r] = fmaf(a.y, w[u].y, acc[r]);
+        acc[r] = fmaf(a.z, w[u].z, acc[r]);
+        acc[r] = fmaf(a.w, w[u].w, acc[r]);
+      }
+    }
+  }
+}
+
 // One warp per output column; MM = accumulators per lane (>= live rows).
 template <int AT, int WT, int MM>
 __global__ void __launch_bounds__(256) gemm_skinny(const __grid_constant__ GemmParams p, bool vec) {
@@ -187,41 +213,12 @@ __global__ void __launch_bounds__(256) gemm_skinny(const __grid_constant__ GemmP
     for (int r = 0; r < MM; ++r) acc[r] = 0.f;
     const size_t wrow = size_t(n) * p.ldw;
     if (vec) {
-      // 4 elements per lane per step; 4 steps in flight.
+      // 4 elements per lane per step: 16 steps in flight (a 2048-wide row in
+      // one round trip to memory), then 4, then 1
       int k = lane * 4;
-      for (; k + 3 * 128 + 3 < p.K; k += 4 * 128) {
-        float4 w[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) w[u] = load4_vec<WT>(g.W, wrow + k + u * 128);
-#pragma unroll
-        for (int r = 0; r < MM; ++r) {
-          if (r < M) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              float4 a = load4_vec<AT>(g.A, size_t(r) * p.lda + k + u * 128);
-              if (round_a) a = round4<WT>(a);
-              acc[r] = fmaf(a.x, w[u].x, acc[r]);
-              acc[r] = fmaf(a.y, w[u].y, acc[r]);
-              acc[r] = fmaf(a.z, w[u].z, acc[r]);
-              acc[r] = fmaf(a.w, w[u].w, acc[r]);
-            }
-          }
-        }
-      }
-      for (; k + 3 < p.K; k += 128) {
-        const float4 w = load4_vec<WT>(g.W, wrow + k);
-#pragma unroll
-        for (int r = 0; r < MM; ++r) {
-          if (r < M) {
-            float4 a = load4_vec<AT>(g.A, size_t(r) * p.lda + k);
-            if (round_a) a = round4<WT>(a);
-            acc[r] = fmaf(a.x, w.x, acc[r]);
-            acc[r] = fmaf(a.y, w.y, acc[r]);
-            acc[r] = fmaf(a.z, w.z, acc[r]);
-            acc[r] = fmaf(a.w, w.w, acc[r]);
-          }
-        }
-      }
+      for (; k + 15 * 128 + 3 < p.K; k += 16 * 128) skinny_steps<AT, WT, MM, 16>(p, g, wrow, k, M, acc);
+      for (; k + 3 * 128 + 3 < p.K; k += 4 * 128) skinny_steps<AT, WT, MM, 4>(p, g, wrow, k, M, acc);
+      for (; k + 3 < p.K; k += 128) skinny_steps<AT, WT, MM, 1>(p, g, wrow, k, M, acc);
     } else {
       for (int k = lane; k < p.K; k += 32) {
         const float w = load1<WT>(g.W, wrow + k);
