@@ -208,6 +208,84 @@ struct Mamba2PreP {
 // and inputs are loaded before any is updated (one round trip to memory per
 // phase), conv and dt weights are shared by the CTA's rows.
 constexpr int kM2Rows = 4;
+// Conv + SiLU of channel i (< mi + 2bc: x, then b, then c) for rows r0.. of the
+// row group (mamba2.py:84-89).
+__device__ __forceinline__ void m2_conv_channel(const Mamba2PreP& p, int i, int r0, int nr, const long long* sslot) {
+  constexpr int RM = kM2Rows;
+  const int mi = p.mi, bc = p.bc;
+  const bool isx = i < mi, isb = !isx && i < mi + bc;
+  const int c = isx ? i : (isb ? i - mi : i - mi - bc), C = isx ? mi : bc;
+  float* base = isx ? p.xconv : (isb ? p.bconv : p.cconv);
+  const long long cs = isx ? p.xcs : (isb ? p.bcs : p.ccs);
+  const float* w = isx ? p.wx : (isb ? p.wb : p.wc);
+  const float* bias = isx ? p.bx : (isb ? p.bb : p.bcv);
+  float* out = isx ? p.xs : (isb ? p.bs : p.cs);
+  const int pi = isx ? i : mi + i;  // the proj row is [x | z | b | c]: b and c sit after z
+  float s0[RM], s1[RM], s2[RM], xv[RM];
+#pragma unroll
+  for (int rr = 0; rr < RM; ++rr) {
+    if (rr < nr) {
+      const float* st = base + sslot[rr] * cs;
+      s0[rr] = st[c];
+      s1[rr] = st[C + c];
+      s2[rr] = st[2 * C + c];
+      xv[rr] = p.proj[size_t(r0 + rr) * p.ldp + pi];
+    }
+  }
+  const float w0 = w[c], w1 = w[C + c], w2 = w[2 * C + c], w3 = w[3 * C + c], b0 = bias[c];
+#pragma unroll
+  for (int rr = 0; rr < RM; ++rr) {
+    if (rr < nr) {
+      // CausalConv1d over [state, x] (model/modules.py:37-41)
+      float acc = w0 * s0[rr];
+      acc = fmaf(w1, s1[rr], acc);
+      acc = fmaf(w2, s2[rr], acc);
+      acc = fmaf(w3, xv[rr], acc);
+      float* st = base + sslot[rr] * cs;
+      st[c] = s1[rr];
+      st[C + c] = s2[rr];
+      st[2 * C + c] = xv[rr];
+      out[size_t(r0 + rr) * C + c] = siluf_(acc + b0);
+    }
+  }
+}
+// dt = softplus(dt_proj(t)); decay = exp(a * dt) (mamba2.py:81, 92-97) of head
+// h by one warp for the row group: lanes stride the weight row, KC loads of it
+// (and of each row's input) in flight before they are summed, in k order.
+template <int KC>
+__device__ __forceinline__ void m2_dt_head(const Mamba2PreP& p, int h, int r0, int nr, int lane) {
+  constexpr int RM = kM2Rows;
+  const float* w = p.dtw + size_t(h) * p.H;
+  float acc[RM];
+#pragma unroll
+  for (int rr = 0; rr < RM; ++rr) acc[rr] = 0.f;
+  for (int k0 = lane; k0 < p.H; k0 += 32 * KC) {
+    float wv[KC], tv[RM][KC];
+#pragma unroll
+    for (int u = 0; u < KC; ++u) {
+      const int k = k0 + 32 * u;
+      wv[u] = k < p.H ? w[k] : 0.f;
+#pragma unroll
+      for (int rr = 0; rr < RM; ++rr) tv[rr][u] = (rr < nr && k < p.H) ? p.tin[size_t(r0 + rr) * p.H + k] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < KC; ++u) {
+      if (k0 + 32 * u >= p.H) break;
+#pragma unroll
+      for (int rr = 0; rr < RM; ++rr)
+        if (rr < nr) acc[rr] = fmaf(tv[rr][u], wv[u], acc[rr]);
+    }
+  }
+#pragma unroll
+  for (int rr = 0; rr < RM; ++rr) {
+    const float v = warp_sum(acc[rr]);
+    if (lane == 0 && rr < nr) {
+      const float d = softplusf_(v + p.dtb[h]);
+      p.dt[size_t(r0 + rr) * p.nh + h] = d;
+      p.dc[size_t(r0 + rr) * p.nh + h] = expf(p.a[h] * d);
+    }
+  }
+}
 __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre_rows(const Mamba2PreP p) {
   pdl_wait();
   constexpr int RM = kM2Rows;
@@ -217,68 +295,31 @@ __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre_rows(const Mamba2Pre
   __shared__ long long sslot[RM];
   if (threadIdx.x < nr) sslot[threadIdx.x] = row_slot(p.rc, r0 + threadIdx.x);
   __syncthreads();
-  const int mi = p.mi, bc = p.bc;
-  // convs + SiLU (mamba2.py:84-89): channel i < mi of x, then bc of b, bc of c
-  for (int i = threadIdx.x; i < mi + 2 * bc; i += blockDim.x) {
-    const bool isx = i < mi, isb = !isx && i < mi + bc;
-    const int c = isx ? i : (isb ? i - mi : i - mi - bc), C = isx ? mi : bc;
-    float* base = isx ? p.xconv : (isb ? p.bconv : p.cconv);
-    const long long cs = isx ? p.xcs : (isb ? p.bcs : p.ccs);
-    const float* w = isx ? p.wx : (isb ? p.wb : p.wc);
-    const float* bias = isx ? p.bx : (isb ? p.bb : p.bcv);
-    float* out = isx ? p.xs : (isb ? p.bs : p.cs);
-    const int pi = isx ? i : mi + i;  // the proj row is [x | z | b | c]: b and c sit after z
-    float s0[RM], s1[RM], s2[RM], xv[RM];
-#pragma unroll
-    for (int rr = 0; rr < RM; ++rr) {
-      if (rr < nr) {
-        const float* st = base + sslot[rr] * cs;
-        s0[rr] = st[c];
-        s1[rr] = st[C + c];
-        s2[rr] = st[2 * C + c];
-        xv[rr] = p.proj[size_t(r0 + rr) * p.ldp + pi];
-      }
-    }
-    const float w0 = w[c], w1 = w[C + c], w2 = w[2 * C + c], w3 = w[3 * C + c], b0 = bias[c];
-#pragma unroll
-    for (int rr = 0; rr < RM; ++rr) {
-      if (rr < nr) {
-        // CausalConv1d over [state, x] (model/modules.py:37-41)
-        float acc = w0 * s0[rr];
-        acc = fmaf(w1, s1[rr], acc);
-        acc = fmaf(w2, s2[rr], acc);
-        acc = fmaf(w3, xv[rr], acc);
-        float* st = base + sslot[rr] * cs;
-        st[c] = s1[rr];
-        st[C + c] = s2[rr];
-        st[2 * C + c] = xv[rr];
-        out[size_t(r0 + rr) * C + c] = siluf_(acc + b0);
-      }
-    }
-  }
-  // dt = softplus(dt_proj(t)); decay = exp(a * dt) (mamba2.py:81, 92-97): one
-  // warp per head, its weight row read once for the CTA's rows
+  for (int i = threadIdx.x; i < p.mi + 2 * p.bc; i += blockDim.x) m2_conv_channel(p, i, r0, nr, sslot);
   const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int h = threadIdx.x >> 5; h < p.nh; h += nw) {
-    const float* w = p.dtw + size_t(h) * p.H;
-    float acc[RM];
-#pragma unroll
-    for (int rr = 0; rr < RM; ++rr) acc[rr] = 0.f;
-    for (int k = lane; k < p.H; k += 32) {
-      const float wk = w[k];
-#pragma unroll
-      for (int rr = 0; rr < RM; ++rr)
-        if (rr < nr) acc[rr] = fmaf(p.tin[size_t(r0 + rr) * p.H + k], wk, acc[rr]);
-    }
-#pragma unroll
-    for (int rr = 0; rr < RM; ++rr) {
-      const float v = warp_sum(acc[rr]);
-      if (lane == 0 && rr < nr) {
-        const float d = softplusf_(v + p.dtb[h]);
-        p.dt[size_t(r0 + rr) * p.nh + h] = d;
-        p.dc[size_t(r0 + rr) * p.nh + h] = expf(p.a[h] * d);
-      }
-    }
+  for (int h = threadIdx.x >> 5; h < p.nh; h += nw) m2_dt_head<4>(p, h, r0, nr, lane);
+}
+// The same for steps of few rows, where one CTA per row group leaves most SMs
+// idle: CTAs x < m2_conv_ctas convolve kRowThreads channels each, the rest
+// compute dt for one head per warp; grid y = row groups.
+constexpr int kM2SplitRows = 64;  // steps up to this many rows take k_mamba2_pre_split
+__host__ __device__ inline int m2_conv_ctas(int mi, int bc) { return (mi + 2 * bc + kRowThreads - 1) / kRowThreads; }
+__global__ void __launch_bounds__(kRowThreads) k_mamba2_pre_split(const Mamba2PreP p) {
+  pdl_wait();
+  constexpr int RM = kM2Rows;
+  const int r0 = blockIdx.y * RM;
+  const int nr = min(RM, live_rows(p.rc.n_dev, p.rc.rows) - r0);
+  if (nr <= 0) return;
+  const int ncv = m2_conv_ctas(p.mi, p.bc);
+  if (int(blockIdx.x) < ncv) {
+    __shared__ long long sslot[RM];
+    if (threadIdx.x < nr) sslot[threadIdx.x] = row_slot(p.rc, r0 + threadIdx.x);
+    __syncthreads();
+    const int i = blockIdx.x * kRowThreads + threadIdx.x;
+    if (i < p.mi + 2 * p.bc) m2_conv_channel(p, i, r0, nr, sslot);
+  } else {
+    const int h = (blockIdx.x - ncv) * (kRowThreads / 32) + (threadIdx.x >> 5);
+    if (h < p.nh) m2_dt_head<16>(p, h, r0, nr, threadIdx.x & 31);
   }
 }
 
@@ -420,7 +461,12 @@ class Mamba2Layer : public Layer {
     linear(c, a1, a1t, H_, w1_, lp_, nullptr, n1_, H_, b.proj, n1_);  // x, z, b, c (mamba2.py:77-80)
     Mamba2PreP pp{rc, b.proj, n1_, mi_, bc_, nh_, in, H_, dtw_, dtb_, xc_, sxc_, bcs_, sbc_, ccs_, scc_,
                   wx_, bx_, wb_, bb_, wc_, bcv_, a_, b.xs, b.bs, b.cs, b.dt, b.dc};
-    launch_k(c.ln, k_mamba2_pre_rows, dim3(ceil_div(c.rows, kM2Rows)), dim3(kRowThreads), 0, c.s, pp);
+    if (c.rows <= kM2SplitRows) {
+      const dim3 g(m2_conv_ctas(mi_, bc_) + ceil_div(nh_, kRowThreads / 32), ceil_div(c.rows, kM2Rows));
+      launch_k(c.ln, k_mamba2_pre_split, g, dim3(kRowThreads), 0, c.s, pp);
+    } else {
+      launch_k(c.ln, k_mamba2_pre_rows, dim3(ceil_div(c.rows, kM2Rows)), dim3(kRowThreads), 0, c.s, pp);
+    }
     SsmColsParams sp;
     sp.at = {ssm_, sssm_, c.slots, nullptr, c.rows, c.n_dev};
     sp.nh = nh_; sp.sh = hs_; sp.sc = bc_;
