@@ -151,6 +151,19 @@ inline int ceil_div(long a, long b) { return int((a + b - 1) / b); }
 // launched without the attribute it is a no-op.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Prefetches of weights, issued before pdl_wait(): no predecessor writes them,
+// so their lines arrive while the predecessor finishes instead of after the
+// kernel's first phase. The CTA's threads take one 128-byte line each, all
+// inside [v, v + n).
+__device__ __forceinline__ void prefetch_l1(const float* v, int n) {
+  if (v == nullptr) return;
+  for (int i = threadIdx.x * 32; i < n; i += blockDim.x * 32) asm volatile("prefetch.global.L1 [%0];" ::"l"(v + i));
+}
+__device__ __forceinline__ void prefetch_l2(const float* v, long long n) {
+  if (v == nullptr) return;
+  for (long long i = threadIdx.x * 32; i < n; i += blockDim.x * 32LL) asm volatile("prefetch.global.L2 [%0];" ::"l"(v + i));
+}
+
 // How a kernel is launched: plain (the C-ABI operators on a caller's stream), or
 // with PDL and a scheduling priority (the engine's chains: the HBM-streaming
 // state kernels run at low priority so that the short latency-bound kernels of

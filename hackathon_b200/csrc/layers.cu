@@ -106,6 +106,7 @@ struct RmsP {
 constexpr int kRowsPerCta = 8;
 
 __global__ void __launch_bounds__(256) k_rmsnorm(const RmsP p) {
+  prefetch_l1(p.w, p.H);
   pdl_wait();
   const int r = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -305,6 +306,14 @@ __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre_rows(const Mamba2Pre
 constexpr int kM2SplitRows = 64;  // steps up to this many rows take k_mamba2_pre_split
 __host__ __device__ inline int m2_conv_ctas(int mi, int bc) { return (mi + 2 * bc + kRowThreads - 1) / kRowThreads; }
 __global__ void __launch_bounds__(kRowThreads) k_mamba2_pre_split(const Mamba2PreP p) {
+  {
+    const int ncv = m2_conv_ctas(p.mi, p.bc);
+    if (int(blockIdx.x) >= ncv) {  // this CTA's dt_proj rows
+      const int h0 = (blockIdx.x - ncv) * (kRowThreads / 32);
+      const int nh = min(kRowThreads / 32, p.nh - h0);
+      if (nh > 0) prefetch_l2(p.dtw + size_t(h0) * p.H, (long long)nh * p.H);
+    }
+  }
   pdl_wait();
   constexpr int RM = kM2Rows;
   const int r0 = blockIdx.y * RM;
@@ -779,6 +788,9 @@ struct SlstmPreP {
   float* axc; float* axn;  // [row][2H]: per block j, [input_j | h_j]
 };
 __global__ void __launch_bounds__(kRowThreads) k_slstm_pre(const SlstmPreP p) {
+  prefetch_l1(p.lnw, p.H);
+  prefetch_l1(p.cw, 4 * p.H);
+  prefetch_l1(p.cb, p.H);
   pdl_wait();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
@@ -837,6 +849,9 @@ struct SlstmPostP {
   float* x1; void* xn2; int at;
 };
 __global__ void __launch_bounds__(kRowThreads) k_slstm_post(const SlstmPostP p) {
+  prefetch_l1(p.gnw, p.H);
+  prefetch_l1(p.gnb, p.H);
+  prefetch_l1(p.mlnw, p.H);
   pdl_wait();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
@@ -1398,6 +1413,8 @@ __global__ void __launch_bounds__(kRowThreads) k_mlstm_qkv_cols(const MlstmMidP 
 }
 
 __global__ void __launch_bounds__(kRowThreads) k_mlstm_cell_heads(const MlstmMidP p, const float* kraw) {
+  prefetch_l2(p.gw + size_t(blockIdx.x) * 3 * p.mi, 3LL * p.mi);
+  prefetch_l2(p.gw + size_t(p.nh + blockIdx.x) * 3 * p.mi, 3LL * p.mi);
   pdl_wait();
   const int h = blockIdx.x, r = blockIdx.y;
   if (!row_live(p.rc, r)) return;
@@ -1411,13 +1428,27 @@ __global__ void __launch_bounds__(kRowThreads) k_mlstm_cell_heads(const MlstmMid
   const float4* wf = reinterpret_cast<const float4*>(p.gw + size_t(nh + h) * 3 * mi);
   const int m4 = mi >> 2;
   float ai = 0.f, af = 0.f;
-  for (int k = tid; k < 3 * m4; k += kRowThreads) {
-    const float4 x = k < m4 ? reinterpret_cast<const float4*>(q)[k]
-                            : (k < 2 * m4 ? reinterpret_cast<const float4*>(kr)[k - m4]
-                                          : reinterpret_cast<const float4*>(q + 2 * mi)[k - 2 * m4]);
-    const float4 a = __ldg(wi + k), b = __ldg(wf + k);
-    ai = fmaf(x.w, a.w, fmaf(x.z, a.z, fmaf(x.y, a.y, fmaf(x.x, a.x, ai))));
-    af = fmaf(x.w, b.w, fmaf(x.z, b.z, fmaf(x.y, b.y, fmaf(x.x, b.x, af))));
+  constexpr int KU = 4;  // k steps whose loads are in flight together
+  for (int k0 = tid; k0 < 3 * m4; k0 += KU * kRowThreads) {
+    float4 xv[KU], av[KU], bv[KU];
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int k = k0 + u * kRowThreads;
+      if (k < 3 * m4) {
+        xv[u] = k < m4 ? reinterpret_cast<const float4*>(q)[k]
+                       : (k < 2 * m4 ? reinterpret_cast<const float4*>(kr)[k - m4]
+                                     : reinterpret_cast<const float4*>(q + 2 * mi)[k - 2 * m4]);
+        av[u] = __ldg(wi + k);
+        bv[u] = __ldg(wf + k);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      if (k0 + u * kRowThreads >= 3 * m4) break;
+      const float4 x = xv[u], a = av[u], b = bv[u];
+      ai = fmaf(x.w, a.w, fmaf(x.z, a.z, fmaf(x.y, a.y, fmaf(x.x, a.x, ai))));
+      af = fmaf(x.w, b.w, fmaf(x.z, b.z, fmaf(x.y, b.y, fmaf(x.x, b.x, af))));
+    }
   }
   ai = warp_sum(ai);
   af = warp_sum(af);
@@ -1439,13 +1470,27 @@ __global__ void __launch_bounds__(kRowThreads) k_mlstm_cell_heads(const MlstmMid
   const float sq = sqrtf(float(hs));
   float* nst = p.n + slot * p.n_s;
   float qn = 0.f;
-  for (int j = tid; j < hs; j += kRowThreads) {
-    const int e = h * hs + j;
-    const float ks = kr[e] / sq;  // k / sqrt(head_size) (xlstm.py:99)
-    const float nv = f_g * nst[e] + i_g * ks;
-    p.qkv[size_t(r) * 3 * mi + mi + e] = ks;
-    nst[e] = nv;
-    qn = fmaf(q[e], nv, qn);
+  for (int j0 = tid; j0 < hs; j0 += kEU * kRowThreads) {
+    float kv[kEU], nv0[kEU], qv[kEU];
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int j = j0 + u * kRowThreads;
+      if (j < hs) {
+        const int e = h * hs + j;
+        kv[u] = kr[e]; nv0[u] = nst[e]; qv[u] = q[e];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kEU; ++u) {
+      const int j = j0 + u * kRowThreads;
+      if (j >= hs) break;
+      const int e = h * hs + j;
+      const float ks = kv[u] / sq;  // k / sqrt(head_size) (xlstm.py:99)
+      const float nv = f_g * nv0[u] + i_g * ks;
+      p.qkv[size_t(r) * 3 * mi + mi + e] = ks;
+      nst[e] = nv;
+      qn = fmaf(qv[u], nv, qn);
+    }
   }
   qn = warp_sum(qn);
   __syncthreads();  // every thread has read red[] and m
@@ -1498,6 +1543,9 @@ __global__ void __launch_bounds__(kRowThreads) k_mlstm_post(const MlstmPostP p) 
 constexpr int kPostWarps = 8;  // warps per CTA
 template <int TM>  // columns per lane at most (hs <= 32 * TM)
 __global__ void __launch_bounds__(256) k_mlstm_post_w(const MlstmPostP p) {
+  prefetch_l1(p.gnw, p.mi);
+  prefetch_l1(p.gnb, p.mi);
+  prefetch_l1(p.skip, p.mi);
   pdl_wait();
   const int w = blockIdx.x * kPostWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int r = w / p.nh, g = w - r * p.nh;
@@ -1549,6 +1597,7 @@ struct XFinalP {
   const float* x2; int H; const float* w; const float* res; float* out;
 };
 __global__ void __launch_bounds__(kRowThreads) k_xlstm_final(const XFinalP p) {
+  prefetch_l1(p.w, p.H);
   pdl_wait();
   const int r = blockIdx.x;
   if (!row_live(p.rc, r)) return;
