@@ -1127,9 +1127,12 @@ __global__ void __launch_bounds__(512) k_slstm_fused(const SlstmFusedP p) {
   group_stats(xc, RB * p.nbl, gs, 1e-5f, gm, gr);  // GroupNorm(num_heads) per row (xlstm.py:300,316)
   {
     const float gw = p.gnw[u], gb = p.gnb[u];
+    float tv[RB];  // every row's skip input loaded before the first store below
+#pragma unroll
+    for (int r = 0; r < RB; ++r) tv[r] = r < nr ? p.t[size_t(r0 + r) * H + u] : 0.f;
 #pragma unroll
     for (int r = 0; r < RB; ++r) {
-      const float t = r < nr ? p.t[size_t(r0 + r) * H + u] : 0.f;
+      const float t = tv[r];
       const float v = (xc[r * H + u] - gm[r * p.nbl + gu]) * gr[r * p.nbl + gu] * gw + gb + t;  // + skip (xlstm.py:318)
       xn[r * H + u] = v;
       if (r < nr) p.x1[size_t(r0 + r) * H + u] = v;
