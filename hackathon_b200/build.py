@@ -11,6 +11,10 @@ A second library, hackathon_b200/lib/libb2e_trace.so, is the same objects with
 latency.cu compiled under B2E_LAT_TRACE: the one-kernel latency path stamps
 each stage with %globaltimer (python -m hackathon_b200.profiling latency-trace).
 The product loads libb2e.so; only that profiling command loads the trace build.
+
+csrc/rows.c, a CPython extension of the drop-in client (Python lists of features
+to float32 rows), compiles with the host C compiler to
+hackathon_b200/lib/_b2e_rows<EXT_SUFFIX>.
 """
 
 from __future__ import annotations
@@ -86,7 +90,25 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         trace_obj = trace_obj.result()
     _link(cc, LIB, objs, force)
     _link(cc, TRACE_LIB, [o for o in objs if o.stem != "latency"] + [trace_obj], force)
+    build_rows(force)
     return LIB
+
+
+def build_rows(force: bool = False) -> Path:
+    """csrc/rows.c against the running interpreter's headers."""
+    import sysconfig
+
+    src = CSRC / "rows.c"
+    out = LIB.parent / ("_b2e_rows" + sysconfig.get_config_var("EXT_SUFFIX"))
+    if force or not out.exists() or src.stat().st_mtime > out.stat().st_mtime:
+        cc = os.environ.get("CC") or shutil.which("gcc") or shutil.which("cc")
+        if cc is None:
+            raise RuntimeError("no C compiler for csrc/rows.c (set CC)")
+        cmd = [cc, "-O3", "-shared", "-fPIC", "-I", sysconfig.get_paths()["include"], str(src), "-o", str(out)]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"cc failed on rows.c:\n{r.stdout}\n{r.stderr}")
+    return out
 
 
 def _link(cc: str, lib: Path, objs, force: bool) -> None:

@@ -170,3 +170,41 @@ def test_device_error_from_an_engine_raises_from_process_batch_and_drains_the_re
     fail["on"] = False
     r = client.process_batch(batch)
     assert len(r.unique_ids) == 18
+
+
+def test_feature_rows_native_helper_matches_numpy_bit_for_bit():
+    """The native row writer (csrc/rows.c) gives numpy's float32 values for float64
+    values that round, ints, bools, numpy scalars, tuples, inf and nan."""
+    assert CL._ROWS is not None, "lib/_b2e_rows is not built (python -m hackathon_b200.build)"
+    rng = np.random.default_rng(7)
+    feats = [rng.standard_normal(79).tolist() for _ in range(300)]  # float64 values: rounding matters
+    feats[3][5] = 7
+    feats[4][0] = True
+    feats[5][1] = np.float64(1e-40)
+    feats[6][2] = np.float32(3.25)
+    feats[7][3] = float("inf")
+    feats[8] = tuple(feats[8])
+    feats[9][4] = 3.4028235677973366e38  # rounds past float32's largest finite value
+    got = CL._feature_rows(feats, 79)
+    with np.errstate(over="ignore"):  # numpy warns on the value that rounds to inf
+        want = np.asarray(feats, dtype=np.float32)
+    assert got.dtype == np.float32 and got.shape == (300, 79)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    nan_row = [[float("nan")] * 3]
+    assert np.isnan(CL._feature_rows(nan_row, 3)).all()
+
+
+def test_feature_rows_refusals_follow_numpy():
+    """A row of another length or a value that is not a number takes numpy's
+    path, which raises as the reference's conversion does."""
+    import pytest
+
+    with pytest.raises(ValueError):
+        CL._feature_rows([[1.0, 2.0], [1.0]], 2)
+    with pytest.raises(ValueError):
+        CL._feature_rows([[1.0, "x"]], 2)
+    out = np.empty((1, 2), np.float32)
+    with pytest.raises(ValueError):
+        CL._ROWS.rows_f32([[1.0, 2.0, 3.0]], 2, out)
+    with pytest.raises(TypeError):
+        CL._ROWS.rows_f32([[1.0, None]], 2, out)
