@@ -208,3 +208,13 @@ def test_feature_rows_refusals_follow_numpy():
         CL._ROWS.rows_f32([[1.0, 2.0, 3.0]], 2, out)
     with pytest.raises(TypeError):
         CL._ROWS.rows_f32([[1.0, None]], 2, out)
+
+
+def test_feature_rows_without_the_native_helper(monkeypatch):
+    """Without lib/_b2e_rows the client converts with numpy: the same values."""
+    rng = np.random.default_rng(8)
+    feats = [rng.standard_normal(79).tolist() for _ in range(64)]
+    with_helper = CL._feature_rows(feats, 79)
+    monkeypatch.setattr(CL, "_ROWS", None)
+    without = CL._feature_rows(feats, 79)
+    assert np.array_equal(with_helper.view(np.uint32), without.view(np.uint32))
